@@ -1,0 +1,260 @@
+"""Generate the golden fixtures by running the REFERENCE's own code.
+
+Run in a container where the reference sources are available:
+
+    python tests/golden/make_golden.py --reference <path to iris-3b-metal checkout>
+
+It imports ``iris3b`` / ``iris_metal`` from ``<reference>/src`` (with a stub for
+``omegaconf``, which only the config loader needs), builds ``IrisDiT`` for the
+small configs, applies the seeded init recipe to the reference model itself,
+and stores inputs and outputs as ``tests/golden/*.pt``. Nothing under
+``tests/`` reads the reference at run time; the tests read these files.
+"""
+
+from __future__ import annotations
+
+import argparse
+import dataclasses
+import math
+import sys
+import types
+from pathlib import Path
+from types import SimpleNamespace
+
+import torch
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parents[1]
+sys.path.insert(0, str(REPO))
+
+from oracle import config as ocfg  # noqa: E402
+from oracle.params import STD, param_spec  # noqa: E402
+
+
+def _import_reference(root: Path):
+    stub = types.ModuleType("omegaconf")
+    stub.OmegaConf = type("OmegaConf", (), {})
+    sys.modules.setdefault("omegaconf", stub)
+    sys.path.insert(0, str(root / "src"))
+    from iris3b.config import ModelConfig, PixelStageConfig
+    from iris3b.models.dit import IrisDiT
+
+    return ModelConfig, PixelStageConfig, IrisDiT
+
+
+def _reference_config(cfg: ocfg.OracleConfig, ModelConfig, PixelStageConfig):
+    fields = {f.name for f in dataclasses.fields(ModelConfig)}
+    values = {k: v for k, v in dataclasses.asdict(cfg).items() if k in fields and k != "pixel"}
+    pixel = PixelStageConfig(**dataclasses.asdict(cfg.pixel))
+    return ModelConfig(**values, pixel=pixel)
+
+
+def _seed_reference(model, seed: int) -> None:
+    """The recipe of ``oracle.params.seeded_init`` applied to the reference model."""
+    from iris3b.nn.norms import RMSNorm
+
+    gains = {id(m.weight) for m in model.modules() if isinstance(m, RMSNorm)}
+    gen = torch.Generator().manual_seed(seed)
+    with torch.no_grad():
+        for _, p in model.named_parameters():
+            value = torch.randn(p.shape, generator=gen) * STD
+            if id(p) in gains:
+                value += 1.0
+            p.copy_(value)
+
+
+def _model_fixture(name, cfg, ModelConfig, PixelStageConfig, IrisDiT, batch, height, width, times):
+    rcfg = _reference_config(cfg, ModelConfig, PixelStageConfig)
+    model = IrisDiT(rcfg).eval()
+    ref_spec = [(n, tuple(p.shape)) for n, p in model.named_parameters()]
+    ours = [(n, tuple(s)) for n, s, _ in param_spec(cfg)]
+    assert ref_spec == ours, f"{name}: parameter inventory differs from the reference"
+    _seed_reference(model, seed=0)
+    gen = torch.Generator().manual_seed(1)
+    x = torch.randn(batch, 3, height, width, generator=gen)
+    y = torch.randn(batch, cfg.text_len, cfg.text_dim, generator=gen)
+    t = torch.tensor(times, dtype=torch.float32)
+    with torch.no_grad():
+        prepared = model.embed_text(y)
+        out = model(x, t, y, capture=(1, cfg.depth)).x
+        features = model(x, t, y, capture=(1, cfg.depth)).features
+    checksums = {n: (float(p.detach().double().sum()), float(p.detach().double().pow(2).sum()))
+                 for n, p in model.named_parameters()}
+    return {
+        "config": dataclasses.asdict(cfg),
+        "x": x,
+        "t": t,
+        "y": y,
+        "prepared_text": prepared,
+        "v": out,
+        "features": {k: v.clone() for k, v in features.items()},
+        "param_checksums": checksums,
+    }, model
+
+
+def _sample_fixture(model, fixture, cfg_scale=3.0, cfg_interval=(0.0, 1.5)):
+    """4-step Turbo Euler with CFG, using the reference's own ``generate_few_step``
+    and ``FlowDPMSolver._model_out`` (CFG on ``[uncond; cond]``). The interval
+    ``(0, 1.5)`` keeps CFG on at sigma = 1 too (the reference's default ``(0, 1)``
+    gates it off there), which is the all-steps-guided workload of the benchmark."""
+    from iris3b.flow.solver import FlowDPMSolver
+    from iris3b.sampling import generate_few_step
+    from iris_metal.turbo import TURBO_SIGMAS
+
+    prepared = fixture["prepared_text"]
+    cond, uncond = prepared[1:], prepared[:1]
+    noise = torch.randn(1, 3, fixture["x"].shape[2], fixture["x"].shape[3], generator=torch.Generator().manual_seed(5))
+
+    def velocity(x, t_model, text):
+        # the reference forward on adapted text (prepared_text), fp32
+        return model(x, t_model, text, prepared_text=text, precompute_modulation=True).x
+
+    solver = FlowDPMSolver(velocity, cfg_scale=cfg_scale, cfg_interval=cfg_interval)
+
+    class CfgModel:
+        cfg = model.cfg
+
+        def parameters(self):
+            return model.parameters()
+
+        def __call__(self, x, t, y, y_mask):
+            return SimpleNamespace(x=solver._model_out(x, float(t[0]) / 1000.0, cond, uncond))
+
+    class Encoder:
+        def encode(self, prompts):
+            return SimpleNamespace(embeddings=torch.zeros(1), mask=torch.ones(1))
+
+    seen = []
+    with torch.no_grad():
+        generate_few_step(
+            CfgModel(), Encoder(), ["p"], noise.shape[2], noise.shape[3], list(TURBO_SIGMAS),
+            noise=noise, device="cpu", check=seen.append,
+        )  # fmt: skip
+    return {"noise": noise, "cond": cond, "uncond": uncond, "cfg_scale": cfg_scale, "cfg_interval": cfg_interval,
+            "sample": seen[0]}
+
+
+def _op_fixtures():
+    from iris3b.nn.embeddings import TimestepEmbedder, sincos_pos_embed_2d
+    from iris3b.nn.rope import apply_rope, rope_1d, rope_2d
+    from iris_metal.kernels import (
+        gated_residual_rms_norm_,
+        pixel_mlp_,
+        pixel_rms_norm,
+        qk_norm_rope,
+        qk_norm_rope_reference,
+        rms_norm_modulate,
+    )
+
+    gen = torch.Generator().manual_seed(0)
+    out = {}
+    # qk_norm_rope at the shapes of tests/test_metal_engine.py:159-176 (CPU branch)
+    batch, tokens, heads = 2, 37, 3
+    fused = torch.randn(batch, tokens, 2 * heads * 128, generator=gen)
+    weight = torch.rand(128, generator=gen) + 0.5
+    angles = torch.rand(tokens + 5, 64, generator=gen) * 6.0
+    cos, sin = angles.cos(), angles.sin()
+    dst = torch.zeros(batch, heads, tokens + 5, 128)
+    qk_norm_rope(fused, weight, cos, sin, 1e-6, heads, col_offset=heads * 128, out=dst, offset=5)
+    out["qk_norm_rope"] = dict(x=fused, weight=weight, cos=cos, sin=sin, heads=heads, col_offset=heads * 128,
+                               offset=5, out=dst,
+                               ref=qk_norm_rope_reference(fused[..., heads * 128:], weight, cos[5:], sin[5:], 1e-6))
+    # row kernels at tests/test_metal_engine.py:191-207
+    x = torch.randn(2, 7, 384, generator=gen)
+    branch = torch.randn(2, 7, 384, generator=gen)
+    w = torch.rand(384, generator=gen) + 0.5
+    shift, scale, gate = (torch.randn(2, 1, 384, generator=gen) for _ in range(3))
+    out["rms_norm_modulate"] = dict(x=x, weight=w, shift=shift, scale=scale,
+                                    out_f32=rms_norm_modulate(x, w, shift, scale, 1e-6, torch.float32),
+                                    out_bf16=rms_norm_modulate(x, w, shift, scale, 1e-6, torch.bfloat16))
+    out["gated_residual"] = dict(residual=x, branch=branch, weight=w, gate=gate,
+                                 out=gated_residual_rms_norm_(x.clone(), branch, w, gate, 1e-6))
+    # pixel kernels at tests/test_metal_engine.py:258-289
+    bf16 = torch.bfloat16
+    pixels = torch.randn(5, 256, 16, generator=gen).to(bf16)
+    pbranch = torch.randn(5, 256, 16, generator=gen).to(bf16)
+    mods = (torch.randn(5, 256, 64, generator=gen) * 0.3).to(bf16)
+    nw, nxt = (torch.rand(16, generator=gen) + 0.5 for _ in range(2))
+    torch.manual_seed(0)
+    fc1, fc2 = torch.nn.Linear(16, 64).to(bf16), torch.nn.Linear(64, 16).to(bf16)
+    new_pixels = pixels.clone()
+    nxt_in = pixel_mlp_(new_pixels, pbranch, mods, nw, fc1, fc2, nxt, 1e-6)
+    out["pixel_mlp"] = dict(pixels=pixels, branch=pbranch, mods=mods, norm_weight=nw, next_norm_weight=nxt,
+                            fc1_w=fc1.weight.detach(), fc1_b=fc1.bias.detach(), fc2_w=fc2.weight.detach(),
+                            fc2_b=fc2.bias.detach(), new_pixels=new_pixels, next_input=nxt_in,
+                            rms=pixel_rms_norm(pixels, nw, 1e-6))
+    # tables
+    out["rope"] = dict(img_64_every16=torch.view_as_real(rope_2d(128, 64, 64, 1e4, 16.0, "isotropic"))[::16].clone(),
+                       img_6x4=torch.view_as_real(rope_2d(128, 6, 4, 1e4, 16.0, "isotropic")),
+                       img_sq=torch.view_as_real(rope_2d(64, 8, 8, 1e4, 16.0, "square")),
+                       txt_256=torch.view_as_real(rope_1d(128, 256, 1e4)))
+    q = torch.randn(2, 9, 3, 128, generator=gen)
+    k = torch.randn(2, 9, 3, 128, generator=gen)
+    cis = rope_2d(128, 3, 3, 1e4, 16.0, "isotropic")
+    qr, kr = apply_rope(q, k, cis)
+    out["apply_rope"] = dict(q=q, k=k, q_out=qr, k_out=kr)
+    out["sincos"] = dict(t_16x24=sincos_pos_embed_2d(16, 16, 24), t_64=sincos_pos_embed_2d(16, 64, 64))
+    emb = TimestepEmbedder(64, max_period=10.0)
+    tt = torch.tensor([0.0, 125.0, 625.0, 938.0, 1000.0])
+    out["timestep"] = dict(t=tt, feats=emb.timestep_embedding(tt))
+    return out
+
+
+def _sampler_fixtures():
+    """Known answers of the samplers with toy models (``tests/test_metal_turbo.py:24-73``,
+    ``tests/test_flow.py``)."""
+    from iris3b.flow.solver import FlowDPMSolver
+
+    out = {}
+    gen = torch.Generator().manual_seed(17)
+    z = torch.randn(2, 3, 8, 8, generator=gen)
+    cond = torch.randn(2, 3, 8, 8, generator=gen)
+    uncond = torch.randn(2, 3, 8, 8, generator=gen)
+
+    def model_fn(x, t, text):
+        return 0.3 * x + 0.05 * text + 1e-4 * t[:, None, None, None]
+
+    for steps, order, shift, scale in ((4, 1, 1.0, 3.0), (10, 2, 4.0, 3.0), (7, 2, 3.0, 1.0)):
+        solver = FlowDPMSolver(model_fn, cfg_scale=scale, cfg_interval=(0.0, 1.0))
+        out[f"dpm_{steps}_{order}_{shift}_{scale}"] = dict(
+            steps=steps, order=order, shift=shift, cfg_scale=scale,
+            grid=FlowDPMSolver.time_grid(steps, shift),
+            sample=solver.sample(z, cond, uncond, steps=steps, order=order, shift=shift))
+    out["inputs"] = dict(z=z, cond=cond, uncond=uncond)
+    return out
+
+
+def main():
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--reference", required=True, type=Path)
+    args = parser.parse_args()
+    torch.set_num_threads(8)
+    ModelConfig, PixelStageConfig, IrisDiT = _import_reference(args.reference)
+    fixtures = {
+        "released_mha": (ocfg.released_topology(num_kv_heads=None), 2, 24, 24, [125.0, 850.0]),
+        "released_gqa": (ocfg.released_topology(), 2, 24, 16, [125.0, 850.0]),
+        "tiny_cpu": (ocfg.tiny_cpu_config(), 1, 128, 128, [431.0]),
+    }
+    for name, (cfg, batch, h, w, times) in fixtures.items():
+        fixture, model = _model_fixture(name, cfg, ModelConfig, PixelStageConfig, IrisDiT, batch, h, w, times)
+        if name == "released_mha":
+            fixture["euler_cfg"] = _sample_fixture(model, fixture)
+        torch.save(fixture, HERE / f"{name}.pt")
+        print(name, "saved", tuple(fixture["v"].shape), float(fixture["v"].abs().max()))
+    torch.save(_op_fixtures(), HERE / "ops.pt")
+    torch.save(_sampler_fixtures(), HERE / "samplers.pt")
+    # the full-size inventories, built on the meta device (no memory)
+    inventories = {}
+    for name, cfg in (("baseline_step", ocfg.baseline_step_config()), ("released_preset", ocfg.OracleConfig(
+            text_adapter="linear"))):
+        with torch.device("meta"):
+            model = IrisDiT(_reference_config(cfg, ModelConfig, PixelStageConfig))
+        spec = [(n, tuple(p.shape)) for n, p in model.named_parameters()]
+        assert spec == [(n, tuple(s)) for n, s, _ in param_spec(cfg)], name
+        inventories[name] = {"names": [n for n, _ in spec], "numel": sum(math.prod(s) for _, s in spec)}
+        print(name, "parameters:", inventories[name]["numel"])
+    torch.save(inventories, HERE / "inventories.pt")
+
+
+if __name__ == "__main__":
+    main()
