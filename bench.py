@@ -1,0 +1,387 @@
+#!/usr/bin/env python
+"""Benchmark: Iris-3B-shaped denoising at 1024^2 on B200s.
+
+One bench step = the 4-step guided flow-Euler loop (sigmas 1.0, 0.938, 0.833,
+0.625; CFG 3 on [uncond; cond], so every denoiser call has 2 rows per image)
+over this rank's share of 8 images; images are split data-parallel across the
+N GPUs with no collective in the timed region. ``value`` = 8 images / the
+slowest rank's step time. The model is the BASELINE config-3 architecture
+(d = 3072, 24 blocks, 24 heads x 128, SwiGLU 8192, 4096 + 256 tokens) with
+random weights (std 0.02); inputs are seeded N(0, 1) noise and text states.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+For N > 1 run one process per GPU under torchrun. Rank 0 prints one JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+for _p in (str(REPO), str(REPO / "iris-3b-metal_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+METRIC = "ms per denoise step and images/sec at 1024² (B=2 CFG) at 1/2/4/8 B200; % roofline"
+UNIT = "images/s"
+IMAGES = 8
+RESOLUTION = 1024
+SIGMAS = (1.0, 0.938, 0.833, 0.625)
+CFG_SCALE = 3.0
+TEXT_LEN, TEXT_DIM = 256, 2560
+WORKLOAD = (
+    "BASELINE config 4: 8 images of 1024^2 noise, 4 flow-Euler steps with CFG 3 on [uncond; cond] "
+    "(2 denoiser rows per image per step), DP split by image across N GPUs"
+)
+
+
+def peaks() -> dict:
+    path = REPO / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return {"hbm_gbs": data["hbm_gbs"], "bf16": data["bf16_tflops"], "bf16_sustained": data["bf16_tflops_sustained"],
+                "source": "measured"}  # fmt: skip
+    return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
+
+
+def step_flops(batch_rows: int, L: int = 4096, T: int = 256) -> float:
+    """Algorithmic FLOPs of one denoiser call (GEMMs + attention) for the
+    benchmark model, as scripts/flops.py of the reference counts them."""
+    d, ffn, heads, hd = 3072, 8192, 24, 128
+    N = T + L
+    per_block = 2 * N * d * (3 * d) + 2 * N * d * d * 2 + 2 * N * d * ffn * 3 + 4 * N * N * heads * hd
+    pp, da = 256, 1280
+    pit = 2 * L * d * (4 * 16 * pp) + 2 * L * (pp * 16) * da * 2 + 2 * L * da * 3 * da + 2 * L * da * da
+    pit += 4 * L * L * da + 2 * L * pp * (16 * 64 * 2)
+    embed = 2 * L * 768 * d
+    return batch_rows * (24 * per_block + 4 * pit + embed)
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = (
+        "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+        "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+        "clocks_event_reasons.sw_power_cap"
+    )
+
+    def __init__(self, device: int):
+        self.proc = None
+        try:
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            ident = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+        except Exception:
+            ident = str(device)
+        self.cmd = ["nvidia-smi", "-i", ident, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(self.cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self) -> dict:
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        sm, sm_max, reasons = [], None, set()
+        for ln in getattr(self, "lines", []):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                sm_max = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        busy = [s for s in sm if sm_max and s > 0.3 * sm_max] or sm
+        return {
+            "sm_mhz": statistics.median(busy) if busy else None,
+            "sm_max_mhz": sm_max,
+            "reasons": sorted(reasons),
+            "samples": len(sm),
+        }
+
+
+def make_inputs(seed_noise: int = 0, seed_text: int = 4):
+    gen = torch.Generator().manual_seed(seed_noise)
+    noise = torch.randn(IMAGES, 3, RESOLUTION, RESOLUTION, generator=gen)
+    tgen = torch.Generator().manual_seed(seed_text)
+    cond = torch.randn(IMAGES, TEXT_LEN, TEXT_DIM, generator=tgen)
+    uncond = torch.randn(1, TEXT_LEN, TEXT_DIM, generator=tgen)
+    return noise, cond, uncond
+
+
+def cpu_baseline_sample(threads: int) -> dict:
+    """The oracle (fp32 PyTorch restatement of the reference's path) on the host
+    cores: one block of each kind at B = 2, 1024^2, extrapolated to a forward."""
+    from oracle.config import baseline_step_config
+    from oracle.timing import BlockSampler
+
+    torch.set_num_threads(threads)
+    sampler = BlockSampler(baseline_step_config(), batch=2, height=RESOLUTION, width=RESOLUTION)
+    seconds = sampler.forward_seconds(repeats=1)
+    per_image = len(SIGMAS) * seconds["forward"]  # 4 guided calls of B = 2 per image
+    return {"seconds": seconds, "images_per_s": 1.0 / per_image}
+
+
+def reference_arm(args, rank: int) -> None:
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    from oracle.config import baseline_step_config
+    from oracle.timing import BlockSampler
+
+    torch.set_num_threads(threads)
+    sampler = BlockSampler(baseline_step_config(), batch=2, height=RESOLUTION, width=RESOLUTION)
+    cfg = sampler.cfg
+    # each step: one block of each kind -> a forward estimate by block counts -> images/s
+    per_kind = {"dual": [], "single": [], "pixel": []}
+    times = []
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            sampler.single()
+        for _ in range(args.steps):
+            step_start = time.perf_counter()
+            for kind in per_kind:
+                t0 = time.perf_counter()
+                getattr(sampler, kind)()
+                per_kind[kind].append(time.perf_counter() - t0)
+            times.append(time.perf_counter() - step_start)
+    med = {kind: statistics.median(v) for kind, v in per_kind.items()}
+    forward = cfg.dual_depth * med["dual"] + (cfg.depth - cfg.dual_depth) * med["single"] + cfg.pixel.depth * med["pixel"]
+    value = 1.0 / (len(SIGMAS) * forward)
+    step_s = statistics.median(times)
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": step_s * 1e3,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": WORKLOAD, "model": "iris-3b-shaped d3072 (BASELINE config 3), random weights",
+                   "global_batch": IMAGES, "seq_len": 4352, "parallelism": "host cores"},  # fmt: skip
+        "cpu_baseline": {
+            "value": value,
+            "unit": UNIT,
+            "cores": threads,
+            "kind": "port",
+            "sample": "oracle fp32 PyTorch path, one dual + one single + one pixel block at B=2 1024^2 per step, "
+            f"extrapolated by block counts to a forward ({forward:.1f} s) and 4 guided calls per image",
+        },
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=5)
+    parser.add_argument("--warmup", type=int, default=3)
+    parser.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    args = parser.parse_args()
+    from iris_b200.parallel import env_world, gather_images, image_shard, init_process_group  # noqa: F401
+
+    rank, world, local = env_world()
+    if args.impl == "reference":
+        reference_arm(args, rank)
+        return
+    args.warmup = max(args.warmup, 3)
+    import torch.distributed as dist
+
+    from iris_b200 import CudaIris, IrisWeights, _lib, baseline_step_config, synthetic_state
+    from iris_b200 import kernels as K
+    from iris_b200.pipeline import DenoisePipeline
+    from iris_b200.sampling import euler_cfg
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        init_process_group("nccl", timeout_s=600)
+    cfg = baseline_step_config()
+    engine = CudaIris(IrisWeights(cfg, synthetic_state(cfg, device, seed=0)))
+    noise, cond_states, uncond_states = make_inputs()
+    lo, hi = image_shard(IMAGES, rank, world)
+    n_local = hi - lo
+    noise_d = noise[lo:hi].to(device)
+    cond = engine.encode_text(cond_states[lo:hi].to(device))
+    uncond = engine.encode_text(uncond_states.to(device))
+
+    def step():
+        return euler_cfg(engine, noise_d, cond, uncond, cfg_scale=CFG_SCALE, sigmas=SIGMAS)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def max_over_ranks(value: float) -> float:
+        if world == 1:
+            return value
+        t = torch.tensor([value], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---------------------------------------------------------------- device-resident
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    K.profile_gemms(True)
+    launches0 = _lib.launch_count()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record()
+        for _ in range(args.steps):
+            step()
+        end.record()
+        torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    launches = (_lib.launch_count() - launches0) // args.steps
+    gemm_flops, gemm_ms, gemm_n = K.profile_gemms(False)
+    ms = max_over_ranks(start.elapsed_time(end) / args.steps)
+    value = IMAGES / (ms / 1e3)
+
+    # ------------------------------------------------------- e2e through the public API
+    pipe = DenoisePipeline(engine, cfg_scale=CFG_SCALE, sigmas=SIGMAS)
+    noise_h = noise[lo:hi].pin_memory()
+    cond_h = cond_states[lo:hi].pin_memory()
+    uncond_h = uncond_states.pin_memory()
+    out_h = torch.empty_like(noise_h).pin_memory()
+    for _ in range(args.warmup):
+        pipe(noise_h, cond_h, uncond_h, out=out_h)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record()
+    for _ in range(args.steps):
+        pipe(noise_h, cond_h, uncond_h, out=out_h)
+    e_end.record()
+    torch.cuda.synchronize()
+    barrier()
+    e_ms = max_over_ranks(e_start.elapsed_time(e_end) / args.steps)
+    h2d = sum(t.numel() * t.element_size() for t in (noise_h, cond_h, uncond_h))
+    d2h = out_h.numel() * out_h.element_size()
+
+    # ---------------------------------------------------- one B = 2 denoiser call (rank 0)
+    b2_ms = None
+    if rank == 0:
+        x2 = noise_d[:1].repeat(2, 1, 1, 1)
+        text2 = torch.cat([uncond, cond[:1]])
+        t2 = torch.full((2,), 625.0, device=device)
+        for _ in range(3):
+            engine(x2, t2, text2)
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        s2.record()
+        for _ in range(5):
+            engine(x2, t2, text2)
+        e2.record()
+        torch.cuda.synchronize()
+        b2_ms = s2.elapsed_time(e2) / 5
+
+    pk = peaks()
+    achieved = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms else None
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        base = cpu_baseline_sample(threads)
+        cpu = {
+            "value": base["images_per_s"],
+            "unit": UNIT,
+            "cores": threads,
+            "kind": "port",
+            "sample": "oracle fp32 PyTorch path on the host, one dual + one single + one pixel block at B=2 1024^2 "
+            f"(s: {', '.join(f'{k} {v:.2f}' for k, v in base['seconds'].items())}), extrapolated to 4 guided "
+            "calls per image",
+        }
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    flops_per_call = step_flops(2)
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": {
+            "workload": WORKLOAD,
+            "model": "iris-3b-shaped: d3072, 8 dual + 16 single-stream blocks, 24 MHA heads x 128, SwiGLU 8192, "
+            "4 post-modulated PiT blocks; random-init weights (std 0.02)",
+            "global_batch": IMAGES,
+            "rows_per_call_per_gpu": 2 * n_local,
+            "seq_len": 4352,
+            "parallelism": f"dp{world}",
+            "ms_per_denoise_step_b2": b2_ms,
+            "b2_step_tflops": (flops_per_call / (b2_ms / 1e3) / 1e12) if b2_ms else None,
+            "l2": "no flush: every step streams 8.7 GB of weights, far above the 126 MB L2",
+        },
+        "roofline": {
+            "kernel": "gemm_bf16_kernel (tcgen05, all GEMM launches of the timed region)",
+            "bound": "tensor",
+            "achieved": achieved,
+            "peak": pk["bf16_sustained"],
+            "unit": "TFLOP/s",
+            "frac": (achieved / pk["bf16_sustained"]) if achieved else None,
+            "traffic": None,
+            "launches": gemm_n,
+            "peak_source": f"{pk['source']} bf16 sustained",
+        },
+        "e2e": {"value": IMAGES / (e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches * args.steps,
+        "clocks": clocks.summary(),
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

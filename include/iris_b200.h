@@ -1,0 +1,199 @@
+/*
+ * iris_b200.h -- C ABI of the B200 (sm_100a) denoiser kernels for Iris-3B.
+ *
+ * The reference dispatches its fused kernels from Python through
+ * torch.mps.compile_shader (src/iris_metal/kernels.py:309-311) and calls
+ * F.linear / F.scaled_dot_product_attention for the rest of the per-step
+ * forward (src/iris_metal/model.py:46-52,243-250). This library is what a
+ * binding of that path binds instead: plain pointers, sizes and a CUDA stream
+ * (cudaStream_t passed as void*). Every entry point
+ *   - validates its arguments before launching anything and returns
+ *     IRIS_EINVAL (message in iris_last_error()) on a bad call,
+ *   - returns IRIS_ECUDA if a CUDA call fails,
+ *   - enqueues work on `stream` and never synchronises the host,
+ *   - never allocates: the caller owns every input, output and workspace.
+ * There is no CPU path: the kernels need an sm_100a device.
+ *
+ * Element types (the *_dtype arguments): IRIS_F32, IRIS_BF16, IRIS_F16.
+ * Row maps (seg_rows, seg_stride, seg_offset): logical row r of an operand is
+ * physical row (r / seg_rows) * seg_stride + seg_offset + r % seg_rows, so one
+ * stream's rows can live inside a joint [text | image] token buffer. The
+ * identity map is (rows, 0, 0).
+ */
+#ifndef IRIS_B200_H
+#define IRIS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define IRIS_OK 0
+#define IRIS_EINVAL 1
+#define IRIS_ECUDA 2
+
+#define IRIS_F32 0
+#define IRIS_BF16 1
+#define IRIS_F16 2
+
+/* GEMM epilogues */
+#define IRIS_EPI_STORE 0  /* out = acc (+ bias)                        */
+#define IRIS_EPI_SWIGLU 1 /* out = silu(acc[w1 block]) * acc[w3 block] */
+#define IRIS_EPI_GATE 2   /* out = aux * sigmoid(acc)                  */
+
+/* Residual-kernel follow-ups (iris_gated_residual_rms_norm next_mode) */
+#define IRIS_NEXT_NONE 0
+#define IRIS_NEXT_NORM_MODULATE 1 /* next_out = rms_norm(res) * w * (1 + scale[b]) + shift[b] */
+#define IRIS_NEXT_SILU_ADD 2      /* next_out = silu(shift[b] + res)  (timestep re-fuse)   */
+
+/* ---- library ---------------------------------------------------------- */
+const char* iris_last_error(void);
+int iris_abi_version(void);
+/* Reads (and with clear != 0 resets) the device error word of the current
+ * device after synchronising `stream`: bit 0 = a kernel's bounded wait timed
+ * out, bit 1 = a kernel rejected its arguments on the device. */
+int iris_device_error(int clear, unsigned int* value, void* stream);
+
+/* ---- row kernels -------------------------------------------------------- */
+/* rms_norm_modulate, src/iris_metal/kernels.py:413-452 (MSL :116-146):
+ * out[r] = (rms_norm(x[r]) * weight * (1 + scale[b]) + shift[b]) in out_dtype,
+ * b = r / rows_per_batch, modulation rows at b * mod_stride. width % 128 == 0. */
+int iris_rms_norm_modulate(const void* x, int x_dtype, int64_t x_seg_rows, int64_t x_seg_stride,
+                           int64_t x_seg_offset, void* out, int out_dtype, const float* weight, const float* shift,
+                           const float* scale, int64_t mod_stride, int64_t rows, int64_t rows_per_batch,
+                           int64_t width, float eps, void* stream);
+
+/* gated_residual_rms_norm_, src/iris_metal/kernels.py:455-480 (MSL :148-175):
+ * residual[r] += gate[b] * rms_norm(branch[r]) * weight, in place (fp32);
+ * residual and branch rows each go through their row map. With next_mode !=
+ * IRIS_NEXT_NONE the updated row also produces the next branch input (see
+ * IRIS_NEXT_*), written to next_out through the third row map. */
+int iris_gated_residual_rms_norm(float* residual, int64_t res_seg_rows, int64_t res_seg_stride,
+                                 int64_t res_seg_offset, const void* branch, int branch_dtype, int64_t br_seg_rows,
+                                 int64_t br_seg_stride, int64_t br_seg_offset, const float* weight, const float* gate,
+                                 int64_t mod_stride, int64_t rows, int64_t rows_per_batch, int64_t width, float eps,
+                                 int next_mode, const float* next_weight, const float* next_shift,
+                                 const float* next_scale, int64_t next_mod_stride, void* next_out, int next_out_dtype,
+                                 int64_t nx_seg_rows, int64_t nx_seg_stride, int64_t nx_seg_offset, void* stream);
+
+/* x[r] = rms_norm(x[r]) * weight + add[r % rows_per_batch]  (in place, fp32):
+ * TextEmbedder norm + y_pos_embedding, src/iris3b/models/dit.py:263-281. */
+int iris_rms_norm_add_rows(float* x, const float* weight, const float* add, int64_t rows, int64_t rows_per_batch,
+                           int64_t width, float eps, void* stream);
+
+/* ---- attention inputs --------------------------------------------------- */
+/* qk_norm_rope, src/iris_metal/kernels.py:334-397 (MSL :37-84): rows of 128
+ * in x[b, n, col_offset + h*128 ...] (row stride row_stride elements) ->
+ * per-head RMSNorm * weight, rotary pairs (2i, 2i+1) by cos/sin[offset + n],
+ * written to out[b, h, offset + n, :] (out has n_out tokens). */
+int iris_qk_norm_rope(const void* x, int x_dtype, int64_t batch, int64_t tokens, int64_t row_stride,
+                      int64_t col_offset, int64_t heads, const float* weight, const float* cos, const float* sin,
+                      float eps, void* out, int out_dtype, int64_t n_out, int64_t offset, void* stream);
+
+/* One projection [b, n, (heads_q + 2 heads_kv) * 128] (bf16, columns q | k | v,
+ * head-major: src/iris3b/models/blocks/single_stream.py:111-117) -> q and k
+ * normed + rotated, v re-laid, all bf16 [b, h, offset + n, 128] (the reference
+ * does this with qk_norm_rope twice plus a V copy, src/iris_metal/model.py:243-250). */
+int iris_qkv_heads(const void* qkv, int64_t batch, int64_t tokens, int64_t row_stride, int64_t heads_q,
+                   int64_t heads_kv, const float* q_weight, const float* k_weight, const float* cos, const float* sin,
+                   float eps, void* q_out, void* k_out, void* v_out, int64_t n_out, int64_t offset, void* stream);
+
+/* ---- tensor-core kernels ------------------------------------------------ */
+/* F.linear in the step (src/iris_metal/model.py:46-52): C = epi(A W^T).
+ * A [M, K] (lda), W [N, K] (ldw), bf16, K-major; out [*, ldc] f32 or bf16 via
+ * the out row map. SWIGLU: W tiles of 256 rows hold 128 rows of w1 then the
+ * matching 128 rows of w3; out has N/2 columns. GATE: aux bf16 [*, ldaux]
+ * through the aux row map; out = aux * sigmoid(acc). */
+int iris_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw, void* out, int out_dtype, int64_t ldc,
+                   int64_t M, int64_t N, int64_t K, int epilogue, const float* bias, const void* aux, int64_t ldaux,
+                   int64_t out_seg_rows, int64_t out_seg_stride, int64_t out_seg_offset, int64_t aux_seg_rows,
+                   int64_t aux_seg_stride, int64_t aux_seg_offset, void* stream);
+
+/* F.scaled_dot_product_attention, non-causal, unmasked
+ * (src/iris_metal/model.py:243-250, src/iris3b/nn/attention.py:61-91):
+ * q [b, heads_q, n, 128], k/v [b, heads_kv, n, 128] bf16 contiguous;
+ * o[(b * n + i) * o_row_stride + h * 128 + d] bf16. heads_q % heads_kv == 0. */
+int iris_flash_attn_fwd(const void* q, const void* k, const void* v, void* o, int64_t batch, int64_t heads_q,
+                        int64_t heads_kv, int64_t n, int64_t head_dim, float scale, int64_t o_row_stride,
+                        void* stream);
+
+/* ---- pixel stage -------------------------------------------------------- */
+/* pixel_rms_norm, src/iris_metal/kernels.py:486-498 (MSL :217-232): bf16 out. */
+int iris_pixel_rms_norm(const void* pixels, int pixel_dtype, void* out, const float* weight, int64_t n_pixels,
+                        float eps, void* stream);
+
+/* pixel_mlp_, src/iris_metal/kernels.py:527-584 (MSL :235-293): per pixel of
+ * 16 channels, pixels += bf16(branch * (1 + scale1) + shift1), RMSNorm,
+ * fc1 16->64 + b, exact GELU, fc2 64->16 + b, pixels += bf16(mlp * (1 + scale2)
+ * + shift2), next_input = rms_norm(pixels) * next_norm_weight. mods bf16
+ * [n, 64] = (scale1, shift1, scale2, shift2); fc weights/biases bf16; pixels
+ * bf16 (rounded like the reference) or f32 (kept unrounded). */
+int iris_pixel_mlp(void* pixels, int pixel_dtype, const void* branch, const void* mods, const float* norm_weight,
+                   const void* fc1_w, const void* fc1_b, const void* fc2_w, const void* fc2_b,
+                   const float* next_norm_weight, void* next_input, int64_t n_pixels, float eps, void* stream);
+
+/* The last pixel block fused with FinalLayer (src/iris3b/models/dit.py:53-62)
+ * and the fold (dit.py:367-374): same update as iris_pixel_mlp, then
+ * v[b, c, y, x] = final_w[c] . rms_norm(pixels) * final_norm_weight + final_b[c]
+ * written straight into the [b, 3, H, W] fp32 velocity. */
+int iris_pixel_mlp_head(void* pixels, int pixel_dtype, const void* branch, const void* mods,
+                        const float* norm_weight, const void* fc1_w, const void* fc1_b, const void* fc2_w,
+                        const void* fc2_b, const float* final_norm_weight, const float* final_w,
+                        const float* final_b, float* v, int64_t batch, int64_t height, int64_t width, int64_t patch,
+                        float eps, void* stream);
+
+/* PixelEmbedder.forward, src/iris3b/nn/embeddings.py:319-328, plus the first
+ * block's pixel_rms_norm: pixels[(b, gy, gx), ky * p + kx, :] =
+ * W x[b, :, y, x] + bias + pos[y * W + x, :] (pos may be null); normed = bf16
+ * rms_norm(pixels) * norm_weight. d_pix == 16, channels == 3. */
+int iris_pixel_embed(const float* x, const float* w, const float* bias, const float* pos, void* pixels,
+                     int pixel_dtype, void* normed, const float* norm_weight, float eps, int64_t batch,
+                     int64_t height, int64_t width, int64_t patch, void* stream);
+
+/* ---- layout and conditioning -------------------------------------------- */
+/* Patchify, src/iris_metal/model.py:188 / F.unfold in dit.py:326:
+ * out[b * L + gy * gw + gx, c * p * p + ky * p + kx] = x[b, c, gy * p + ky, gx * p + kx] (bf16 out). */
+int iris_patchify(const float* x, void* out, int64_t batch, int64_t channels, int64_t height, int64_t width,
+                  int64_t patch, void* stream);
+
+/* Fold of a per-pixel head output, src/iris3b/models/dit.py:367-374:
+ * v[b, c, gy * p + ky, gx * p + kx] = out[b * L + gy * gw + gx, ky * p + kx, c] (fp32). */
+int iris_unpatchify(const float* out, float* v, int64_t batch, int64_t channels, int64_t height, int64_t width,
+                    int64_t patch, void* stream);
+
+/* TimestepEmbedder.timestep_embedding, src/iris3b/nn/embeddings.py:41-45:
+ * out[b] = [cos(t_b f_k) | sin(t_b f_k)], f_k = exp(-ln(max_period) k / (freq_dim / 2)). */
+int iris_timestep_embedding(const float* t, float* out, int64_t batch, int64_t freq_dim, float max_period,
+                            void* stream);
+
+/* Small-M linear for the conditioning MLP and shared adaLN cores
+ * (src/iris3b/nn/embeddings.py:47-52, src/iris_metal/model.py:190-192):
+ * out[m, n] = act_out(sum_k act_in(x[m, k]) w[n, k] + bias[n]); act 0 = none, 1 = silu. */
+int iris_gemv(const float* x, int64_t M, int64_t K, const void* w, int w_dtype, const float* bias, float* out,
+              int64_t N, int act_in, int act_out, void* stream);
+
+/* Per-block modulation rows, SharedCoreBias.forward (src/iris3b/nn/modulation.py:284-285):
+ * out[j, b, :] = core[b, :] + bias[j, :] for j < n_blocks. */
+int iris_add_bias_rows(const float* core, const float* bias, float* out, int64_t batch, int64_t n_blocks,
+                       int64_t width, void* stream);
+
+/* ---- sampler ------------------------------------------------------------ */
+/* One CFG + Euler flow step (src/iris3b/flow/solver.py:72-74 and
+ * src/iris3b/sampling.py:129-135): with guided != 0, v holds [uncond; cond]
+ * (2 * images rows) and v_g = v_u + cfg_scale (v_c - v_u); clean = x - sigma v_g;
+ * if sigma_next < 0 x_out = clean (pre-clamp final sample), else
+ * x_out = (1 - sigma_next) clean + sigma_next (x - (1 - sigma) clean) / sigma. */
+int iris_cfg_euler(const float* v, const float* x, float* x_out, int64_t images, int64_t per_image, float cfg_scale,
+                   float sigma, float sigma_next, int guided, void* stream);
+
+/* require_finite, src/iris_metal/model.py:102-110: *flag (device int) = 1 if
+ * every x[i] is finite, else 0. */
+int iris_all_finite(const float* x, int64_t n, int* flag, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* IRIS_B200_H */

@@ -1,0 +1,361 @@
+// Persistent, warp-specialised BF16 GEMM on the 5th-generation tensor cores.
+//
+//   C[m, n] = epilogue( sum_k A[m, k] * W[n, k] )      A: [M, K], W: [N, K], both K-major
+//
+// This is every Linear of the denoiser step (F.linear in the reference:
+// src/iris_metal/model.py:46-52, SwiGLU :51-52, gate :282-283,309, projections
+// :284-285,310, pixel stage :332-341).
+//
+// Per CTA (one per SM, persistent over output tiles of 128 x 256):
+//   warp 0      TMA producer: A and W tiles (64-wide K slabs, 128B swizzle)
+//               into a 4-stage shared-memory ring;
+//   warp 1      TMEM allocator and MMA issuer: one thread issues
+//               tcgen05.mma (M=128, N=256, K=16) into one of two TMEM
+//               accumulators (2 x 256 fp32 columns) and commits to mbarriers;
+//   warps 2..5  epilogue: tcgen05.ld of their 32 TMEM lanes (= 32 rows),
+//               fused epilogue math, direct vectorised global stores, then
+//               release the accumulator so the next tile's MMAs overlap.
+//
+// Epilogues: STORE (optional bias, fp32 or bf16 out), SWIGLU (each 256-wide
+// W tile holds 128 rows of w1 then the matching 128 rows of w3; writes
+// silu(a) * b as bf16, 128 columns per tile), GATE (out = aux * sigmoid(acc),
+// bf16; aux is the attention output). Output and aux rows go through a
+// segmented row map so a stream's rows can live inside a joint
+// [text | image] token buffer.
+#include "common.cuh"
+#include "iris_abi_internal.h"
+
+namespace iris {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;  // 16 KB
+constexpr int B_BYTES = BN * BK * 2;  // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int TMEM_COLS = 512;        // two 256-column fp32 accumulators
+constexpr int THREADS = 192;
+constexpr int GROUP_M = 16;           // tile rasterisation: 16 M-blocks per group
+constexpr size_t SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + 256 /*barriers*/;
+
+enum Epilogue : int { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_GATE = 2 };
+
+struct Params {
+  int M, N, K;
+  int epilogue;
+  int out_dtype;  // 0 f32, 1 bf16
+  void* out;
+  int64_t ldc;
+  RowMap out_map;
+  const float* bias;            // [N] or null (STORE only)
+  const __nv_bfloat16* aux;     // GATE: [*, ldaux]
+  int64_t ldaux;
+  RowMap aux_map;
+};
+
+struct Smem {
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tmem_full[2];
+  uint64_t tmem_empty[2];
+  uint64_t teardown;
+  uint32_t tmem_base;
+  int abort;
+};
+
+IRIS_DEVICE void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
+  const int per_group = GROUP_M * num_n;
+  const int group = t / per_group;
+  const int first_m = group * GROUP_M;
+  const int gm = min(GROUP_M, num_m - first_m);
+  const int local = t - group * per_group;
+  mb = first_m + local % gm;
+  nb = local / gm;
+}
+
+IRIS_DEVICE float sigmoidf_fast(float x) { return 1.0f / (1.0f + __expf(-x)); }
+
+IRIS_DEVICE void store_row32(const Params& p, int64_t prow, int col0, const float (&v)[32]) {
+  if (p.out_dtype == 1) {
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + prow * p.ldc + col0;
+    uint32_t packed[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) packed[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) d4[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+  } else {
+    float4* d4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + prow * p.ldc + col0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  }
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                     const Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte alignment for the 128B-swizzled tiles
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* tiles = base;
+  Smem* s = reinterpret_cast<Smem*>(base + STAGES * STAGE_BYTES);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int num_m = (p.M + BM - 1) / BM;
+  const int num_n = (p.N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int nk = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&s->full[i], 1);
+      mbar_init(&s->empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s->tmem_full[i], 1);
+      mbar_init(&s->tmem_empty[i], 4);
+    }
+    mbar_init(&s->teardown, 1);
+    s->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) tmem_alloc(&s->tmem_base, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s->tmem_base;
+  volatile int* abort = &s->abort;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued_phase[STAGES];
+#pragma unroll
+      for (int i = 0; i < STAGES; ++i) issued_phase[i] = -1;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        int mb, nb;
+        tile_coords(t, num_m, num_n, mb, nb);
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&s->empty[stage], phase ^ 1u, abort)) {
+            ok = false;
+            break;
+          }
+          uint8_t* a_dst = tiles + stage * STAGE_BYTES;
+          uint8_t* b_dst = a_dst + A_BYTES;
+          mbar_arrive_expect_tx(&s->full[stage], STAGE_BYTES);
+          tma_load_2d(&tmap_a, &s->full[stage], a_dst, kb * BK, mb * BM);
+          tma_load_2d(&tmap_b, &s->full[stage], b_dst, kb * BK, nb * BN);
+          issued_phase[stage] = static_cast<int>(phase);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // let the copies already in flight land before shared memory is released
+        int dummy = 0;
+        for (int i = 0; i < STAGES; ++i)
+          if (issued_phase[i] >= 0) mbar_wait(&s->full[i], static_cast<uint32_t>(issued_phase[i]), &dummy);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
+        const int acc = it & 1;
+        const uint32_t acc_phase = static_cast<uint32_t>((it >> 1) & 1);
+        if (!mbar_wait(&s->tmem_empty[acc], acc_phase ^ 1u, abort)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&s->full[stage], phase, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_addr(tiles + stage * STAGE_BYTES);
+          const uint32_t b_addr = a_addr + A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = umma_desc(a_addr + k * 32, 16, 1024, kLayoutSw128);
+            const uint64_t bd = umma_desc(b_addr + k * 32, 16, 1024, kLayoutSw128);
+            umma_ss(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&s->empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) umma_commit(&s->tmem_full[acc]);
+      }
+      // all MMAs of this thread are complete once this barrier flips
+      umma_commit(&s->teardown);
+      int dummy = 0;
+      mbar_wait(&s->teardown, 0, &dummy);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32)
+    const int row_in_tile = quarter * 32 + lane;
+    int it = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
+      int mb, nb;
+      tile_coords(t, num_m, num_n, mb, nb);
+      const int acc = it & 1;
+      const uint32_t acc_phase = static_cast<uint32_t>((it >> 1) & 1);
+      // warp-uniform decision: tcgen05.ld below is a .sync.aligned warp instruction
+      if (!__all_sync(0xffffffffu, mbar_wait(&s->tmem_full[acc], acc_phase, abort))) break;
+      tc_fence_after();
+      const uint32_t t_base = tmem + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(quarter * 32) << 16);
+      const int64_t m = static_cast<int64_t>(mb) * BM + row_in_tile;
+      const bool row_ok = m < p.M;
+      if (p.epilogue == EPI_SWIGLU) {
+        const int64_t prow = row_ok ? p.out_map(m) : 0;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t ra[32], rb[32];
+          tmem_ld32(t_base + c * 32, ra);
+          tmem_ld32(t_base + 128 + c * 32, rb);
+          tmem_wait_ld();
+          const int col0 = nb * (BN / 2) + c * 32;
+          if (row_ok && col0 < p.N / 2) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float a = __uint_as_float(ra[j]);
+              v[j] = a * sigmoidf_fast(a) * __uint_as_float(rb[j]);
+            }
+            store_row32(p, prow, col0, v);
+          }
+        }
+      } else {
+        const int64_t prow = row_ok ? p.out_map(m) : 0;
+        const int64_t arow = (row_ok && p.epilogue == EPI_GATE) ? p.aux_map(m) : 0;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(t_base + c * 32, r);
+          tmem_wait_ld();
+          const int col0 = nb * BN + c * 32;
+          if (row_ok && col0 < p.N) {
+            float v[32];
+            if (p.epilogue == EPI_GATE) {
+              const uint4* a4 = reinterpret_cast<const uint4*>(p.aux + arow * p.ldaux + col0);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const uint4 w = a4[j];
+                const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                  const float2 f = unpack_bf16x2(ws[h]);
+                  const int e = j * 8 + h * 2;
+                  v[e] = f.x * sigmoidf_fast(__uint_as_float(r[e]));
+                  v[e + 1] = f.y * sigmoidf_fast(__uint_as_float(r[e + 1]));
+                }
+              }
+            } else if (p.bias != nullptr) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) + __ldg(p.bias + col0 + j);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+            }
+            store_row32(p, prow, col0, v);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s->tmem_empty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+}  // namespace gemm
+}  // namespace iris
+
+using namespace iris;
+
+extern "C" int iris_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw, void* out, int out_dtype,
+                              int64_t ldc, int64_t M, int64_t N, int64_t K, int epilogue, const float* bias,
+                              const void* aux, int64_t ldaux, int64_t out_seg_rows, int64_t out_seg_stride,
+                              int64_t out_seg_offset, int64_t aux_seg_rows, int64_t aux_seg_stride,
+                              int64_t aux_seg_offset, void* stream) {
+  using namespace iris::gemm;
+  IRIS_REQUIRE(a && w && out, "iris_gemm_bf16: null pointer");
+  IRIS_REQUIRE(M > 0 && N > 0 && K > 0, "iris_gemm_bf16: empty problem");
+  IRIS_REQUIRE(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "iris_gemm_bf16: dimension too large");
+  IRIS_REQUIRE(K % 8 == 0 && lda % 8 == 0 && ldw % 8 == 0 && lda >= K && ldw >= K,
+               "iris_gemm_bf16: K and leading dimensions must be multiples of 8 (16-byte TMA rows)");
+  IRIS_REQUIRE(N % 32 == 0, "iris_gemm_bf16: N must be a multiple of 32");
+  IRIS_REQUIRE(epilogue >= EPI_STORE && epilogue <= EPI_GATE, "iris_gemm_bf16: unknown epilogue");
+  IRIS_REQUIRE(out_dtype == 0 || out_dtype == 1, "iris_gemm_bf16: out dtype must be f32 or bf16");
+  IRIS_REQUIRE(aligned16(a) && aligned16(w) && aligned16(out), "iris_gemm_bf16: pointers must be 16-byte aligned");
+  IRIS_REQUIRE(ldc % 8 == 0, "iris_gemm_bf16: ldc must be a multiple of 8");
+  if (epilogue == EPI_SWIGLU) {
+    IRIS_REQUIRE(N % BN == 0 && out_dtype == 1 && ldc >= N / 2,
+                 "iris_gemm_bf16: SwiGLU needs N % 256 == 0 (paired 128-row w1/w3 blocks) and bf16 out");
+  } else {
+    IRIS_REQUIRE(ldc >= N, "iris_gemm_bf16: ldc < N");
+  }
+  if (epilogue == EPI_GATE) {
+    IRIS_REQUIRE(aux != nullptr && aligned16(aux) && ldaux % 8 == 0 && ldaux >= N && out_dtype == 1,
+                 "iris_gemm_bf16: gate epilogue needs an aligned bf16 aux with ldaux % 8 == 0");
+    IRIS_REQUIRE(bias == nullptr, "iris_gemm_bf16: gate epilogue takes no bias");
+  }
+  IRIS_REQUIRE(out_seg_rows > 0 && aux_seg_rows > 0, "iris_gemm_bf16: row maps need seg_rows > 0");
+
+  CUtensorMap ta, tb;
+  IRIS_CHECK_STATUS(make_tmap_2d_bf16(&ta, a, K, M, lda, BK, BM));
+  IRIS_CHECK_STATUS(make_tmap_2d_bf16(&tb, w, K, N, ldw, BK, BN));
+
+  Params p;
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.epilogue = epilogue;
+  p.out_dtype = out_dtype;
+  p.out = out;
+  p.ldc = ldc;
+  p.out_map = RowMap{out_seg_rows, out_seg_stride, out_seg_offset};
+  p.bias = bias;
+  p.aux = reinterpret_cast<const __nv_bfloat16*>(aux);
+  p.ldaux = ldaux;
+  p.aux_map = RowMap{aux_seg_rows, aux_seg_stride, aux_seg_offset};
+
+  static bool configured[64] = {false};
+  int dev = 0;
+  IRIS_CUDA(cudaGetDevice(&dev));
+  if (dev < 64 && !configured[dev]) {
+    IRIS_CUDA(cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(SMEM_BYTES)));
+    configured[dev] = true;
+  }
+  const int tiles = static_cast<int>(((M + BM - 1) / BM) * ((N + BN - 1) / BN));
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  gemm_bf16_kernel<<<grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(ta, tb, p);
+  IRIS_CUDA(cudaGetLastError());
+  return IRIS_OK;
+}

@@ -1,0 +1,9 @@
+// Single translation unit of libiris_b200.so: the device error word and the
+// kernels share one module, so no relocatable device code is needed.
+#include "abi.cu"
+#include "attention.cu"
+#include "gemm.cu"
+#include "heads.cu"
+#include "pixel.cu"
+#include "rows.cu"
+#include "small.cu"

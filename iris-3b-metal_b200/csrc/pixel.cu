@@ -1,0 +1,367 @@
+// Pixel-stage kernels, one thread per pixel with its 16 channels in
+// registers (HBM-bound; the 16 -> 64 -> 16 MLP weights sit in shared memory):
+//   pixel_rms_norm    src/iris_metal/kernels.py:217-232, 486-498
+//   pixel_mlp_        src/iris_metal/kernels.py:235-293, 527-584 (post-mod PiT
+//                     tail, src/iris3b/models/blocks/pit.py:88-92)
+//   pixel_mlp_head    the last block's tail fused with FinalLayer + fold
+//                     (src/iris3b/models/dit.py:53-62, 367-374)
+//   pixel_embed       PixelEmbedder (src/iris3b/nn/embeddings.py:319-328)
+//                     fused with the first block's pixel_rms_norm.
+// With bf16 pixels the kernel rounds where the reference's autocast path
+// materialises bf16 values; with an fp32 pixel stream it rounds nothing.
+#include "common.cuh"
+#include "iris_abi_internal.h"
+
+namespace iris {
+namespace pixel {
+
+constexpr int C = 16;
+constexpr int HID = 64;
+constexpr int THREADS = 256;
+
+IRIS_DEVICE void load16(const void* p, int64_t i, bool f32, float (&x)[C]) {
+  if (f32) {
+    const float4* q = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i * C);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float4 v = q[j];
+      x[4 * j] = v.x; x[4 * j + 1] = v.y; x[4 * j + 2] = v.z; x[4 * j + 3] = v.w;
+    }
+  } else {
+    const uint4* q = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p) + i * C);
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const uint4 u = q[j];
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const float2 f = unpack_bf16x2(w[h]);
+        x[8 * j + 2 * h] = f.x;
+        x[8 * j + 2 * h + 1] = f.y;
+      }
+    }
+  }
+}
+
+IRIS_DEVICE void store16(void* p, int64_t i, bool f32, const float (&x)[C]) {
+  if (f32) {
+    float4* q = reinterpret_cast<float4*>(reinterpret_cast<float*>(p) + i * C);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) q[j] = make_float4(x[4 * j], x[4 * j + 1], x[4 * j + 2], x[4 * j + 3]);
+  } else {
+    uint4* q = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p) + i * C);
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+      q[j] = make_uint4(pack_bf16x2(x[8 * j], x[8 * j + 1]), pack_bf16x2(x[8 * j + 2], x[8 * j + 3]),
+                        pack_bf16x2(x[8 * j + 4], x[8 * j + 5]), pack_bf16x2(x[8 * j + 6], x[8 * j + 7]));
+  }
+}
+
+IRIS_DEVICE float inv_rms16(const float (&x)[C], float eps) {
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < C; ++c) ss += x[c] * x[c];
+  return rsqrtf(ss / C + eps);
+}
+
+IRIS_DEVICE float gelu_erf(float a) { return 0.5f * a * (1.f + erff(a * 0.70710678118654752f)); }
+
+struct MlpWeights {
+  float w1[HID * C];  // [64, 16]
+  float b1[HID];
+  float w2[C * HID];  // [16, 64]
+  float b2[C];
+  float nw[C];
+  float nnw[C];
+  float fw[3 * C];
+  float fb[4];
+};
+
+IRIS_DEVICE void load_weights(MlpWeights& s, const __nv_bfloat16* w1, const __nv_bfloat16* b1,
+                              const __nv_bfloat16* w2, const __nv_bfloat16* b2, const float* nw, const float* nnw,
+                              const float* fw, const float* fb) {
+  for (int i = threadIdx.x; i < HID * C; i += blockDim.x) {
+    s.w1[i] = __bfloat162float(w1[i]);
+    s.w2[i] = __bfloat162float(w2[i]);
+  }
+  for (int i = threadIdx.x; i < HID; i += blockDim.x) s.b1[i] = __bfloat162float(b1[i]);
+  for (int i = threadIdx.x; i < C; i += blockDim.x) {
+    s.b2[i] = __bfloat162float(b2[i]);
+    s.nw[i] = nw[i];
+    s.nnw[i] = nnw ? nnw[i] : 0.f;
+  }
+  if (fw != nullptr) {
+    for (int i = threadIdx.x; i < 3 * C; i += blockDim.x) s.fw[i] = fw[i];
+    for (int i = threadIdx.x; i < 3; i += blockDim.x) s.fb[i] = fb[i];
+  }
+  __syncthreads();
+}
+
+// The post-modulated PiT tail for one pixel; returns the updated stream in x.
+template <bool ROUND>
+IRIS_DEVICE void pit_tail(float (&x)[C], const float (&attn)[C], const __nv_bfloat16* mod, const MlpWeights& s,
+                          float eps) {
+  auto r = [](float v) { return ROUND ? round_bf16(v) : v; };
+  float m[4 * C];
+  {
+    const uint4* q = reinterpret_cast<const uint4*>(mod);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint4 u = q[j];
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const float2 f = unpack_bf16x2(w[h]);
+        m[8 * j + 2 * h] = f.x;
+        m[8 * j + 2 * h + 1] = f.y;
+      }
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < C; ++c) x[c] = r(x[c] + r(attn[c] * (1.f + m[c]) + m[C + c]));
+  const float inv = inv_rms16(x, eps);
+  float h[C];
+#pragma unroll
+  for (int c = 0; c < C; ++c) h[c] = r(x[c] * inv * s.nw[c]);
+  float out[C];
+#pragma unroll
+  for (int c = 0; c < C; ++c) out[c] = s.b2[c];
+#pragma unroll 4
+  for (int j = 0; j < HID; ++j) {
+    float a = s.b1[j];
+#pragma unroll
+    for (int c = 0; c < C; ++c) a = fmaf(h[c], s.w1[j * C + c], a);
+    const float g = r(gelu_erf(r(a)));
+#pragma unroll
+    for (int c = 0; c < C; ++c) out[c] = fmaf(g, s.w2[c * HID + j], out[c]);
+  }
+#pragma unroll
+  for (int c = 0; c < C; ++c) x[c] = r(x[c] + r(r(out[c]) * (1.f + m[2 * C + c]) + m[3 * C + c]));
+}
+
+__global__ void __launch_bounds__(THREADS) pixel_rms_norm_kernel(const void* pixels, bool f32,
+                                                                  __nv_bfloat16* __restrict__ out,
+                                                                  const float* __restrict__ weight, int64_t n,
+                                                                  float eps) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float x[C];
+    load16(pixels, i, f32, x);
+    const float inv = inv_rms16(x, eps);
+#pragma unroll
+    for (int c = 0; c < C; ++c) x[c] = x[c] * inv * __ldg(weight + c);
+    store16(out, i, false, x);
+  }
+}
+
+template <bool F32>
+__global__ void __launch_bounds__(THREADS) pixel_mlp_kernel(void* pixels, const __nv_bfloat16* __restrict__ branch,
+                                                             const __nv_bfloat16* __restrict__ mods,
+                                                             const float* nw, const __nv_bfloat16* w1,
+                                                             const __nv_bfloat16* b1, const __nv_bfloat16* w2,
+                                                             const __nv_bfloat16* b2, const float* nnw,
+                                                             __nv_bfloat16* __restrict__ next_input, int64_t n,
+                                                             float eps) {
+  __shared__ MlpWeights s;
+  load_weights(s, w1, b1, w2, b2, nw, nnw, nullptr, nullptr);
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float x[C], attn[C];
+    load16(pixels, i, F32, x);
+    load16(branch, i, false, attn);
+    pit_tail<!F32>(x, attn, mods + i * 4 * C, s, eps);
+    store16(pixels, i, F32, x);
+    const float inv = inv_rms16(x, eps);
+    float y[C];
+#pragma unroll
+    for (int c = 0; c < C; ++c) y[c] = x[c] * inv * s.nnw[c];
+    store16(next_input, i, false, y);
+  }
+}
+
+template <bool F32>
+__global__ void __launch_bounds__(THREADS) pixel_mlp_head_kernel(
+    const void* pixels, const __nv_bfloat16* __restrict__ branch, const __nv_bfloat16* __restrict__ mods,
+    const float* nw, const __nv_bfloat16* w1, const __nv_bfloat16* b1, const __nv_bfloat16* w2,
+    const __nv_bfloat16* b2, const float* fnw, const float* fw, const float* fb, float* __restrict__ v, int64_t n,
+    int64_t height, int64_t width, int patch, float eps) {
+  __shared__ MlpWeights s;
+  load_weights(s, w1, b1, w2, b2, nw, fnw, fw, fb);
+  const int pp = patch * patch;
+  const int64_t gw = width / patch;
+  const int64_t L = (height / patch) * gw;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float x[C], attn[C];
+    load16(pixels, i, F32, x);
+    load16(branch, i, false, attn);
+    pit_tail<!F32>(x, attn, mods + i * 4 * C, s, eps);
+    const float inv = inv_rms16(x, eps);
+    float h[C];
+#pragma unroll
+    for (int c = 0; c < C; ++c) h[c] = F32 ? x[c] * inv * s.nnw[c] : round_bf16(x[c] * inv * s.nnw[c]);
+    const int64_t patch_idx = i / pp;
+    const int k = static_cast<int>(i % pp);
+    const int64_t b = patch_idx / L, l = patch_idx % L;
+    const int64_t y = (l / gw) * patch + k / patch, xx = (l % gw) * patch + k % patch;
+#pragma unroll
+    for (int ch = 0; ch < 3; ++ch) {
+      float acc = s.fb[ch];
+#pragma unroll
+      for (int c = 0; c < C; ++c) acc = fmaf(h[c], s.fw[ch * C + c], acc);
+      v[((b * 3 + ch) * height + y) * width + xx] = acc;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(THREADS) pixel_embed_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                               const float* __restrict__ bias,
+                                                               const float* __restrict__ pos, void* pixels, bool f32,
+                                                               __nv_bfloat16* __restrict__ normed,
+                                                               const float* __restrict__ nw, float eps, int64_t n,
+                                                               int64_t height, int64_t width, int patch) {
+  __shared__ float sw[3 * C + C + C];
+  for (int i = threadIdx.x; i < 3 * C; i += blockDim.x) sw[i] = w[i];
+  for (int i = threadIdx.x; i < C; i += blockDim.x) {
+    sw[3 * C + i] = bias[i];
+    sw[4 * C + i] = nw[i];
+  }
+  __syncthreads();
+  const int pp = patch * patch;
+  const int64_t gw = width / patch;
+  const int64_t L = (height / patch) * gw;
+  const int64_t plane = height * width;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t patch_idx = i / pp;
+    const int k = static_cast<int>(i % pp);
+    const int64_t b = patch_idx / L, l = patch_idx % L;
+    const int64_t y = (l / gw) * patch + k / patch, xx = (l % gw) * patch + k % patch;
+    const float* xp = x + b * 3 * plane + y * width + xx;
+    const float x0 = xp[0], x1 = xp[plane], x2 = xp[2 * plane];
+    float o[C];
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      // F.linear(x, W, b): sum over the 3 input channels, then the bias
+      o[c] = fmaf(x2, sw[c * 3 + 2], fmaf(x1, sw[c * 3 + 1], x0 * sw[c * 3])) + sw[3 * C + c];
+    }
+    if (pos != nullptr) {
+      const float4* p4 = reinterpret_cast<const float4*>(pos + (y * width + xx) * C);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float4 pv = __ldg(p4 + j);
+        o[4 * j] += pv.x; o[4 * j + 1] += pv.y; o[4 * j + 2] += pv.z; o[4 * j + 3] += pv.w;
+      }
+    }
+    if (!f32) {
+#pragma unroll
+      for (int c = 0; c < C; ++c) o[c] = round_bf16(o[c]);
+    }
+    store16(pixels, i, f32, o);
+    const float inv = inv_rms16(o, eps);
+    float h[C];
+#pragma unroll
+    for (int c = 0; c < C; ++c) h[c] = o[c] * inv * sw[4 * C + c];
+    store16(normed, i, false, h);
+  }
+}
+
+inline unsigned grid_for(int64_t n) {
+  int64_t blocks = (n + THREADS - 1) / THREADS;
+  const int64_t cap = static_cast<int64_t>(num_sms()) * 16;
+  return static_cast<unsigned>(blocks < cap ? blocks : cap);
+}
+
+}  // namespace pixel
+}  // namespace iris
+
+using namespace iris;
+
+static int check_pixel_params(const void* w1, const void* b1, const void* w2, const void* b2, const float* nw) {
+  IRIS_REQUIRE(w1 && b1 && w2 && b2 && nw, "pixel_mlp_ needs the released pixel-stage widths");
+  return IRIS_OK;
+}
+
+extern "C" int iris_pixel_rms_norm(const void* pixels, int pixel_dtype, void* out, const float* weight,
+                                   int64_t n_pixels, float eps, void* stream) {
+  using namespace iris::pixel;
+  IRIS_REQUIRE(pixels && out && weight, "pixel_rms_norm gain width mismatch (null pointer)");
+  IRIS_REQUIRE(pixel_dtype == IRIS_F32 || pixel_dtype == IRIS_BF16, "pixel_rms_norm: pixels must be f32 or bf16");
+  IRIS_REQUIRE(aligned16(pixels) && aligned16(out), "pixel_rms_norm: pointers must be 16-byte aligned");
+  IRIS_REQUIRE(n_pixels >= 0, "pixel_rms_norm: negative size");
+  if (n_pixels == 0) return IRIS_OK;
+  pixel_rms_norm_kernel<<<grid_for(n_pixels), THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
+      pixels, pixel_dtype == IRIS_F32, reinterpret_cast<__nv_bfloat16*>(out), weight, n_pixels, eps);
+  IRIS_CUDA(cudaGetLastError());
+  return IRIS_OK;
+}
+
+extern "C" int iris_pixel_mlp(void* pixels, int pixel_dtype, const void* branch, const void* mods,
+                              const float* norm_weight, const void* fc1_w, const void* fc1_b, const void* fc2_w,
+                              const void* fc2_b, const float* next_norm_weight, void* next_input, int64_t n_pixels,
+                              float eps, void* stream) {
+  using namespace iris::pixel;
+  IRIS_REQUIRE(pixels && branch && mods && next_input && next_norm_weight, "pixel_mlp_: null pointer");
+  IRIS_CHECK_STATUS(check_pixel_params(fc1_w, fc1_b, fc2_w, fc2_b, norm_weight));
+  IRIS_REQUIRE(pixel_dtype == IRIS_F32 || pixel_dtype == IRIS_BF16, "pixel_mlp_: pixels must be f32 or bf16");
+  IRIS_REQUIRE(aligned16(pixels) && aligned16(branch) && aligned16(mods) && aligned16(next_input),
+               "pixel_mlp_: activations must be 16-byte aligned");
+  IRIS_REQUIRE(n_pixels >= 0, "pixel_mlp_: negative size");
+  if (n_pixels == 0) return IRIS_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto bf = [](const void* p) { return reinterpret_cast<const __nv_bfloat16*>(p); };
+  if (pixel_dtype == IRIS_F32)
+    pixel_mlp_kernel<true><<<grid_for(n_pixels), THREADS, 0, st>>>(
+        pixels, bf(branch), bf(mods), norm_weight, bf(fc1_w), bf(fc1_b), bf(fc2_w), bf(fc2_b), next_norm_weight,
+        reinterpret_cast<__nv_bfloat16*>(next_input), n_pixels, eps);
+  else
+    pixel_mlp_kernel<false><<<grid_for(n_pixels), THREADS, 0, st>>>(
+        pixels, bf(branch), bf(mods), norm_weight, bf(fc1_w), bf(fc1_b), bf(fc2_w), bf(fc2_b), next_norm_weight,
+        reinterpret_cast<__nv_bfloat16*>(next_input), n_pixels, eps);
+  IRIS_CUDA(cudaGetLastError());
+  return IRIS_OK;
+}
+
+extern "C" int iris_pixel_mlp_head(void* pixels, int pixel_dtype, const void* branch, const void* mods,
+                                   const float* norm_weight, const void* fc1_w, const void* fc1_b, const void* fc2_w,
+                                   const void* fc2_b, const float* final_norm_weight, const float* final_w,
+                                   const float* final_b, float* v, int64_t batch, int64_t height, int64_t width,
+                                   int64_t patch, float eps, void* stream) {
+  using namespace iris::pixel;
+  IRIS_REQUIRE(pixels && branch && mods && final_norm_weight && final_w && final_b && v, "pixel_mlp_head: null pointer");
+  IRIS_CHECK_STATUS(check_pixel_params(fc1_w, fc1_b, fc2_w, fc2_b, norm_weight));
+  IRIS_REQUIRE(pixel_dtype == IRIS_F32 || pixel_dtype == IRIS_BF16, "pixel_mlp_head: pixels must be f32 or bf16");
+  IRIS_REQUIRE(patch > 0 && height % patch == 0 && width % patch == 0 && batch >= 0, "pixel_mlp_head: bad geometry");
+  IRIS_REQUIRE(aligned16(pixels) && aligned16(branch) && aligned16(mods), "pixel_mlp_head: alignment");
+  const int64_t n = batch * height * width;
+  if (n == 0) return IRIS_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto bf = [](const void* p) { return reinterpret_cast<const __nv_bfloat16*>(p); };
+  if (pixel_dtype == IRIS_F32)
+    pixel_mlp_head_kernel<true><<<grid_for(n), THREADS, 0, st>>>(
+        pixels, bf(branch), bf(mods), norm_weight, bf(fc1_w), bf(fc1_b), bf(fc2_w), bf(fc2_b), final_norm_weight,
+        final_w, final_b, v, n, height, width, static_cast<int>(patch), eps);
+  else
+    pixel_mlp_head_kernel<false><<<grid_for(n), THREADS, 0, st>>>(
+        pixels, bf(branch), bf(mods), norm_weight, bf(fc1_w), bf(fc1_b), bf(fc2_w), bf(fc2_b), final_norm_weight,
+        final_w, final_b, v, n, height, width, static_cast<int>(patch), eps);
+  IRIS_CUDA(cudaGetLastError());
+  return IRIS_OK;
+}
+
+extern "C" int iris_pixel_embed(const float* x, const float* w, const float* bias, const float* pos, void* pixels,
+                                int pixel_dtype, void* normed, const float* norm_weight, float eps, int64_t batch,
+                                int64_t height, int64_t width, int64_t patch, void* stream) {
+  using namespace iris::pixel;
+  IRIS_REQUIRE(x && w && bias && pixels && normed && norm_weight, "pixel_embed: null pointer");
+  IRIS_REQUIRE(pixel_dtype == IRIS_F32 || pixel_dtype == IRIS_BF16, "pixel_embed: pixels must be f32 or bf16");
+  IRIS_REQUIRE(patch > 0 && height % patch == 0 && width % patch == 0 && batch >= 0, "pixel_embed: bad geometry");
+  IRIS_REQUIRE(aligned16(pixels) && aligned16(normed) && (pos == nullptr || aligned16(pos)), "pixel_embed: alignment");
+  const int64_t n = batch * height * width;
+  if (n == 0) return IRIS_OK;
+  pixel_embed_kernel<<<grid_for(n), THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, w, bias, pos, pixels, pixel_dtype == IRIS_F32, reinterpret_cast<__nv_bfloat16*>(normed), norm_weight, eps, n,
+      height, width, static_cast<int>(patch));
+  IRIS_CUDA(cudaGetLastError());
+  return IRIS_OK;
+}

@@ -1,0 +1,378 @@
+// Row kernels on the 3072-wide residual stream (HBM-bound):
+//   rms_norm_modulate           src/iris_metal/kernels.py:116-146, 413-452
+//   gated_residual_rms_norm(+)  src/iris_metal/kernels.py:148-175, 455-480
+//   rms_norm_add_rows           TextEmbedder norm + position table
+//
+// One warp per row; lane l owns the 4-element vectors l, l + 32, ... so every
+// warp load is one coalesced 512-byte (fp32) or 256-byte (bf16) segment. The
+// whole row stays in registers (NV vectors per lane, width = 128 * NV), so
+// each row is read once and written once; the sum of squares is a warp
+// shuffle reduction.
+#include "common.cuh"
+#include "iris_abi_internal.h"
+
+namespace iris {
+namespace rows {
+
+constexpr int WARPS = 8;  // rows per 256-thread block
+
+template <typename T>
+struct Vec4 {};
+template <>
+struct Vec4<float> {
+  IRIS_DEVICE static float4 load(const float* p) { return *reinterpret_cast<const float4*>(p); }
+  IRIS_DEVICE static void store(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
+};
+template <>
+struct Vec4<__nv_bfloat16> {
+  IRIS_DEVICE static float4 load(const __nv_bfloat16* p) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y);
+    return make_float4(a.x, a.y, b.x, b.y);
+  }
+  IRIS_DEVICE static void store(__nv_bfloat16* p, float4 v) {
+    *reinterpret_cast<uint2*>(p) = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+  }
+};
+template <>
+struct Vec4<__half> {
+  IRIS_DEVICE static float4 load(const __half* p) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+  }
+  IRIS_DEVICE static void store(__half* p, float4 v) {
+    *reinterpret_cast<uint2*>(p) = make_uint2(pack_f16x2(v.x, v.y), pack_f16x2(v.z, v.w));
+  }
+};
+
+IRIS_DEVICE float4 ld4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+IRIS_DEVICE float sumsq(float4 v) { return v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w; }
+
+template <typename TX, typename TO, int NV>
+__global__ void __launch_bounds__(WARPS * 32) rms_norm_modulate_kernel(
+    const TX* __restrict__ x, RowMap xmap, TO* __restrict__ out, const float* __restrict__ weight,
+    const float* __restrict__ shift, const float* __restrict__ scale, int64_t mod_stride, int64_t rows,
+    int64_t rows_per_batch, int width, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * WARPS + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const TX* xr = x + xmap(r) * width;
+  const int nv = width >> 7;
+  float4 v[NV];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    if (i < nv) {
+      v[i] = Vec4<TX>::load(xr + (i * 32 + lane) * 4);
+      ss += sumsq(v[i]);
+    }
+  }
+  ss = warp_sum(ss);
+  const float inv = rsqrtf(ss / static_cast<float>(width) + eps);
+  const int64_t b = r / rows_per_batch;
+  const float* sh = shift + b * mod_stride;
+  const float* sc = scale + b * mod_stride;
+  TO* o = out + r * width;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    if (i < nv) {
+      const int e = (i * 32 + lane) * 4;
+      const float4 w = ld4(weight + e), s4 = ld4(sh + e), c4 = ld4(sc + e);
+      float4 h;
+      h.x = v[i].x * inv * w.x * (1.f + c4.x) + s4.x;
+      h.y = v[i].y * inv * w.y * (1.f + c4.y) + s4.y;
+      h.z = v[i].z * inv * w.z * (1.f + c4.z) + s4.z;
+      h.w = v[i].w * inv * w.w * (1.f + c4.w) + s4.w;
+      Vec4<TO>::store(o + e, h);
+    }
+  }
+}
+
+// residual[r] += gate[b] * rms_norm(branch[r]) * weight; then optionally the
+// next branch input from the updated row (norm+modulate or silu(t + x)).
+template <typename TB, typename TO, int NV>
+__global__ void __launch_bounds__(WARPS * 32) gated_residual_kernel(
+    float* __restrict__ residual, RowMap rmap, const TB* __restrict__ branch, RowMap bmap,
+    const float* __restrict__ weight, const float* __restrict__ gate, int64_t mod_stride, int64_t rows,
+    int64_t rows_per_batch, int width, float eps, int next_mode, const float* __restrict__ next_weight,
+    const float* __restrict__ next_shift, const float* __restrict__ next_scale, int64_t next_mod_stride,
+    TO* __restrict__ next_out, RowMap nmap) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * WARPS + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const int nv = width >> 7;
+  const TB* br = branch + bmap(r) * width;
+  float* xr = residual + rmap(r) * width;
+  float4 v[NV];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    if (i < nv) {
+      v[i] = Vec4<TB>::load(br + (i * 32 + lane) * 4);
+      ss += sumsq(v[i]);
+    }
+  }
+  ss = warp_sum(ss);
+  const float inv = rsqrtf(ss / static_cast<float>(width) + eps);
+  const int64_t b = r / rows_per_batch;
+  const float* g = gate + b * mod_stride;
+  float ss2 = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    if (i < nv) {
+      const int e = (i * 32 + lane) * 4;
+      const float4 w = ld4(weight + e), g4 = ld4(g + e);
+      float4 x = *reinterpret_cast<const float4*>(xr + e);
+      x.x += g4.x * (v[i].x * inv * w.x);
+      x.y += g4.y * (v[i].y * inv * w.y);
+      x.z += g4.z * (v[i].z * inv * w.z);
+      x.w += g4.w * (v[i].w * inv * w.w);
+      *reinterpret_cast<float4*>(xr + e) = x;
+      v[i] = x;
+      ss2 += sumsq(x);
+    }
+  }
+  if (next_mode == IRIS_NEXT_NONE) return;
+  TO* o = next_out + nmap(r) * width;
+  const float* sh = next_shift + b * next_mod_stride;
+  if (next_mode == IRIS_NEXT_NORM_MODULATE) {
+    ss2 = warp_sum(ss2);
+    const float inv2 = rsqrtf(ss2 / static_cast<float>(width) + eps);
+    const float* sc = next_scale + b * next_mod_stride;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      if (i < nv) {
+        const int e = (i * 32 + lane) * 4;
+        const float4 w = ld4(next_weight + e), s4 = ld4(sh + e), c4 = ld4(sc + e);
+        float4 h;
+        h.x = v[i].x * inv2 * w.x * (1.f + c4.x) + s4.x;
+        h.y = v[i].y * inv2 * w.y * (1.f + c4.y) + s4.y;
+        h.z = v[i].z * inv2 * w.z * (1.f + c4.z) + s4.z;
+        h.w = v[i].w * inv2 * w.w * (1.f + c4.w) + s4.w;
+        Vec4<TO>::store(o + e, h);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      if (i < nv) {
+        const int e = (i * 32 + lane) * 4;
+        const float4 t4 = ld4(sh + e);
+        float4 h;
+        const float a0 = t4.x + v[i].x, a1 = t4.y + v[i].y, a2 = t4.z + v[i].z, a3 = t4.w + v[i].w;
+        h.x = a0 / (1.f + __expf(-a0));
+        h.y = a1 / (1.f + __expf(-a1));
+        h.z = a2 / (1.f + __expf(-a2));
+        h.w = a3 / (1.f + __expf(-a3));
+        Vec4<TO>::store(o + e, h);
+      }
+    }
+  }
+}
+
+template <int NV>
+__global__ void __launch_bounds__(WARPS * 32) rms_norm_add_kernel(float* __restrict__ x,
+                                                                   const float* __restrict__ weight,
+                                                                   const float* __restrict__ add, int64_t rows,
+                                                                   int64_t rows_per_batch, int width, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * WARPS + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const int nv = width >> 7;
+  float* xr = x + r * width;
+  const float* ar = add + (r % rows_per_batch) * width;
+  float4 v[NV];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    if (i < nv) {
+      v[i] = *reinterpret_cast<const float4*>(xr + (i * 32 + lane) * 4);
+      ss += sumsq(v[i]);
+    }
+  }
+  ss = warp_sum(ss);
+  const float inv = rsqrtf(ss / static_cast<float>(width) + eps);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    if (i < nv) {
+      const int e = (i * 32 + lane) * 4;
+      const float4 w = ld4(weight + e), a = ld4(ar + e);
+      float4 h;
+      h.x = w.x * (v[i].x * inv) + a.x;
+      h.y = w.y * (v[i].y * inv) + a.y;
+      h.z = w.z * (v[i].z * inv) + a.z;
+      h.w = w.w * (v[i].w * inv) + a.w;
+      *reinterpret_cast<float4*>(xr + e) = h;
+    }
+  }
+}
+
+// NV buckets: a row of width 128 * nv runs with the smallest bucket >= nv.
+#define IRIS_NV_DISPATCH(nv, MACRO) \
+  if ((nv) <= 2) {                  \
+    MACRO(2);                       \
+  } else if ((nv) <= 4) {           \
+    MACRO(4);                       \
+  } else if ((nv) <= 8) {           \
+    MACRO(8);                       \
+  } else if ((nv) <= 16) {          \
+    MACRO(16);                      \
+  } else if ((nv) <= 24) {          \
+    MACRO(24);                      \
+  } else {                          \
+    MACRO(32);                      \
+  }
+
+template <typename TX, typename TO>
+int launch_norm_modulate(const void* x, RowMap xm, void* out, const float* w, const float* sh, const float* sc,
+                         int64_t mod_stride, int64_t rows, int64_t rpb, int width, float eps, cudaStream_t st) {
+  const int nv = width / 128;
+  const unsigned grid = static_cast<unsigned>((rows + WARPS - 1) / WARPS);
+#define IRIS_LAUNCH(NV)                                                                                           \
+  rms_norm_modulate_kernel<TX, TO, NV><<<grid, WARPS * 32, 0, st>>>(reinterpret_cast<const TX*>(x), xm,          \
+                                                                     reinterpret_cast<TO*>(out), w, sh, sc,      \
+                                                                     mod_stride, rows, rpb, width, eps)
+  IRIS_NV_DISPATCH(nv, IRIS_LAUNCH)
+#undef IRIS_LAUNCH
+  IRIS_CUDA(cudaGetLastError());
+  return IRIS_OK;
+}
+
+template <typename TB, typename TO>
+int launch_residual(float* res, RowMap rm, const void* branch, RowMap bm, const float* w, const float* gate,
+                    int64_t ms, int64_t rows, int64_t rpb, int width, float eps, int mode, const float* nw,
+                    const float* nsh, const float* nsc, int64_t nms, void* nout, RowMap nm, cudaStream_t st) {
+  const int nv = width / 128;
+  const unsigned grid = static_cast<unsigned>((rows + WARPS - 1) / WARPS);
+#define IRIS_LAUNCH(NV)                                                                                            \
+  gated_residual_kernel<TB, TO, NV><<<grid, WARPS * 32, 0, st>>>(res, rm, reinterpret_cast<const TB*>(branch), bm, \
+                                                                  w, gate, ms, rows, rpb, width, eps, mode, nw, nsh,  \
+                                                                  nsc, nms, reinterpret_cast<TO*>(nout), nm)
+  IRIS_NV_DISPATCH(nv, IRIS_LAUNCH)
+#undef IRIS_LAUNCH
+  IRIS_CUDA(cudaGetLastError());
+  return IRIS_OK;
+}
+
+}  // namespace rows
+}  // namespace iris
+
+using namespace iris;
+
+static int check_mod(const float* p, int64_t stride, const char* name) {
+  if (p == nullptr) return set_error(IRIS_EINVAL, "%s: null modulation pointer", name);
+  if (!aligned16(p) || stride % 4 != 0)
+    return set_error(IRIS_EINVAL, "%s: modulation rows must be 16-byte aligned (stride %% 4 == 0)", name);
+  return IRIS_OK;
+}
+
+extern "C" int iris_rms_norm_modulate(const void* x, int x_dtype, int64_t x_seg_rows, int64_t x_seg_stride,
+                                      int64_t x_seg_offset, void* out, int out_dtype, const float* weight,
+                                      const float* shift, const float* scale, int64_t mod_stride, int64_t rows,
+                                      int64_t rows_per_batch, int64_t width, float eps, void* stream) {
+  using namespace iris::rows;
+  IRIS_REQUIRE(x && out && weight, "rms_norm_modulate: null pointer");
+  IRIS_REQUIRE(width > 0 && width % 128 == 0 && width <= 4096,
+               "rms_norm_modulate needs a contiguous input, width % 128 == 0 (and <= 4096)");
+  IRIS_REQUIRE(rows >= 0 && rows_per_batch > 0 && x_seg_rows > 0, "rms_norm_modulate: bad row counts");
+  IRIS_REQUIRE(x_dtype == IRIS_F32 || x_dtype == IRIS_BF16, "rms_norm_modulate: x must be f32 or bf16");
+  IRIS_REQUIRE(out_dtype >= IRIS_F32 && out_dtype <= IRIS_F16, "rms_norm_modulate: bad out dtype");
+  IRIS_REQUIRE(aligned16(x) && aligned16(out) && aligned16(weight), "rms_norm_modulate: pointers must be 16-byte aligned");
+  IRIS_CHECK_STATUS(check_mod(shift, mod_stride, "rms_norm_modulate"));
+  IRIS_CHECK_STATUS(check_mod(scale, mod_stride, "rms_norm_modulate"));
+  if (rows == 0) return IRIS_OK;
+  const RowMap xm{x_seg_rows, x_seg_stride, x_seg_offset};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int w = static_cast<int>(width);
+  if (x_dtype == IRIS_F32) {
+    if (out_dtype == IRIS_BF16)
+      return launch_norm_modulate<float, __nv_bfloat16>(x, xm, out, weight, shift, scale, mod_stride, rows,
+                                                        rows_per_batch, w, eps, st);
+    if (out_dtype == IRIS_F16)
+      return launch_norm_modulate<float, __half>(x, xm, out, weight, shift, scale, mod_stride, rows, rows_per_batch,
+                                                 w, eps, st);
+    return launch_norm_modulate<float, float>(x, xm, out, weight, shift, scale, mod_stride, rows, rows_per_batch, w,
+                                              eps, st);
+  }
+  if (out_dtype == IRIS_BF16)
+    return launch_norm_modulate<__nv_bfloat16, __nv_bfloat16>(x, xm, out, weight, shift, scale, mod_stride, rows,
+                                                              rows_per_batch, w, eps, st);
+  if (out_dtype == IRIS_F16)
+    return launch_norm_modulate<__nv_bfloat16, __half>(x, xm, out, weight, shift, scale, mod_stride, rows,
+                                                       rows_per_batch, w, eps, st);
+  return launch_norm_modulate<__nv_bfloat16, float>(x, xm, out, weight, shift, scale, mod_stride, rows,
+                                                    rows_per_batch, w, eps, st);
+}
+
+extern "C" int iris_gated_residual_rms_norm(float* residual, int64_t res_seg_rows, int64_t res_seg_stride,
+                                            int64_t res_seg_offset, const void* branch, int branch_dtype,
+                                            int64_t br_seg_rows, int64_t br_seg_stride, int64_t br_seg_offset,
+                                            const float* weight, const float* gate, int64_t mod_stride, int64_t rows,
+                                            int64_t rows_per_batch, int64_t width, float eps, int next_mode,
+                                            const float* next_weight, const float* next_shift,
+                                            const float* next_scale, int64_t next_mod_stride, void* next_out,
+                                            int next_out_dtype, int64_t nx_seg_rows, int64_t nx_seg_stride,
+                                            int64_t nx_seg_offset, void* stream) {
+  using namespace iris::rows;
+  IRIS_REQUIRE(residual && branch && weight, "gated_residual_rms_norm_: null pointer");
+  IRIS_REQUIRE(width > 0 && width % 128 == 0 && width <= 4096, "gated_residual_rms_norm_: width % 128 != 0");
+  IRIS_REQUIRE(rows >= 0 && rows_per_batch > 0 && res_seg_rows > 0 && br_seg_rows > 0,
+               "gated_residual_rms_norm_: bad row counts");
+  IRIS_REQUIRE(branch_dtype >= IRIS_F32 && branch_dtype <= IRIS_F16, "gated_residual_rms_norm_: bad branch dtype");
+  IRIS_REQUIRE(aligned16(residual) && aligned16(branch) && aligned16(weight),
+               "gated_residual_rms_norm_: pointers must be 16-byte aligned");
+  IRIS_CHECK_STATUS(check_mod(gate, mod_stride, "gated_residual_rms_norm_"));
+  IRIS_REQUIRE(next_mode >= IRIS_NEXT_NONE && next_mode <= IRIS_NEXT_SILU_ADD, "gated_residual_rms_norm_: bad next_mode");
+  if (next_mode != IRIS_NEXT_NONE) {
+    IRIS_REQUIRE(next_out && aligned16(next_out), "gated_residual_rms_norm_: next output must be 16-byte aligned");
+    IRIS_REQUIRE(next_out_dtype == IRIS_BF16 || next_out_dtype == IRIS_F32, "gated_residual_rms_norm_: next dtype");
+    IRIS_REQUIRE(nx_seg_rows > 0, "gated_residual_rms_norm_: next row map needs seg_rows > 0");
+    IRIS_CHECK_STATUS(check_mod(next_shift, next_mod_stride, "gated_residual_rms_norm_ (next)"));
+    if (next_mode == IRIS_NEXT_NORM_MODULATE) {
+      IRIS_REQUIRE(next_weight && aligned16(next_weight), "gated_residual_rms_norm_: next weight");
+      IRIS_CHECK_STATUS(check_mod(next_scale, next_mod_stride, "gated_residual_rms_norm_ (next)"));
+    }
+  }
+  if (rows == 0) return IRIS_OK;
+  const RowMap rm{res_seg_rows, res_seg_stride, res_seg_offset};
+  const RowMap bm{br_seg_rows, br_seg_stride, br_seg_offset};
+  const RowMap nm{nx_seg_rows > 0 ? nx_seg_rows : 1, nx_seg_stride, nx_seg_offset};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int w = static_cast<int>(width);
+#define IRIS_RES(TB, TO)                                                                                          \
+  return launch_residual<TB, TO>(residual, rm, branch, bm, weight, gate, mod_stride, rows, rows_per_batch, w, eps, \
+                                 next_mode, next_weight, next_shift, next_scale, next_mod_stride, next_out, nm, st)
+  const bool nf32 = next_out_dtype == IRIS_F32;
+  if (branch_dtype == IRIS_BF16) {
+    if (nf32) IRIS_RES(__nv_bfloat16, float);
+    IRIS_RES(__nv_bfloat16, __nv_bfloat16);
+  }
+  if (branch_dtype == IRIS_F16) {
+    if (nf32) IRIS_RES(__half, float);
+    IRIS_RES(__half, __nv_bfloat16);
+  }
+  if (nf32) IRIS_RES(float, float);
+  IRIS_RES(float, __nv_bfloat16);
+#undef IRIS_RES
+}
+
+extern "C" int iris_rms_norm_add_rows(float* x, const float* weight, const float* add, int64_t rows,
+                                      int64_t rows_per_batch, int64_t width, float eps, void* stream) {
+  using namespace iris::rows;
+  IRIS_REQUIRE(x && weight && add, "rms_norm_add_rows: null pointer");
+  IRIS_REQUIRE(width > 0 && width % 128 == 0 && width <= 4096, "rms_norm_add_rows: width % 128 != 0");
+  IRIS_REQUIRE(rows >= 0 && rows_per_batch > 0, "rms_norm_add_rows: bad row counts");
+  IRIS_REQUIRE(aligned16(x) && aligned16(weight) && aligned16(add), "rms_norm_add_rows: alignment");
+  if (rows == 0) return IRIS_OK;
+  const int nv = static_cast<int>(width / 128);
+  const unsigned grid = static_cast<unsigned>((rows + WARPS - 1) / WARPS);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+#define IRIS_LAUNCH(NV) \
+  rms_norm_add_kernel<NV><<<grid, WARPS * 32, 0, st>>>(x, weight, add, rows, rows_per_batch, static_cast<int>(width), eps)
+  IRIS_NV_DISPATCH(nv, IRIS_LAUNCH)
+#undef IRIS_LAUNCH
+  IRIS_CUDA(cudaGetLastError());
+  return IRIS_OK;
+}

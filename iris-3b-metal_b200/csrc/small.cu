@@ -1,0 +1,274 @@
+// Layout, conditioning and sampler kernels around the trunk:
+//   patchify / unpatchify    integer index maps (bit-exact), dit.py:326, 367-374
+//   timestep_embedding       src/iris3b/nn/embeddings.py:41-45
+//   gemv                     small-M linear (conditioning MLP, shared adaLN cores)
+//   add_bias_rows            SharedCoreBias, src/iris3b/nn/modulation.py:284-285
+//   cfg_euler                CFG combine + flow-Euler step, solver.py:72-74, sampling.py:129-135
+//   all_finite               require_finite, src/iris_metal/model.py:102-110
+#include "common.cuh"
+#include "iris_abi_internal.h"
+
+namespace iris {
+namespace small {
+
+constexpr int THREADS = 256;
+
+inline unsigned grid_for(int64_t n, int per_thread = 1) {
+  int64_t blocks = (n + static_cast<int64_t>(THREADS) * per_thread - 1) / (static_cast<int64_t>(THREADS) * per_thread);
+  const int64_t cap = static_cast<int64_t>(num_sms()) * 32;
+  if (blocks < 1) blocks = 1;
+  return static_cast<unsigned>(blocks < cap ? blocks : cap);
+}
+
+// out[(b, gy, gx), (c, ky, kx)] = x[b, c, gy p + ky, gx p + kx]
+__global__ void patchify_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ out, int64_t total,
+                                int channels, int64_t height, int64_t width, int patch) {
+  const int64_t gw = width / patch, L = (height / patch) * gw;
+  const int64_t feat = static_cast<int64_t>(channels) * patch * patch;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = i / feat, f = i % feat;
+    const int64_t b = row / L, l = row % L;
+    const int c = static_cast<int>(f / (patch * patch));
+    const int k = static_cast<int>(f % (patch * patch));
+    const int64_t y = (l / gw) * patch + k / patch, xx = (l % gw) * patch + k % patch;
+    out[i] = __float2bfloat16_rn(x[((b * channels + c) * height + y) * width + xx]);
+  }
+}
+
+// v[b, c, y, x] = out[(b, gy, gx), ky p + kx, c]
+__global__ void unpatchify_kernel(const float* __restrict__ src, float* __restrict__ v, int64_t total, int channels,
+                                  int64_t height, int64_t width, int patch) {
+  const int64_t gw = width / patch, L = (height / patch) * gw;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t xx = i % width;
+    const int64_t y = (i / width) % height;
+    const int64_t c = (i / (width * height)) % channels;
+    const int64_t b = i / (width * height * channels);
+    const int64_t l = (y / patch) * gw + xx / patch;
+    const int64_t k = (y % patch) * patch + xx % patch;
+    v[i] = src[((b * L + l) * patch * patch + k) * channels + c];
+  }
+}
+
+__global__ void timestep_kernel(const float* __restrict__ t, float* __restrict__ out, int64_t batch, int half,
+                                float log_period) {
+  const int64_t total = batch * half;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t b = i / half;
+    const int k = static_cast<int>(i % half);
+    // exp(-ln(max_period) * k / n), then the fp32 product with t, as the reference evaluates it
+    const float freq = expf(-log_period * static_cast<float>(k) / static_cast<float>(half));
+    const float phase = t[b] * freq;
+    out[b * 2 * half + k] = cosf(phase);
+    out[b * 2 * half + half + k] = sinf(phase);
+  }
+}
+
+IRIS_DEVICE float silu(float v) { return v / (1.f + __expf(-v)); }
+
+// One warp per output column n, up to MT rows of x per pass: the weight row is
+// streamed once per pass with 16-byte loads.
+template <typename TW, int MT>
+__global__ void __launch_bounds__(THREADS) gemv_kernel(const float* __restrict__ x, int M, int K,
+                                                       const TW* __restrict__ w, const float* __restrict__ bias,
+                                                       float* __restrict__ out, int N, int act_in, int act_out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t n = static_cast<int64_t>(blockIdx.x) * (THREADS / 32) + (threadIdx.x >> 5);
+  if (n >= N) return;
+  const TW* wr = w + n * K;
+  for (int m0 = 0; m0 < M; m0 += MT) {
+    float acc[MT];
+#pragma unroll
+    for (int j = 0; j < MT; ++j) acc[j] = 0.f;
+    for (int k = lane * 8; k < K; k += 32 * 8) {
+      float wv[8];
+      if constexpr (sizeof(TW) == 2) {
+        const uint4 u = *reinterpret_cast<const uint4*>(wr + k);
+        const uint32_t ws[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const float2 f = unpack_bf16x2(ws[h]);
+          wv[2 * h] = f.x;
+          wv[2 * h + 1] = f.y;
+        }
+      } else {
+        const float4 a = *reinterpret_cast<const float4*>(wr + k), b = *reinterpret_cast<const float4*>(wr + k + 4);
+        wv[0] = a.x; wv[1] = a.y; wv[2] = a.z; wv[3] = a.w; wv[4] = b.x; wv[5] = b.y; wv[6] = b.z; wv[7] = b.w;
+      }
+#pragma unroll
+      for (int j = 0; j < MT; ++j) {
+        if (m0 + j < M) {
+          const float* xr = x + static_cast<int64_t>(m0 + j) * K + k;
+          const float4 a = __ldg(reinterpret_cast<const float4*>(xr));
+          const float4 b = __ldg(reinterpret_cast<const float4*>(xr + 4));
+          float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[j] = fmaf(act_in ? silu(xv[e]) : xv[e], wv[e], acc[j]);
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < MT; ++j) {
+      const float s = warp_sum(acc[j]);
+      if (lane == 0 && m0 + j < M) {
+        float r = s + (bias ? bias[n] : 0.f);
+        out[static_cast<int64_t>(m0 + j) * N + n] = act_out ? silu(r) : r;
+      }
+    }
+  }
+}
+
+__global__ void add_bias_rows_kernel(const float* __restrict__ core, const float* __restrict__ bias,
+                                     float* __restrict__ out, int64_t batch, int64_t n_blocks, int64_t width) {
+  const int64_t total = n_blocks * batch * width;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t e = i % width;
+    const int64_t b = (i / width) % batch;
+    const int64_t j = i / (width * batch);
+    out[i] = core[b * width + e] + bias[j * width + e];
+  }
+}
+
+__global__ void cfg_euler_kernel(const float* __restrict__ v, const float* __restrict__ x, float* __restrict__ x_out,
+                                 int64_t images, int64_t per_image, float cfg_scale, float sigma, float sigma_next,
+                                 int guided) {
+  const int64_t total = images * per_image;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float vel;
+    if (guided) {
+      const float u = v[i], c = v[total + i];
+      vel = u + cfg_scale * (c - u);
+    } else {
+      vel = v[i];
+    }
+    const float xi = x[i];
+    const float clean = xi - sigma * vel;
+    if (sigma_next < 0.f) {
+      x_out[i] = clean;
+    } else {
+      const float implied = (xi - (1.f - sigma) * clean) / sigma;
+      x_out[i] = (1.f - sigma_next) * clean + sigma_next * implied;
+    }
+  }
+}
+
+__global__ void all_finite_kernel(const float* __restrict__ x, int64_t n, int* flag) {
+  int bad = 0;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    bad |= !isfinite(x[i]);
+  bad = __syncthreads_or(bad);
+  if (bad && threadIdx.x == 0) atomicExch(flag, 0);
+}
+
+__global__ void set_int_kernel(int* p, int v) { *p = v; }
+
+}  // namespace small
+}  // namespace iris
+
+using namespace iris;
+
+extern "C" int iris_patchify(const float* x, void* out, int64_t batch, int64_t channels, int64_t height,
+                             int64_t width, int64_t patch, void* stream) {
+  using namespace iris::small;
+  IRIS_REQUIRE(x && out, "patchify: null pointer");
+  IRIS_REQUIRE(patch > 0 && height % patch == 0 && width % patch == 0 && batch >= 0 && channels > 0,
+               "input is not divisible by patch_size");
+  const int64_t total = batch * channels * height * width;
+  if (total == 0) return IRIS_OK;
+  patchify_kernel<<<grid_for(total), THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, reinterpret_cast<__nv_bfloat16*>(out), total, static_cast<int>(channels), height, width,
+      static_cast<int>(patch));
+  IRIS_CUDA(cudaGetLastError());
+  return IRIS_OK;
+}
+
+extern "C" int iris_unpatchify(const float* out, float* v, int64_t batch, int64_t channels, int64_t height,
+                               int64_t width, int64_t patch, void* stream) {
+  using namespace iris::small;
+  IRIS_REQUIRE(out && v, "unpatchify: null pointer");
+  IRIS_REQUIRE(patch > 0 && height % patch == 0 && width % patch == 0 && batch >= 0 && channels > 0,
+               "input is not divisible by patch_size");
+  const int64_t total = batch * channels * height * width;
+  if (total == 0) return IRIS_OK;
+  unpatchify_kernel<<<grid_for(total), THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
+      out, v, total, static_cast<int>(channels), height, width, static_cast<int>(patch));
+  IRIS_CUDA(cudaGetLastError());
+  return IRIS_OK;
+}
+
+extern "C" int iris_timestep_embedding(const float* t, float* out, int64_t batch, int64_t freq_dim, float max_period,
+                                       void* stream) {
+  using namespace iris::small;
+  IRIS_REQUIRE(t && out, "timestep_embedding: null pointer");
+  IRIS_REQUIRE(freq_dim > 0 && freq_dim % 2 == 0, "freq_dim must be even");
+  IRIS_REQUIRE(max_period > 0.f, "timestep_embedding: max_period must be positive");
+  if (batch <= 0) return IRIS_OK;
+  const int half = static_cast<int>(freq_dim / 2);
+  timestep_kernel<<<grid_for(batch * half), THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
+      t, out, batch, half, logf(max_period));
+  IRIS_CUDA(cudaGetLastError());
+  return IRIS_OK;
+}
+
+extern "C" int iris_gemv(const float* x, int64_t M, int64_t K, const void* w, int w_dtype, const float* bias,
+                         float* out, int64_t N, int act_in, int act_out, void* stream) {
+  using namespace iris::small;
+  IRIS_REQUIRE(x && w && out, "gemv: null pointer");
+  IRIS_REQUIRE(M > 0 && N > 0 && K > 0 && K % 8 == 0, "gemv: K must be a positive multiple of 8");
+  IRIS_REQUIRE(M < (1 << 20) && N < (1ll << 31) && K < (1ll << 31), "gemv: size");
+  IRIS_REQUIRE(w_dtype == IRIS_F32 || w_dtype == IRIS_BF16, "gemv: weights must be f32 or bf16");
+  IRIS_REQUIRE(aligned16(x) && aligned16(w), "gemv: pointers must be 16-byte aligned");
+  const unsigned grid = static_cast<unsigned>((N + THREADS / 32 - 1) / (THREADS / 32));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (w_dtype == IRIS_BF16)
+    gemv_kernel<__nv_bfloat16, 4><<<grid, THREADS, 0, st>>>(x, static_cast<int>(M), static_cast<int>(K),
+                                                             reinterpret_cast<const __nv_bfloat16*>(w), bias, out,
+                                                             static_cast<int>(N), act_in, act_out);
+  else
+    gemv_kernel<float, 4><<<grid, THREADS, 0, st>>>(x, static_cast<int>(M), static_cast<int>(K),
+                                                     reinterpret_cast<const float*>(w), bias, out,
+                                                     static_cast<int>(N), act_in, act_out);
+  IRIS_CUDA(cudaGetLastError());
+  return IRIS_OK;
+}
+
+extern "C" int iris_add_bias_rows(const float* core, const float* bias, float* out, int64_t batch, int64_t n_blocks,
+                                  int64_t width, void* stream) {
+  using namespace iris::small;
+  IRIS_REQUIRE(core && bias && out, "add_bias_rows: null pointer");
+  const int64_t total = batch * n_blocks * width;
+  if (total <= 0) return IRIS_OK;
+  add_bias_rows_kernel<<<grid_for(total), THREADS, 0, static_cast<cudaStream_t>(stream)>>>(core, bias, out, batch,
+                                                                                          n_blocks, width);
+  IRIS_CUDA(cudaGetLastError());
+  return IRIS_OK;
+}
+
+extern "C" int iris_cfg_euler(const float* v, const float* x, float* x_out, int64_t images, int64_t per_image,
+                              float cfg_scale, float sigma, float sigma_next, int guided, void* stream) {
+  using namespace iris::small;
+  IRIS_REQUIRE(v && x && x_out, "cfg_euler: null pointer");
+  IRIS_REQUIRE(sigma > 0.f, "cfg_euler: sigma must be positive");
+  const int64_t total = images * per_image;
+  if (total <= 0) return IRIS_OK;
+  cfg_euler_kernel<<<grid_for(total, 4), THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
+      v, x, x_out, images, per_image, cfg_scale, sigma, sigma_next, guided);
+  IRIS_CUDA(cudaGetLastError());
+  return IRIS_OK;
+}
+
+extern "C" int iris_all_finite(const float* x, int64_t n, int* flag, void* stream) {
+  using namespace iris::small;
+  IRIS_REQUIRE(x && flag, "all_finite: null pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  set_int_kernel<<<1, 1, 0, st>>>(flag, 1);
+  if (n > 0) all_finite_kernel<<<grid_for(n, 8), THREADS, 0, st>>>(x, n, flag);
+  IRIS_CUDA(cudaGetLastError());
+  return IRIS_OK;
+}

@@ -1,0 +1,94 @@
+"""ctypes binding of ``libiris_b200.so`` (the C ABI in ``include/iris_b200.h``).
+
+Loading fails loudly: there is no CPU or library fallback behind these
+symbols. ``call`` raises ``ValueError`` for a rejected argument
+(``IRIS_EINVAL``) and ``RuntimeError`` for a CUDA failure.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+LIBRARY = Path(__file__).resolve().parent / "libiris_b200.so"
+
+IRIS_OK, IRIS_EINVAL, IRIS_ECUDA = 0, 1, 2
+F32, BF16, F16 = 0, 1, 2
+EPI_STORE, EPI_SWIGLU, EPI_GATE = 0, 1, 2
+NEXT_NONE, NEXT_NORM_MODULATE, NEXT_SILU_ADD = 0, 1, 2
+
+P, I64, I32, F = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float
+
+# name -> argument types, in the order of include/iris_b200.h
+SIGNATURES: dict[str, list] = {
+    "iris_device_error": [I32, ctypes.POINTER(ctypes.c_uint), P],
+    "iris_rms_norm_modulate": [P, I32, I64, I64, I64, P, I32, P, P, P, I64, I64, I64, I64, F, P],
+    "iris_gated_residual_rms_norm": [
+        P, I64, I64, I64, P, I32, I64, I64, I64, P, P, I64, I64, I64, I64, F, I32, P, P, P, I64, P, I32, I64, I64, I64, P
+    ],
+    "iris_rms_norm_add_rows": [P, P, P, I64, I64, I64, F, P],
+    "iris_qk_norm_rope": [P, I32, I64, I64, I64, I64, I64, P, P, P, F, P, I32, I64, I64, P],
+    "iris_qkv_heads": [P, I64, I64, I64, I64, I64, P, P, P, P, F, P, P, P, I64, I64, P],
+    "iris_gemm_bf16": [P, I64, P, I64, P, I32, I64, I64, I64, I64, I32, P, P, I64, I64, I64, I64, I64, I64, I64, P],
+    "iris_flash_attn_fwd": [P, P, P, P, I64, I64, I64, I64, I64, F, I64, P],
+    "iris_pixel_rms_norm": [P, I32, P, P, I64, F, P],
+    "iris_pixel_mlp": [P, I32, P, P, P, P, P, P, P, P, P, I64, F, P],
+    "iris_pixel_mlp_head": [P, I32, P, P, P, P, P, P, P, P, P, P, P, I64, I64, I64, I64, F, P],
+    "iris_pixel_embed": [P, P, P, P, P, I32, P, P, F, I64, I64, I64, I64, P],
+    "iris_patchify": [P, P, I64, I64, I64, I64, I64, P],
+    "iris_unpatchify": [P, P, I64, I64, I64, I64, I64, P],
+    "iris_timestep_embedding": [P, P, I64, I64, F, P],
+    "iris_gemv": [P, I64, I64, P, I32, P, P, I64, I32, I32, P],
+    "iris_add_bias_rows": [P, P, P, I64, I64, I64, P],
+    "iris_cfg_euler": [P, P, P, I64, I64, F, F, F, I32, P],
+    "iris_all_finite": [P, I64, P, P],
+}
+
+_lib: ctypes.CDLL | None = None
+
+
+def load() -> ctypes.CDLL:
+    """The loaded library; raises if it was not built."""
+    global _lib
+    if _lib is None:
+        if not LIBRARY.exists():
+            raise RuntimeError(
+                f"{LIBRARY.name} is not built; run `python -m iris_b200.build` (needs nvcc) -- "
+                "there is no CPU fallback for the B200 kernels"
+            )
+        lib = ctypes.CDLL(str(LIBRARY))
+        lib.iris_last_error.restype = ctypes.c_char_p
+        lib.iris_last_error.argtypes = []
+        lib.iris_abi_version.restype = ctypes.c_int
+        for name, argtypes in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.argtypes = argtypes
+            fn.restype = ctypes.c_int
+        _lib = lib
+    return _lib
+
+
+_launches = 0
+# kernels each entry point enqueues (1 unless listed)
+_KERNELS_PER_CALL = {"iris_device_error": 0, "iris_all_finite": 2}
+
+
+def launch_count() -> int:
+    """Kernels of this library enqueued so far by this process."""
+    return _launches
+
+
+def call(name: str, *args) -> None:
+    global _launches
+    status = getattr(load(), name)(*args)
+    if status == IRIS_OK:
+        _launches += _KERNELS_PER_CALL.get(name, 1)
+        return
+    message = load().iris_last_error().decode(errors="replace")
+    if status == IRIS_EINVAL:
+        raise ValueError(message)
+    raise RuntimeError(f"{name}: {message}")
+
+
+def exported_symbols() -> list[str]:
+    return ["iris_last_error", "iris_abi_version", *SIGNATURES]

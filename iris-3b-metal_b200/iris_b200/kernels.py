@@ -1,0 +1,328 @@
+"""B200 kernels behind the reference's kernel-level Python API.
+
+Same names, signatures, conventions and errors as
+``src/iris_metal/kernels.py``:
+
+- ``qk_norm_rope`` (``kernels.py:334-397``), ``rms_norm_modulate``
+  (``:413-452``), ``gated_residual_rms_norm_`` (``:455-480``, in place),
+  ``pixel_rms_norm`` (``:486-498``), ``pixel_mlp_`` (``:527-584``, in place);
+- gains, rotary tables and modulation rows must be contiguous FP32 (a BF16
+  gain would be misread silently, ``kernels.py:304-306``); modulation rows may
+  be strided ``[B, 1, D]`` views and are copied only if misaligned
+  (``_per_batch``, ``kernels.py:404-410``);
+- arguments are validated before any launch and rejected with ``ValueError``.
+
+The work runs in ``libiris_b200.so`` on the current CUDA stream; there is no
+CPU path, so CPU tensors are rejected too. Further entry points used by the
+engine (``gemm``, ``flash_attention``, ...) follow the same rules.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from iris_b200 import _lib
+
+HEAD_DIM = 128
+PIXEL_WIDTH, PIXEL_HIDDEN = 16, 64
+
+_DTYPES = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16, torch.float16: _lib.F16}
+
+
+def _require(condition: bool, message: str) -> None:
+    if not condition:
+        raise ValueError(message)
+
+
+def _require_fp32(**tensors: torch.Tensor) -> None:
+    for name, tensor in tensors.items():
+        _require(tensor.dtype == torch.float32 and tensor.is_contiguous(), f"{name} must be contiguous FP32")
+
+
+def _require_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        _require(t.device.type == "cuda", "the B200 kernels need CUDA tensors (there is no CPU path)")
+
+
+def _dtype(t: torch.Tensor | torch.dtype) -> int:
+    dt = t if isinstance(t, torch.dtype) else t.dtype
+    _require(dt in _DTYPES, f"unsupported dtype {dt}")
+    return _DTYPES[dt]
+
+
+def stream_of(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _per_batch(vector: torch.Tensor, batch: int, width: int) -> tuple[torch.Tensor, int]:
+    """``[B, 1, D]`` modulation slice -> FP32 ``[B, D]`` rows, read in place when
+    possible, and the element stride between them (``kernels.py:404-410``)."""
+    rows = vector.reshape(batch, width).float()
+    if rows.stride(1) != 1 or rows.stride(0) % 4 or rows.storage_offset() % 4:
+        rows = rows.clone(memory_format=torch.contiguous_format)  # 16-byte vector loads
+    return rows, rows.stride(0)
+
+
+# ---------------------------------------------------------------- reference API
+def qk_norm_rope(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    cos: torch.Tensor,
+    sin: torch.Tensor,
+    eps: float,
+    heads: int,
+    col_offset: int = 0,
+    out: torch.Tensor | None = None,
+    offset: int = 0,
+    out_dtype: torch.dtype | None = None,
+) -> torch.Tensor:
+    """Fused per-head RMSNorm + RoPE + ``[B, N, H, D] -> [B, H, N, D]`` layout.
+
+    ``x``: contiguous ``[B, N, W]`` projection whose columns
+    ``[col_offset, col_offset + heads*128)`` hold the heads. ``cos``/``sin``: FP32
+    ``[N_out, 64]``. With ``out`` (``[B, heads, N_out, 128]``) rows are written from
+    token ``offset`` on. The result has ``out_dtype`` (default: the input dtype).
+    """
+    _require(heads > 0 and col_offset >= 0 and offset >= 0, "heads must be positive and offsets nonnegative")
+    batch, tokens, width = x.shape
+    _require(
+        col_offset + heads * HEAD_DIM <= width and x.is_contiguous(),
+        "qk_norm_rope needs a contiguous [B, N, W] input holding the heads",
+    )
+    if out is None:
+        _require_cuda(x)
+        out = x.new_empty(batch, heads, tokens, HEAD_DIM, dtype=out_dtype or x.dtype)
+    _require(
+        out.shape[:2] == (batch, heads) and out.shape[3] == HEAD_DIM and out.is_contiguous(),
+        f"qk_norm_rope output must be a contiguous [{batch}, {heads}, N, {HEAD_DIM}] tensor",
+    )
+    _require(
+        cos.shape == sin.shape == (cos.shape[0], HEAD_DIM // 2) and offset + tokens <= min(cos.shape[0], out.shape[2]),
+        "qk_norm_rope rotary tables or output do not cover the written rows",
+    )
+    _require_fp32(weight=weight, cos=cos, sin=sin)
+    _require(weight.numel() == HEAD_DIM, f"qk_norm_rope gain must have {HEAD_DIM} entries")
+    _require_cuda(x, weight, cos, sin, out)
+    _lib.call(
+        "iris_qk_norm_rope", x.data_ptr(), _dtype(x), batch, tokens, width, col_offset, heads, weight.data_ptr(),
+        cos.data_ptr(), sin.data_ptr(), float(eps), out.data_ptr(), _dtype(out), out.shape[2], offset, stream_of(x),
+    )  # fmt: skip
+    return out
+
+
+def rms_norm_modulate(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    shift: torch.Tensor,
+    scale: torch.Tensor,
+    eps: float,
+    out_dtype: torch.dtype,
+) -> torch.Tensor:
+    """``(rms_norm(x) * weight * (1 + scale) + shift).to(out_dtype)`` for ``x``: ``[B, N, D]``
+    and per-sample ``shift``/``scale``: ``[B, 1, D]``."""
+    batch, tokens, width = x.shape
+    _require(width % 128 == 0 and x.is_contiguous(), "rms_norm_modulate needs a contiguous input, width % 128 == 0")
+    _require_fp32(weight=weight)
+    _require(weight.numel() == width, "rms_norm_modulate gain width mismatch")
+    _require(x.dtype in (torch.float32, torch.bfloat16), "rms_norm_modulate reads FP32 or BF16 rows")
+    _require_cuda(x, weight, shift, scale)
+    out = torch.empty(x.shape, device=x.device, dtype=out_dtype)
+    shift, shift_stride = _per_batch(shift, batch, width)
+    scale, scale_stride = _per_batch(scale, batch, width)
+    if shift_stride != scale_stride:  # the kernel takes one stride
+        shift, scale = shift.contiguous(), scale.contiguous()
+        shift_stride = width
+    rows = batch * tokens
+    _lib.call(
+        "iris_rms_norm_modulate", x.data_ptr(), _dtype(x), max(rows, 1), 0, 0, out.data_ptr(), _dtype(out_dtype),
+        weight.data_ptr(), shift.data_ptr(), scale.data_ptr(), shift_stride, rows, max(tokens, 1), width, float(eps),
+        stream_of(x),
+    )  # fmt: skip
+    return out
+
+
+def gated_residual_rms_norm_(
+    residual: torch.Tensor, branch: torch.Tensor, weight: torch.Tensor, gate: torch.Tensor, eps: float
+) -> torch.Tensor:
+    """``residual += gate * rms_norm(branch) * weight`` in place; ``residual``: FP32 ``[B, N, D]``."""
+    batch, tokens, width = residual.shape
+    _require(width % 128 == 0 and branch.shape == residual.shape, "gated_residual_rms_norm_ shape mismatch")
+    _require(branch.is_contiguous(), "gated_residual_rms_norm_ needs a contiguous branch")
+    _require_fp32(residual=residual, weight=weight)
+    _require(weight.numel() == width, "gated_residual_rms_norm_ gain width mismatch")
+    _require_cuda(residual, branch, weight, gate)
+    gate, gate_stride = _per_batch(gate, batch, width)
+    rows = batch * tokens
+    _lib.call(
+        "iris_gated_residual_rms_norm", residual.data_ptr(), max(rows, 1), 0, 0, branch.data_ptr(), _dtype(branch),
+        max(rows, 1), 0, 0, weight.data_ptr(), gate.data_ptr(), gate_stride, rows, max(tokens, 1), width, float(eps),
+        _lib.NEXT_NONE, None, None, None, 0, None, _lib.BF16, 1, 0, 0, stream_of(residual),
+    )  # fmt: skip
+    return residual
+
+
+def pixel_rms_norm(pixels: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    """``rms_norm(pixels) * weight`` over the 16 channels of each pixel (BF16 out)."""
+    _require(pixels.shape[-1] == PIXEL_WIDTH and pixels.is_contiguous(), "pixel_rms_norm needs 16-wide pixels")
+    _require(pixels.dtype in (torch.bfloat16, torch.float32), "pixel_rms_norm reads BF16 or FP32 pixels")
+    _require_fp32(weight=weight)
+    _require(weight.numel() == PIXEL_WIDTH, "pixel_rms_norm gain width mismatch")
+    _require_cuda(pixels, weight)
+    out = torch.empty(pixels.shape, device=pixels.device, dtype=torch.bfloat16)
+    n_pixels = pixels.numel() // PIXEL_WIDTH
+    _lib.call(
+        "iris_pixel_rms_norm", pixels.data_ptr(), _dtype(pixels), out.data_ptr(), weight.data_ptr(), n_pixels,
+        float(eps), stream_of(pixels),
+    )  # fmt: skip
+    return out
+
+
+def _mlp_params(fc1, fc2) -> tuple[torch.Tensor, ...]:
+    _require(
+        fc1.weight.shape == (PIXEL_HIDDEN, PIXEL_WIDTH)
+        and fc2.weight.shape == (PIXEL_WIDTH, PIXEL_HIDDEN)
+        and fc1.bias is not None
+        and fc1.bias.shape == (PIXEL_HIDDEN,)
+        and fc2.bias is not None
+        and fc2.bias.shape == (PIXEL_WIDTH,),
+        "pixel_mlp_ needs the released pixel-stage widths",
+    )
+    params = (fc1.weight, fc1.bias, fc2.weight, fc2.bias)
+    _require(
+        all(t.dtype == torch.bfloat16 and t.is_contiguous() for t in params),
+        "pixel_mlp_ needs contiguous BF16 activations and MLP parameters",
+    )
+    return params
+
+
+def pixel_mlp_(
+    pixels: torch.Tensor,
+    branch: torch.Tensor,
+    mods: torch.Tensor,
+    norm_weight: torch.Tensor,
+    fc1,
+    fc2,
+    next_norm_weight: torch.Tensor,
+    eps: float,
+) -> torch.Tensor:
+    """Finish a post-modulated PiT block in place; return the next block's normed input.
+
+    ``pixels``/``branch``: BF16 ``[..., 16]`` (stream, attention branch); ``mods``:
+    BF16 ``[..., 64]`` per pixel (scale1, shift1, scale2, shift2). An FP32 ``pixels``
+    stream is also accepted and kept unrounded.
+    """
+    _require(
+        pixels.shape[-1] == PIXEL_WIDTH
+        and branch.shape == pixels.shape
+        and mods.shape == (*pixels.shape[:-1], 4 * PIXEL_WIDTH),
+        "pixel_mlp_ needs the released pixel-stage widths",
+    )
+    w1, b1, w2, b2 = _mlp_params(fc1, fc2)
+    _require(
+        pixels.dtype in (torch.bfloat16, torch.float32)
+        and all(t.dtype == torch.bfloat16 and t.is_contiguous() for t in (branch, mods))
+        and pixels.is_contiguous(),
+        "pixel_mlp_ needs contiguous BF16 activations and MLP parameters",
+    )
+    _require_fp32(norm_weight=norm_weight, next_norm_weight=next_norm_weight)
+    _require(norm_weight.numel() == next_norm_weight.numel() == PIXEL_WIDTH, "pixel_mlp_ gain width mismatch")
+    _require_cuda(pixels, branch, mods, norm_weight, next_norm_weight, w1)
+    next_input = torch.empty(pixels.shape, device=pixels.device, dtype=torch.bfloat16)
+    n_pixels = pixels.numel() // PIXEL_WIDTH
+    _lib.call(
+        "iris_pixel_mlp", pixels.data_ptr(), _dtype(pixels), branch.data_ptr(), mods.data_ptr(), norm_weight.data_ptr(),
+        w1.data_ptr(), b1.data_ptr(), w2.data_ptr(), b2.data_ptr(), next_norm_weight.data_ptr(), next_input.data_ptr(),
+        n_pixels, float(eps), stream_of(pixels),
+    )  # fmt: skip
+    return next_input
+
+
+# ----------------------------------------------------------- engine entry points
+def gemm(
+    a: torch.Tensor,
+    w: torch.Tensor,
+    out: torch.Tensor,
+    *,
+    bias: torch.Tensor | None = None,
+    epilogue: int = _lib.EPI_STORE,
+    aux: torch.Tensor | None = None,
+    out_rows: tuple[int, int, int] | None = None,
+    aux_rows: tuple[int, int, int] | None = None,
+) -> torch.Tensor:
+    """``out = epilogue(a @ w.T)`` on the tensor cores; ``a``: bf16 ``[M, K]``
+    (row stride may exceed K), ``w``: bf16 ``[N, K]``; ``out`` rows through the
+    row map ``(seg_rows, seg_stride, seg_offset)`` (identity by default)."""
+    _require(a.dim() == 2 and w.dim() == 2 and a.dtype == w.dtype == torch.bfloat16, "gemm needs bf16 [M, K] x [N, K]")
+    _require(a.stride(1) == 1 and w.stride(1) == 1 and out.stride(-1) == 1, "gemm operands must be row-major")
+    M, K = a.shape
+    N = w.shape[0]
+    _require(w.shape[1] == K, "gemm: inner dimensions differ")
+    ldc = out.stride(-2) if out.dim() >= 2 else N
+    out_rows = out_rows or (M, 0, 0)
+    aux_rows = aux_rows or (M, 0, 0)
+    if bias is not None:
+        _require_fp32(bias=bias)
+        _require(bias.numel() == N, "gemm: bias width")
+    _require_cuda(a, w, out)
+    timing = _gemm_profile is not None
+    if timing:
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+    _lib.call(
+        "iris_gemm_bf16", a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), out.data_ptr(), _dtype(out), ldc,
+        M, N, K, epilogue, _ptr(bias), _ptr(aux), aux.stride(-2) if aux is not None else 0, *out_rows, *aux_rows,
+        stream_of(a),
+    )  # fmt: skip
+    if timing:
+        end.record()
+        _gemm_profile.append((start, end, 2.0 * M * N * K))
+    return out
+
+
+_gemm_profile: list | None = None
+
+
+def profile_gemms(enable: bool):
+    """Start (``True``) or stop (``False``) timing every GEMM launch with CUDA
+    events on its stream. Stopping synchronises and returns
+    ``(algorithmic FLOPs, milliseconds, launches)`` summed over the launches."""
+    global _gemm_profile
+    if enable:
+        _gemm_profile = []
+        return None
+    records, _gemm_profile = _gemm_profile or [], None
+    torch.cuda.synchronize()
+    flops = sum(r[2] for r in records)
+    ms = sum(r[0].elapsed_time(r[1]) for r in records)
+    return flops, ms, len(records)
+
+
+def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor, scale: float | None = None):
+    """``softmax(q k^T * scale) v`` for ``q``: ``[B, H, N, 128]``, ``k``/``v``:
+    ``[B, H_kv, N, 128]`` (bf16, contiguous); ``out``: ``[B, N, >= H*128]`` bf16."""
+    _require(q.dim() == 4 and k.shape == v.shape and q.shape[0] == k.shape[0] and q.shape[2:] == k.shape[2:],
+             "flash_attention: q [B, H, N, D], k/v [B, H_kv, N, D]")  # fmt: skip
+    _require(all(t.dtype == torch.bfloat16 and t.is_contiguous() for t in (q, k, v)), "flash_attention: contiguous bf16")
+    batch, heads, n, d = q.shape
+    _require(out.dtype == torch.bfloat16 and out.stride(-1) == 1 and out.shape[-2] == n, "flash_attention: out layout")
+    _require(out.dim() == 3 and out.stride(0) == n * out.stride(1), "flash_attention: out rows must be [B*N, stride]")
+    _require_cuda(q, k, v, out)
+    _lib.call(
+        "iris_flash_attn_fwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), batch, heads, k.shape[1], n, d,
+        float(scale if scale is not None else d**-0.5), out.stride(1), stream_of(q),
+    )  # fmt: skip
+    return out
+
+
+def device_error(clear: bool = True, device: torch.device | None = None) -> int:
+    """The device error word (bit 0: a bounded wait timed out); synchronises the stream."""
+    import ctypes
+
+    value = ctypes.c_uint(0)
+    stream = torch.cuda.current_stream(device).cuda_stream
+    _lib.call("iris_device_error", int(clear), ctypes.byref(value), stream)
+    return int(value.value)

@@ -1,0 +1,576 @@
+"""``CudaIris``: the per-step Iris-3B denoiser forward on B200 kernels.
+
+Drop-in for ``MetalIris`` (``src/iris_metal/model.py:113-345``): same
+constructor (a loaded model exposing ``.cfg`` and ``.state_dict()`` -- the
+upstream ``IrisDiT`` or :class:`iris_b200.weights.IrisWeights`), same
+``encode_text`` and ``__call__(x, t, text) -> v`` contract. ``text`` is never
+written, the host is never synchronised, outputs are allocated fresh and the
+residual streams are internal workspace. Every launch goes to
+``libiris_b200.so``.
+
+Per step (``dit.py:283-375`` restructured):
+
+* conditioning: timestep features -> MLP -> silu -> both shared adaLN cores,
+  once per step; per-block modulation rows = core + block bias in one launch;
+* residual stream: one FP32 ``[B, T + L, D]`` buffer, text rows first. The
+  dual-stream blocks address its text and image rows through row maps, so the
+  single-stream tail needs no concatenation;
+* every branch input is written by the kernel that finishes the previous
+  residual update (gated post-norm + residual + next RMSNorm-modulate fused);
+* GEMMs on the tensor cores with fused epilogues (bias, SwiGLU, sigmoid gate),
+  attention by the tcgen05 flash kernel; Q/K/V written by one fused
+  norm + RoPE + head-transpose kernel;
+* pixel stage: per-pixel adaLN GEMM, compress / attention / expand on the
+  tensor cores, the post-modulated per-pixel MLP fused, and the last block
+  fused with the FinalLayer and the fold into the velocity image.
+
+Precision plan: BF16 GEMM operands and attention, FP32 accumulation, FP32
+residual streams, norms, modulation and conditioning, FP32 pixel stream
+(the reference keeps BF16 there; FP32 is closer to the fp32 model).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from iris_b200 import _lib
+from iris_b200 import kernels as K
+from iris_b200.config import ModelConfig, from_any
+from iris_b200.tables import cos_sin, rope_1d, rope_2d, sincos_pos_embed_2d
+
+HEAD_DIM = 128
+SWIGLU_TILE = 128  # w1/w3 rows per SwiGLU GEMM tile half
+
+
+def check_supported(cfg: ModelConfig, state: dict) -> None:
+    """Reject topologies the fused forward does not handle (``model.py:68-99``)."""
+    requirements = {
+        "a pixel stage with post-modulated blocks of 16 channels": cfg.pixel.enabled
+        and cfg.pixel.modulation == "post"
+        and cfg.pixel.hidden_size == 16
+        and cfg.pixel.mlp_ratio == 4.0,
+        "shared_bias modulation": cfg.modulation == "shared_bias",
+        "a single-stream tail after the dual-stream prefix": cfg.block == "single_stream" and cfg.depth > cfg.dual_depth,
+        "gated, sandwich-normed, QK-normed attention without QKV bias": cfg.gated_attention
+        and cfg.sandwich_norm
+        and cfg.qk_norm
+        and not cfg.qkv_bias,
+        f"{HEAD_DIM}-wide attention heads": cfg.hidden_size // cfg.num_heads == HEAD_DIM
+        and cfg.pixel.attn_hidden_size // cfg.pixel.num_heads == HEAD_DIM
+        and cfg.num_heads % cfg.kv_heads == 0,
+        "text RoPE without frame pairs": cfg.text_rope and cfg.rope_frame_pairs == 0,
+        "text output kept in the final block": cfg.final_block_text == "keep",
+        "a hidden size that is a multiple of 128": cfg.hidden_size % 128 == 0,
+    }
+    missing = [name for name, ok in requirements.items() if not ok]
+    if missing:
+        raise ValueError(f"CudaIris supports the released Iris-3B topology family; this model lacks {missing}")
+    for key in ("s_embedder.proj.weight", "t_embedder.mlp.0.weight", "final_layer.linear.weight"):
+        if key not in state:
+            raise ValueError(f"CudaIris: missing parameter {key}")
+
+
+def pack_swiglu(w1: torch.Tensor, w3: torch.Tensor, w2: torch.Tensor, tile: int = SWIGLU_TILE):
+    """SwiGLU weights (``src/iris3b/nn/mlp.py:24-40``) in the layout of the GEMM's
+    SwiGLU epilogue: each 256-row tile of ``w13`` holds ``tile`` rows of ``w1``
+    followed by the same rows of ``w3``; the hidden width is zero-padded to a
+    multiple of ``tile`` (``silu(0) * 0 = 0`` and the padded ``w2`` columns are 0)."""
+    ffn, d = w1.shape
+    pad = -(-ffn // tile) * tile
+    tiles = pad // tile
+    w1p = torch.zeros(pad, d, device=w1.device, dtype=w1.dtype)
+    w3p = torch.zeros(pad, d, device=w3.device, dtype=w3.dtype)
+    w1p[:ffn], w3p[:ffn] = w1, w3
+    w13 = torch.stack([w1p.view(tiles, tile, d), w3p.view(tiles, tile, d)], dim=1)  # [tiles, 2, tile, d]
+    w2p = torch.zeros(w2.shape[0], pad, device=w2.device, dtype=w2.dtype)
+    w2p[:, :ffn] = w2
+    return w13.reshape(2 * pad, d).contiguous(), w2p
+
+
+def require_finite(result: torch.Tensor) -> torch.Tensor:
+    """Raise rather than let an overflowed result become a black image
+    (``src/iris_metal/model.py:102-110``); one device flag, one sync."""
+    flag = torch.empty(1, device=result.device, dtype=torch.int32)
+    data = result.float().contiguous()
+    _lib.call("iris_all_finite", data.data_ptr(), data.numel(), flag.data_ptr(), K.stream_of(data))
+    if int(flag.item()) != 1:
+        raise FloatingPointError("the model produced non-finite values; please report the input and settings")
+    return result
+
+
+@dataclass
+class _Block:
+    dual: bool
+    norms: dict
+    qkv: dict  # stream -> bf16 [(H + 2 Hkv) 128, D]
+    qk_norm: dict  # stream -> (q gain, k gain)
+    gate: dict
+    proj: dict  # stream -> (weight, bias)
+    w13: dict
+    w2: dict
+    mod_index: dict  # stream -> row in the stacked modulation table
+
+
+class CudaIris:
+    """Velocity predictor ``(x, t, text) -> v`` for a loaded Iris model."""
+
+    def __init__(self, dit, attention_dtype: torch.dtype | None = None, pixel_dtype: torch.dtype = torch.float32):
+        cfg = from_any(dit.cfg)
+        state = dit.state_dict()
+        check_supported(cfg, state)
+        if attention_dtype not in (None, torch.bfloat16):
+            raise ValueError("CudaIris computes attention in BF16")
+        if pixel_dtype not in (torch.float32, torch.bfloat16):
+            raise ValueError("pixel_dtype must be torch.float32 or torch.bfloat16")
+        self.dit = dit
+        self.cfg = cfg
+        self.device = state["s_embedder.proj.weight"].device
+        if self.device.type != "cuda":
+            raise ValueError("CudaIris needs the model's weights on a CUDA device")
+        self.dtype = torch.bfloat16
+        self.attention_dtype = torch.bfloat16
+        self.pixel_dtype = pixel_dtype
+        self.text_dtype = torch.bfloat16
+        self._pack(state)
+        self._tables: dict = {}
+        self._work: dict = {}
+
+    # -- weight repacking (once) --------------------------------------------------
+    def _pack(self, state: dict) -> None:
+        cfg, dev = self.cfg, self.device
+        d = cfg.hidden_size
+        ffn = cfg.swiglu_hidden
+        self.ffn_pad = -(-ffn // SWIGLU_TILE) * SWIGLU_TILE
+
+        def bf(name):
+            return state[name].detach().to(dev, torch.bfloat16).contiguous()
+
+        def f32(name):
+            return state[name].detach().to(dev, torch.float32).contiguous()
+
+        def pad_k(w: torch.Tensor) -> torch.Tensor:
+            k = w.shape[1]
+            kp = -(-k // 8) * 8
+            if kp == k:
+                return w.contiguous()
+            out = torch.zeros(w.shape[0], kp, device=dev, dtype=w.dtype)
+            out[:, :k] = w
+            return out
+
+        def qkv(prefix, suffix):
+            fused = f"{prefix}.qkv{suffix}.weight"
+            if fused in state:
+                return bf(fused)
+            parts = [bf(f"{prefix}.{n}_proj{suffix}.weight") for n in ("q", "k", "v")]
+            return torch.cat(parts).contiguous()
+
+        def swiglu(prefix):
+            return pack_swiglu(bf(f"{prefix}.w1.weight"), bf(f"{prefix}.w3.weight"), bf(f"{prefix}.w2.weight"))
+
+        if (cfg.in_channels * cfg.patch_size**2) % 8:
+            raise ValueError("CudaIris needs in_channels * patch_size^2 to be a multiple of 8")
+        self.s_embed = (bf("s_embedder.proj.weight"), f32("s_embedder.proj.bias"))
+        self.t_mlp = [(f32(f"t_embedder.mlp.{i}.weight"), f32(f"t_embedder.mlp.{i}.bias")) for i in (0, 2)]
+        self.cores = {s: (f32(f"modulation_cores.adaln_{s}.weight"), f32(f"modulation_cores.adaln_{s}.bias"))
+                      for s in ("img", "txt")}  # fmt: skip
+        self.blocks: list[_Block] = []
+        img_bias, txt_bias = [], []
+        for i in range(cfg.depth):
+            b = f"blocks.{i}"
+            if i < cfg.dual_depth:
+                streams = {"x": "img", "y": "txt"}
+                norms = {
+                    s: {
+                        "norm1": f32(f"{b}.norm_{s}1.weight"),
+                        "norm2": f32(f"{b}.norm_{s}2.weight"),
+                        "post_attn": f32(f"{b}.attn_post_norm_{s}.weight"),
+                        "post_mlp": f32(f"{b}.mlp_post_norm_{s}.weight"),
+                    }
+                    for s in streams
+                }
+                w13, w2 = {}, {}
+                for s in streams:
+                    w13[s], w2[s] = swiglu(f"{b}.mlp_{s}")
+                mod_index = {"x": len(img_bias), "y": len(txt_bias)}
+                img_bias.append(f32(f"{b}.adaln_img.bias"))
+                txt_bias.append(f32(f"{b}.adaln_txt.bias"))
+                self.blocks.append(
+                    _Block(
+                        dual=True,
+                        norms=norms,
+                        qkv={s: qkv(f"{b}.attn", f"_{s}") for s in streams},
+                        qk_norm={s: (f32(f"{b}.attn.q_norm_{s}.weight"), f32(f"{b}.attn.k_norm_{s}.weight"))
+                                 for s in streams},  # fmt: skip
+                        gate={s: bf(f"{b}.attn_gate_{s}.weight") for s in streams},
+                        proj={s: (bf(f"{b}.attn.proj_{s}.weight"), f32(f"{b}.attn.proj_{s}.bias")) for s in streams},
+                        w13=w13,
+                        w2=w2,
+                        mod_index=mod_index,
+                    )
+                )
+            else:
+                w13, w2 = swiglu(f"{b}.mlp")
+                mod_index = {"j": len(img_bias)}
+                img_bias.append(f32(f"{b}.adaln.bias"))
+                self.blocks.append(
+                    _Block(
+                        dual=False,
+                        norms={"j": {
+                            "norm1": f32(f"{b}.norm1.weight"),
+                            "norm2": f32(f"{b}.norm2.weight"),
+                            "post_attn": f32(f"{b}.attn_post_norm.weight"),
+                            "post_mlp": f32(f"{b}.mlp_post_norm.weight"),
+                        }},  # fmt: skip
+                        qkv={"j": qkv(b, "")},
+                        qk_norm={"j": (f32(f"{b}.q_norm.weight"), f32(f"{b}.k_norm.weight"))},
+                        gate={"j": bf(f"{b}.attn_gate.weight")},
+                        proj={"j": (bf(f"{b}.attn_proj.weight"), f32(f"{b}.attn_proj.bias"))},
+                        w13={"j": w13},
+                        w2={"j": w2},
+                        mod_index=mod_index,
+                    )
+                )
+        self.img_bias = torch.stack(img_bias).contiguous()
+        self.txt_bias = torch.stack(txt_bias).contiguous() if txt_bias else None
+        pix = cfg.pixel
+        self.pixel_embed_w = (f32("pixel_embedder.proj.weight"), f32("pixel_embedder.proj.bias"))
+        self.pixel_blocks = []
+        for i in range(pix.depth):
+            b = f"pixel_blocks.{i}"
+            self.pixel_blocks.append(
+                {
+                    "norm1": f32(f"{b}.norm1.weight"),
+                    "norm2": f32(f"{b}.norm2.weight"),
+                    "adaln": (bf(f"{b}.adaln.weight"), f32(f"{b}.adaln.bias")),
+                    "compress": (pad_k(bf(f"{b}.compress.weight")), f32(f"{b}.compress.bias")),
+                    "qkv": bf(f"{b}.attn.qkv.weight"),
+                    "qk_norm": (f32(f"{b}.attn.q_norm.weight"), f32(f"{b}.attn.k_norm.weight")),
+                    "proj": (bf(f"{b}.attn.proj.weight"), f32(f"{b}.attn.proj.bias")),
+                    "expand": (bf(f"{b}.expand.weight"), f32(f"{b}.expand.bias")),
+                    "fc1": (bf(f"{b}.mlp.fc1.weight"), bf(f"{b}.mlp.fc1.bias")),
+                    "fc2": (bf(f"{b}.mlp.fc2.weight"), bf(f"{b}.mlp.fc2.bias")),
+                }
+            )
+        self.final = (f32("final_layer.norm.weight"), f32("final_layer.linear.weight"), f32("final_layer.linear.bias"))
+        self.text_adapter = None
+        if cfg.text_adapter == "linear" and "y_embedder.proj.weight" in state:
+            self.text_adapter = (
+                pad_k(bf("y_embedder.proj.weight")),
+                f32("y_embedder.proj.bias"),
+                f32("y_embedder.norm.weight"),
+                f32("y_pos_embedding").reshape(-1, d) if "y_pos_embedding" in state else None,
+            )
+
+    # -- conditioning ---------------------------------------------------------------
+    @torch.no_grad()
+    def encode_text(self, states: torch.Tensor, mask: torch.Tensor | None = None) -> torch.Tensor:
+        """Encoder states ``[B, T, text_dim]`` -> trunk text tokens ``[B, T, D]`` (FP32):
+        ``TextEmbedder`` (Linear + RMSNorm) + ``y_pos_embedding`` (``dit.py:263-281``).
+        The masked transformer adapters run once per prompt outside this engine."""
+        if self.text_adapter is None:
+            raise NotImplementedError("CudaIris.encode_text implements the linear text adapter")
+        w, b, norm_w, pos = self.text_adapter
+        cfg = self.cfg
+        states = states[:, : cfg.text_len].to(self.device)
+        batch, n, dim = states.shape
+        a = torch.zeros(batch * n, w.shape[1], device=self.device, dtype=torch.bfloat16)
+        a[:, :dim] = states.reshape(batch * n, dim)
+        out = torch.empty(batch, n, cfg.hidden_size, device=self.device, dtype=torch.float32)
+        K.gemm(a, w, out.view(batch * n, -1), bias=b)
+        add = pos[:n].contiguous() if pos is not None else torch.zeros(n, cfg.hidden_size, device=self.device)
+        _lib.call("iris_rms_norm_add_rows", out.data_ptr(), norm_w.data_ptr(), add.data_ptr(), batch * n, n,
+                  cfg.hidden_size, float(cfg.norm_eps), K.stream_of(out))  # fmt: skip
+        return out
+
+    def _rope(self, grid: tuple[int, int], n_text: int):
+        key = (grid, n_text)
+        if key not in self._tables:
+            cfg = self.cfg
+            image = rope_2d(HEAD_DIM, *grid, cfg.rope_theta, cfg.rope_scale, cfg.rope_aspect)
+            text = rope_1d(HEAD_DIM, n_text, cfg.text_rope_theta)
+            trunk = cos_sin(text, image, device=self.device)
+            pixel = cos_sin(image, device=self.device)  # pixel heads are 128 wide too
+            pos = None
+            if cfg.pixel.abs_pos_embed:
+                p = cfg.patch_size
+                pos = sincos_pos_embed_2d(cfg.pixel.hidden_size, grid[0] * p, grid[1] * p).to(self.device)
+            if len(self._tables) >= 4:
+                self._tables.pop(next(iter(self._tables)))
+            self._tables[key] = (trunk, pixel, pos)
+        return self._tables[key]
+
+    def _workspace(self, batch: int, grid: tuple[int, int], n_text: int) -> dict:
+        key = (batch, grid, n_text)
+        if key in self._work:
+            return self._work[key]
+        self._work.clear()
+        cfg, dev = self.cfg, self.device
+        d, p = cfg.hidden_size, cfg.patch_size
+        L = grid[0] * grid[1]
+        N = n_text + L
+        hq, hkv = cfg.num_heads, cfg.kv_heads
+        pix = cfg.pixel
+        pp = p * p
+        bf16 = torch.bfloat16
+        wq = (hq + 2 * hkv) * HEAD_DIM
+        e = lambda *shape, dtype=bf16: torch.empty(*shape, device=dev, dtype=dtype)  # noqa: E731
+        ws = {
+            "tokens": e(batch * N, d, dtype=torch.float32),
+            "patches": e(batch * L, self.s_embed[0].shape[1]),
+            "h": e(batch * N, d),
+            "h2": e(batch * N, d),
+            "qkv": e(batch * N, wq),
+            "q": e(batch, hq, N, HEAD_DIM),
+            "k": e(batch, hkv, N, HEAD_DIM),
+            "v": e(batch, hkv, N, HEAD_DIM),
+            "o": e(batch * N, d),
+            "g": e(batch * N, d),
+            "branch": e(batch * N, d),
+            "act": e(batch * N, self.ffn_pad),
+            "s_cond": e(batch * L, d),
+            "pixels": e(batch * L * pp, pix.hidden_size, dtype=self.pixel_dtype),
+            "ph": e(batch * L, pp * pix.hidden_size),
+            "pmods": e(batch * L, pp * 4 * pix.hidden_size),
+            "comp": e(batch * L, pix.attn_hidden_size),
+            "pqkv": e(batch * L, 3 * pix.attn_hidden_size),
+            "pq": e(batch, pix.num_heads, L, HEAD_DIM),
+            "pk": e(batch, pix.num_heads, L, HEAD_DIM),
+            "pv": e(batch, pix.num_heads, L, HEAD_DIM),
+            "po": e(batch * L, pix.attn_hidden_size),
+            "pproj": e(batch * L, pix.attn_hidden_size),
+            "pbranch": e(batch * L, pp * pix.hidden_size),
+            "t_freq": e(batch, 256, dtype=torch.float32),
+            "t_h": e(batch, d, dtype=torch.float32),
+            "t_emb": e(batch, d, dtype=torch.float32),
+            "core_img": e(batch, 6 * d, dtype=torch.float32),
+            "core_txt": e(batch, 6 * d, dtype=torch.float32),
+            "mods_img": e(self.img_bias.shape[0], batch, 6 * d, dtype=torch.float32),
+            "mods_txt": e(max(1, 0 if self.txt_bias is None else self.txt_bias.shape[0]), batch, 6 * d,
+                          dtype=torch.float32),  # fmt: skip
+        }
+        self._work[key] = ws
+        return ws
+
+    # -- forward ----------------------------------------------------------------------
+    @torch.no_grad()
+    def __call__(self, x: torch.Tensor, t: torch.Tensor, text: torch.Tensor) -> torch.Tensor:
+        """``x``: ``[B, 3, H, W]``; ``t``: model time ``[B]``; ``text``: ``[B, T, D]``
+        from :meth:`encode_text`. Returns the FP32 velocity ``[B, 3, H, W]``."""
+        cfg = self.cfg
+        p = cfg.patch_size
+        batch, channels, height, width = x.shape
+        if height % p or width % p:
+            raise ValueError(f"input {height}x{width} is not divisible by patch_size {p}")
+        if channels != cfg.in_channels:
+            raise ValueError(f"expected {cfg.in_channels} input channels, got {channels}")
+        if text.shape[0] != batch or text.shape[2] != cfg.hidden_size:
+            raise ValueError("text must be [B, T, hidden_size] for the same batch as x")
+        grid = (height // p, width // p)
+        L, T = grid[0] * grid[1], text.shape[1]
+        N = T + L
+        d = cfg.hidden_size
+        dev = self.device
+        x = x.to(dev, torch.float32).contiguous()
+        t = t.to(dev, torch.float32).reshape(batch).contiguous()
+        ws = self._workspace(batch, grid, T)
+        (cos, sin), (pcos, psin), pos = self._rope(grid, T)
+        st = torch.cuda.current_stream(dev).cuda_stream
+        eps = float(cfg.norm_eps)
+        tokens = ws["tokens"]
+
+        # conditioning: t -> t_emb -> silu -> shared cores -> per-block rows
+        _lib.call("iris_timestep_embedding", t.data_ptr(), ws["t_freq"].data_ptr(), batch, 256,
+                  float(cfg.timestep_max_period), st)  # fmt: skip
+        (w0, b0), (w2, b2) = self.t_mlp
+        _lib.call("iris_gemv", ws["t_freq"].data_ptr(), batch, 256, w0.data_ptr(), _lib.F32, b0.data_ptr(),
+                  ws["t_h"].data_ptr(), d, 0, 1, st)  # fmt: skip
+        _lib.call("iris_gemv", ws["t_h"].data_ptr(), batch, d, w2.data_ptr(), _lib.F32, b2.data_ptr(),
+                  ws["t_emb"].data_ptr(), d, 0, 0, st)  # fmt: skip
+        for name, bias_table in (("img", self.img_bias), ("txt", self.txt_bias)):
+            if bias_table is None:
+                continue
+            w, b = self.cores[name]
+            core = ws[f"core_{name}"]
+            _lib.call("iris_gemv", ws["t_emb"].data_ptr(), batch, d, w.data_ptr(), _lib.F32, b.data_ptr(),
+                      core.data_ptr(), 6 * d, 1, 0, st)  # fmt: skip
+            _lib.call("iris_add_bias_rows", core.data_ptr(), bias_table.data_ptr(), ws[f"mods_{name}"].data_ptr(),
+                      batch, bias_table.shape[0], 6 * d, st)  # fmt: skip
+
+        # residual stream: [text | image] rows per sample
+        tokens.view(batch, N, d)[:, :T].copy_(text.to(dev, torch.float32))
+        _lib.call("iris_patchify", x.data_ptr(), ws["patches"].data_ptr(), batch, channels, height, width, p, st)
+        K.gemm(ws["patches"], self.s_embed[0], tokens, bias=self.s_embed[1], out_rows=(L, N, T))
+
+        geom = _Geometry(batch=batch, T=T, L=L, N=N, d=d)
+        self._first_norm(self.blocks[0], ws, geom, eps, st)
+        for i, block in enumerate(self.blocks):
+            nxt = self.blocks[i + 1] if i + 1 < len(self.blocks) else None
+            if block.dual:
+                self._dual_block(block, nxt, ws, geom, cos, sin, eps, st)
+            else:
+                self._single_block(block, nxt, ws, geom, cos, sin, eps, st)
+
+        # pixel stage
+        v = torch.empty(batch, channels, height, width, device=dev, dtype=torch.float32)
+        self._pixel_stage(x, ws, geom, grid, pcos, psin, pos, v, eps, st)
+        return v
+
+    # -- trunk --------------------------------------------------------------------------
+    def _mods(self, ws, block: _Block, stream: str) -> torch.Tensor:
+        """``[B, 6D]`` modulation rows of a block's stream (shift1, scale1, gate1, shift2, scale2, gate2)."""
+        if stream == "y":
+            return ws["mods_txt"][block.mod_index["y"]]
+        return ws["mods_img"][block.mod_index["x" if stream == "x" else "j"]]
+
+    @staticmethod
+    def _chunk(mods: torch.Tensor, k: int, d: int) -> int:
+        return mods.data_ptr() + k * d * 4
+
+    def _segments(self, block: _Block, g: "_Geometry"):
+        """(stream, rows, rows per batch, token map, dense offset) for a block."""
+        if block.dual:
+            return [("y", g.batch * g.T, g.T, (g.T, g.N, 0), 0), ("x", g.batch * g.L, g.L, (g.L, g.N, g.T), g.batch * g.T)]
+        rows = g.batch * g.N
+        return [("j", rows, g.N, (rows, 0, 0), 0)]
+
+    def _first_norm(self, block: _Block, ws, g, eps, st) -> None:
+        for stream, rows, rpb, tmap, off in self._segments(block, g):
+            mods = self._mods(ws, block, stream)
+            _lib.call(
+                "iris_rms_norm_modulate", ws["tokens"].data_ptr(), _lib.F32, *tmap, ws["h"][off:].data_ptr(), _lib.BF16,
+                block.norms[stream]["norm1"].data_ptr(), self._chunk(mods, 0, g.d), self._chunk(mods, 1, g.d), 6 * g.d,
+                rows, rpb, g.d, eps, st,
+            )  # fmt: skip
+
+    def _dual_block(self, block, nxt, ws, g, cos, sin, eps, st) -> None:
+        cfg = self.cfg
+        hq, hkv = cfg.num_heads, cfg.kv_heads
+        segs = self._segments(block, g)
+        wq = block.qkv["x"].shape[0]
+        for stream, rows, rpb, tmap, off in segs:
+            K.gemm(ws["h"][off : off + rows], block.qkv[stream], ws["qkv"][off : off + rows])
+            qn, kn = block.qk_norm[stream]
+            _lib.call(
+                "iris_qkv_heads", ws["qkv"][off:].data_ptr(), g.batch, rpb, wq, hq, hkv, qn.data_ptr(), kn.data_ptr(),
+                cos.data_ptr(), sin.data_ptr(), eps, ws["q"].data_ptr(), ws["k"].data_ptr(), ws["v"].data_ptr(), g.N,
+                tmap[2], st,
+            )  # fmt: skip
+        K.flash_attention(ws["q"], ws["k"], ws["v"], ws["o"].view(g.batch, g.N, g.d))
+        for stream, rows, rpb, tmap, off in segs:
+            self._branch_tail(block, nxt, stream, rows, rpb, tmap, off, ws, g, eps, st)
+
+    def _single_block(self, block, nxt, ws, g, cos, sin, eps, st) -> None:
+        cfg = self.cfg
+        rows = g.batch * g.N
+        K.gemm(ws["h"], block.qkv["j"], ws["qkv"])
+        qn, kn = block.qk_norm["j"]
+        _lib.call(
+            "iris_qkv_heads", ws["qkv"].data_ptr(), g.batch, g.N, block.qkv["j"].shape[0], cfg.num_heads, cfg.kv_heads,
+            qn.data_ptr(), kn.data_ptr(), cos.data_ptr(), sin.data_ptr(), eps, ws["q"].data_ptr(), ws["k"].data_ptr(),
+            ws["v"].data_ptr(), g.N, 0, st,
+        )  # fmt: skip
+        K.flash_attention(ws["q"], ws["k"], ws["v"], ws["o"].view(g.batch, g.N, g.d))
+        self._branch_tail(block, nxt, "j", rows, g.N, (rows, 0, 0), 0, ws, g, eps, st)
+
+    def _branch_tail(self, block, nxt, stream, rows, rpb, tmap, off, ws, g, eps, st) -> None:
+        """gate -> out proj -> post-norm residual (+ norm2) -> SwiGLU -> post-norm residual (+ next input)."""
+        d = g.d
+        mods = self._mods(ws, block, stream)
+        norms = block.norms[stream]
+        h, h2 = ws["h"][off : off + rows], ws["h2"][off : off + rows]
+        gbuf, branch = ws["g"][off : off + rows], ws["branch"][off : off + rows]
+        # attention output rows of this stream live in the joint [B, N, D] tensor
+        aux_rows = tmap if stream != "j" else (rows, 0, 0)
+        K.gemm(h, block.gate[stream], gbuf, epilogue=_lib.EPI_GATE, aux=ws["o"], aux_rows=aux_rows)
+        w, b = block.proj[stream]
+        K.gemm(gbuf, w, branch, bias=b)
+        tok = ws["tokens"].data_ptr()
+        _lib.call(
+            "iris_gated_residual_rms_norm", tok, *tmap, branch.data_ptr(), _lib.BF16, rows, 0, 0,
+            norms["post_attn"].data_ptr(), self._chunk(mods, 2, d), 6 * d, rows, rpb, d, eps, _lib.NEXT_NORM_MODULATE,
+            norms["norm2"].data_ptr(), self._chunk(mods, 3, d), self._chunk(mods, 4, d), 6 * d, h2.data_ptr(),
+            _lib.BF16, rows, 0, 0, st,
+        )  # fmt: skip
+        act = ws["act"][off : off + rows]
+        K.gemm(h2, block.w13[stream], act, epilogue=_lib.EPI_SWIGLU)
+        K.gemm(act, block.w2[stream], branch)
+        # the mlp residual also writes the next block's input
+        if nxt is None:
+            # last block: only image rows continue; they leave as s = silu(t_emb + x)
+            image_map = (g.L, g.N, g.T)
+            _lib.call(
+                "iris_gated_residual_rms_norm", tok, *image_map, branch.data_ptr(), _lib.BF16, *image_map,
+                norms["post_mlp"].data_ptr(), self._chunk(mods, 5, d), 6 * d, g.batch * g.L, g.L, d, eps,
+                _lib.NEXT_SILU_ADD, None, ws["t_emb"].data_ptr(), None, d, ws["s_cond"].data_ptr(), _lib.BF16,
+                g.batch * g.L, 0, 0, st,
+            )  # fmt: skip
+            return
+        nstream = stream if nxt.dual else "j"
+        nmods = self._mods(ws, nxt, nstream)
+        if nxt.dual:
+            next_map = (rows, 0, 0)
+            next_out = ws["h"][off:]
+        else:
+            next_map = tmap if stream != "j" else (rows, 0, 0)
+            next_out = ws["h"]
+        _lib.call(
+            "iris_gated_residual_rms_norm", tok, *tmap, branch.data_ptr(), _lib.BF16, rows, 0, 0,
+            norms["post_mlp"].data_ptr(), self._chunk(mods, 5, d), 6 * d, rows, rpb, d, eps, _lib.NEXT_NORM_MODULATE,
+            nxt.norms[nstream]["norm1"].data_ptr(), self._chunk(nmods, 0, d), self._chunk(nmods, 1, d), 6 * d,
+            next_out.data_ptr(), _lib.BF16, *next_map, st,
+        )  # fmt: skip
+
+    # -- pixel stage ------------------------------------------------------------------
+    def _pixel_stage(self, x, ws, g, grid, pcos, psin, pos, v, eps, st) -> None:
+        cfg = self.cfg
+        pix = cfg.pixel
+        p = cfg.patch_size
+        height, width = grid[0] * p, grid[1] * p
+        pdt = _lib.F32 if self.pixel_dtype == torch.float32 else _lib.BF16
+        pw, pb = self.pixel_embed_w
+        blocks = self.pixel_blocks
+        _lib.call(
+            "iris_pixel_embed", x.data_ptr(), pw.data_ptr(), pb.data_ptr(), None if pos is None else pos.data_ptr(),
+            ws["pixels"].data_ptr(), pdt, ws["ph"].data_ptr(), blocks[0]["norm1"].data_ptr(), eps, g.batch, height,
+            width, p, st,
+        )  # fmt: skip
+        heads = pix.num_heads
+        for i, blk in enumerate(blocks):
+            K.gemm(ws["s_cond"], blk["adaln"][0], ws["pmods"], bias=blk["adaln"][1])
+            K.gemm(ws["ph"], blk["compress"][0], ws["comp"], bias=blk["compress"][1])
+            K.gemm(ws["comp"], blk["qkv"], ws["pqkv"])
+            qn, kn = blk["qk_norm"]
+            _lib.call(
+                "iris_qkv_heads", ws["pqkv"].data_ptr(), g.batch, g.L, 3 * pix.attn_hidden_size, heads, heads,
+                qn.data_ptr(), kn.data_ptr(), pcos.data_ptr(), psin.data_ptr(), eps, ws["pq"].data_ptr(),
+                ws["pk"].data_ptr(), ws["pv"].data_ptr(), g.L, 0, st,
+            )  # fmt: skip
+            K.flash_attention(ws["pq"], ws["pk"], ws["pv"], ws["po"].view(g.batch, g.L, -1))
+            K.gemm(ws["po"], blk["proj"][0], ws["pproj"], bias=blk["proj"][1])
+            K.gemm(ws["pproj"], blk["expand"][0], ws["pbranch"], bias=blk["expand"][1])
+            (w1, b1), (w2, b2) = blk["fc1"], blk["fc2"]
+            if i + 1 < len(blocks):
+                _lib.call(
+                    "iris_pixel_mlp", ws["pixels"].data_ptr(), pdt, ws["pbranch"].data_ptr(), ws["pmods"].data_ptr(),
+                    blk["norm2"].data_ptr(), w1.data_ptr(), b1.data_ptr(), w2.data_ptr(), b2.data_ptr(),
+                    blocks[i + 1]["norm1"].data_ptr(), ws["ph"].data_ptr(), ws["pixels"].numel() // 16, eps, st,
+                )  # fmt: skip
+            else:
+                fn, fw, fb = self.final
+                _lib.call(
+                    "iris_pixel_mlp_head", ws["pixels"].data_ptr(), pdt, ws["pbranch"].data_ptr(),
+                    ws["pmods"].data_ptr(), blk["norm2"].data_ptr(), w1.data_ptr(), b1.data_ptr(), w2.data_ptr(),
+                    b2.data_ptr(), fn.data_ptr(), fw.data_ptr(), fb.data_ptr(), v.data_ptr(), g.batch, height, width,
+                    p, eps, st,
+                )  # fmt: skip
+
+
+@dataclass
+class _Geometry:
+    batch: int
+    T: int
+    L: int
+    N: int
+    d: int

@@ -24,6 +24,8 @@ def cfg_velocity(model_fn: ModelFn, x, t_model: float, cond, uncond, cfg_scale: 
         t = torch.full((x.shape[0],), t_model, device=x.device, dtype=torch.float32)
         return model_fn(x, t, cond)
     t = torch.full((2 * x.shape[0],), t_model, device=x.device, dtype=torch.float32)
+    # one negative prompt serves every image, as the pipeline expands it (pipeline.py:297-300)
+    uncond = uncond.expand(cond.shape[0], *uncond.shape[1:]) if uncond.shape[0] == 1 else uncond
     out = model_fn(torch.cat([x, x], dim=0), t, torch.cat([uncond, cond], dim=0))
     out_u, out_c = out.chunk(2, dim=0)
     return out_u + cfg_scale * (out_c - out_u)

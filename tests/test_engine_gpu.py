@@ -1,0 +1,145 @@
+"""Whole-forward parity of CudaIris on the B200 against the reference.
+
+* toy released topology (MHA and GQA): the reference's own fp32 outputs stored
+  in tests/golden (tests/test_metal_engine.py:73-91 is the reference's version);
+* the 4-step guided Euler sample: PSNR >= 40 dB against the reference's sample;
+* the BASELINE config-3 model at 1024^2: against the fp32 oracle run on the
+  same GPU with TF32 off (per-op metric max|a-b|/max|b| and PSNR).
+"""
+
+import math
+
+import pytest
+import torch
+
+from conftest import golden, requires_gpu
+from oracle.config import OracleConfig, PixelConfig, baseline_step_config
+from oracle.model import OracleModel
+from oracle.params import seeded_init
+from oracle.sampler import euler_cfg as oracle_euler
+
+pytestmark = requires_gpu
+
+REL_TOL = 2e-2  # per-op max relative error in BF16 (max|a-b| / max|b|)
+PSNR_MIN = 40.0
+
+
+def _config(d):
+    d = dict(d)
+    return OracleConfig(**{**d, "pixel": PixelConfig(**d["pixel"])})
+
+
+def rel_err(a, b):
+    a, b = a.double().cpu(), b.double().cpu()
+    return float((a - b).abs().max() / b.abs().max())
+
+
+def psnr(a, ref, peak_to_peak=None):
+    a, ref = a.double().cpu(), ref.double().cpu()
+    mse = float(((a - ref) ** 2).mean())
+    ptp = float(ref.max() - ref.min()) if peak_to_peak is None else peak_to_peak
+    return 10 * math.log10(ptp**2 / mse) if mse > 0 else math.inf
+
+
+@pytest.fixture(scope="module")
+def iris():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    import iris_b200
+
+    return iris_b200
+
+
+def _engine(iris, cfg, params):
+    state = {k: v.cuda() for k, v in params.items()}
+    return iris.CudaIris(iris.IrisWeights(cfg, state))
+
+
+@pytest.mark.parametrize("name", ["released_mha", "released_gqa"])
+def test_forward_matches_reference(iris, name):
+    fx = golden(name)
+    cfg = _config(fx["config"])
+    engine = _engine(iris, cfg, seeded_init(cfg, seed=0))
+    text = fx["prepared_text"].cuda()
+    text_before = text.clone()
+    v = engine(fx["x"].cuda(), fx["t"].cuda(), text)
+    assert torch.equal(text, text_before), "the engine must not write its text input"
+    err = rel_err(v, fx["v"])
+    print(f"{name}: max rel err {err:.3e}, psnr {psnr(v, fx['v']):.1f} dB")
+    assert err < REL_TOL
+    assert psnr(v, fx["v"]) > PSNR_MIN
+
+
+def test_encode_text_matches_reference(iris):
+    fx = golden("released_mha")
+    cfg = _config(fx["config"])
+    engine = _engine(iris, cfg, seeded_init(cfg, seed=0))
+    text = engine.encode_text(fx["y"].cuda())
+    assert rel_err(text, fx["prepared_text"]) < REL_TOL
+
+
+def test_euler_cfg_sample_matches_reference(iris):
+    fx = golden("released_mha")
+    cfg = _config(fx["config"])
+    engine = _engine(iris, cfg, seeded_init(cfg, seed=0))
+    s = fx["euler_cfg"]
+    sample = iris.euler_cfg(engine, s["noise"].cuda(), s["cond"].cuda(), s["uncond"].cuda(), cfg_scale=s["cfg_scale"],
+                            cfg_interval=s["cfg_interval"])  # fmt: skip
+    value = psnr(sample, s["sample"])
+    print(f"euler cfg sample: psnr {value:.1f} dB (ptp-2: {psnr(sample, s['sample'], 2.0):.1f} dB)")
+    assert value >= PSNR_MIN
+
+
+def test_non_square_grid_and_odd_batch(iris):
+    fx = golden("released_gqa")  # 24 x 16 input: a 6 x 4 patch grid
+    cfg = _config(fx["config"])
+    params = seeded_init(cfg, seed=0)
+    engine = _engine(iris, cfg, params)
+    oracle = OracleModel(cfg, params)
+    x, t, text = fx["x"][:1], fx["t"][:1], fx["prepared_text"][:1]
+    with torch.no_grad():
+        expected = oracle(x, t, text)
+    v = engine(x.cuda(), t.cuda(), text.cuda())
+    assert rel_err(v, expected) < REL_TOL
+
+
+@pytest.fixture(scope="module")
+def full_size(iris):
+    """BASELINE config 3 (d = 3072, 24 blocks, 24 MHA heads x 128) with seeded
+    random weights drawn on the GPU, shared by the oracle (fp32) and the engine."""
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    cfg = baseline_step_config()
+    params = seeded_init(cfg, seed=0, device="cuda")
+    engine = iris.CudaIris(iris.IrisWeights(cfg, params))
+    gen = torch.Generator().manual_seed(1)
+    x = torch.randn(1, 3, 1024, 1024, generator=gen).repeat(2, 1, 1, 1)
+    y = torch.randn(2, 256, cfg.text_dim, generator=gen)
+    oracle = OracleModel(cfg, params)
+    with torch.no_grad():
+        text = oracle.embed_text(y.cuda())
+    return cfg, params, engine, oracle, x.cuda(), text
+
+
+def test_full_size_step_matches_fp32_oracle(full_size):
+    cfg, params, engine, oracle, x, text = full_size
+    t = torch.full((2,), 625.0, device="cuda")
+    with torch.no_grad():
+        expected = oracle(x, t, text)
+    v = engine(x, t, text)
+    err, value = rel_err(v, expected), psnr(v, expected)
+    print(f"1024^2 step: max rel err {err:.3e}, psnr {value:.1f} dB")
+    assert err < REL_TOL
+    assert value > PSNR_MIN
+
+
+def test_full_size_euler_cfg_psnr(full_size, iris):
+    cfg, params, engine, oracle, x, text = full_size
+    noise = torch.randn(1, 3, 1024, 1024, generator=torch.Generator().manual_seed(0)).cuda()
+    cond, uncond = text[1:], text[:1]
+    with torch.no_grad():
+        expected = oracle_euler(oracle, noise, cond, uncond, 3.0)
+    sample = iris.euler_cfg(engine, noise, cond, uncond, cfg_scale=3.0)
+    value = psnr(sample, expected)
+    print(f"1024^2 4-step Euler CFG 3: psnr {value:.1f} dB (ptp-2: {psnr(sample, expected, 2.0):.1f} dB)")
+    assert value >= PSNR_MIN

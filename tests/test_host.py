@@ -1,0 +1,108 @@
+"""Host-side logic of iris_b200 on the CPU: position tables (bit-exact against
+the reference), topology checks, weight packing, samplers, configs."""
+
+import dataclasses
+
+import pytest
+import torch
+
+from conftest import golden
+from oracle.config import baseline_step_config as oracle_baseline
+from oracle.config import released_topology
+
+
+def test_tables_are_bit_exact_with_reference():
+    from iris_b200 import tables
+
+    r = golden("ops")["rope"]
+    assert torch.equal(torch.view_as_real(tables.rope_2d(128, 64, 64, 1e4, 16.0, "isotropic"))[::16], r["img_64_every16"])
+    assert torch.equal(torch.view_as_real(tables.rope_2d(128, 6, 4, 1e4, 16.0, "isotropic")), r["img_6x4"])
+    assert torch.equal(torch.view_as_real(tables.rope_2d(64, 8, 8, 1e4, 16.0, "square")), r["img_sq"])
+    assert torch.equal(torch.view_as_real(tables.rope_1d(128, 256, 1e4)), r["txt_256"])
+    s = golden("ops")["sincos"]
+    assert torch.equal(tables.sincos_pos_embed_2d(16, 16, 24), s["t_16x24"])
+    assert torch.equal(tables.sincos_pos_embed_2d(16, 64, 64), s["t_64"])
+
+
+def test_trunk_table_puts_text_rows_first():
+    from iris_b200 import tables
+
+    text, image = tables.rope_1d(128, 5, 1e4), tables.rope_2d(128, 2, 3, 1e4, 16.0, "isotropic")
+    cos, sin = tables.cos_sin(text, image, device="cpu")
+    assert cos.shape == (11, 64) and cos.is_contiguous()
+    assert torch.equal(cos[:5], text.real) and torch.equal(sin[5:], image.imag)
+
+
+def test_config_round_trip_from_oracle_fields():
+    from iris_b200.config import baseline_step_config, from_any
+
+    ours = from_any(oracle_baseline())
+    assert ours.hidden_size == 3072 and ours.num_heads == 24 and ours.kv_heads == 24
+    assert ours.swiglu_hidden == 8192 and ours.text_len == 256
+    assert dataclasses.asdict(baseline_step_config())["pixel"] == dataclasses.asdict(ours.pixel)
+
+
+@pytest.mark.parametrize(
+    "change,missing",
+    [
+        ({"modulation": "per_block"}, "shared_bias"),
+        ({"sandwich_norm": False}, "sandwich"),
+        ({"num_heads": 4}, "128-wide"),
+        ({"block": "mmdit"}, "single-stream tail"),
+    ],
+)
+def test_check_supported_rejects_other_topologies(change, missing):
+    from iris_b200.config import from_any
+    from iris_b200.model import check_supported
+
+    cfg = dataclasses.replace(from_any(released_topology()), **change)
+    state = {"s_embedder.proj.weight": 0, "t_embedder.mlp.0.weight": 0, "final_layer.linear.weight": 0}
+    with pytest.raises(ValueError, match=missing):
+        check_supported(cfg, state)
+    check_supported(from_any(released_topology()), state)
+
+
+def test_pack_swiglu_layout():
+    from iris_b200.model import pack_swiglu
+
+    ffn, d = 300, 8
+    w1 = torch.arange(ffn * d, dtype=torch.float32).reshape(ffn, d)
+    w3 = -w1
+    w2 = torch.ones(d, ffn)
+    w13, w2p = pack_swiglu(w1, w3, w2)
+    assert w13.shape == (2 * 384, d) and w2p.shape == (d, 384)
+    for tile in range(3):
+        rows = slice(tile * 128, min(ffn, (tile + 1) * 128))
+        n = rows.stop - rows.start
+        assert torch.equal(w13[tile * 256 : tile * 256 + n], w1[rows])
+        assert torch.equal(w13[tile * 256 + 128 : tile * 256 + 128 + n], w3[rows])
+    assert torch.all(w13[2 * 256 + 44 : 2 * 256 + 128] == 0) and torch.all(w2p[:, ffn:] == 0)
+
+
+def test_flow_dpm_solver_matches_reference():
+    from iris_b200.sampling import FlowDPMSolver
+
+    fx = golden("samplers")
+    z, cond, uncond = fx["inputs"]["z"], fx["inputs"]["cond"], fx["inputs"]["uncond"]
+
+    def model_fn(x, t, text):
+        return 0.3 * x + 0.05 * text + 1e-4 * t[:, None, None, None]
+
+    for key, case in fx.items():
+        if key.startswith("dpm_"):
+            solver = FlowDPMSolver(model_fn, cfg_scale=case["cfg_scale"])
+            assert solver.time_grid(case["steps"], case["shift"]) == case["grid"]
+            out = solver.sample(z, cond, uncond, steps=case["steps"], order=case["order"], shift=case["shift"])
+            torch.testing.assert_close(out, case["sample"], rtol=1e-6, atol=1e-6)
+
+
+def test_dp_shards_cover_every_image_once():
+    from iris_b200.parallel import image_shard
+
+    for images in (1, 5, 8, 13):
+        for world in (1, 2, 4, 8):
+            seen = []
+            for rank in range(world):
+                lo, hi = image_shard(images, rank, world)
+                seen.extend(range(lo, hi))
+            assert seen == list(range(images))

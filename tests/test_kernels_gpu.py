@@ -1,0 +1,316 @@
+"""Kernel parity on the B200: each entry point of libiris_b200.so against the
+reference's own outputs (tests/golden/ops.pt) or the fp32 oracle, mirroring
+tests/test_metal_engine.py:159-289 of the reference."""
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from conftest import golden, requires_gpu
+from oracle import ops
+
+pytestmark = requires_gpu
+
+DTYPES = [torch.float32, torch.bfloat16, torch.float16]
+
+
+@pytest.fixture(scope="module")
+def K():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from iris_b200 import kernels
+
+    return kernels
+
+
+def rel_err(a, b):
+    """max |a - b| / max |b| (the per-op tolerance metric)."""
+    a, b = a.float().cpu(), b.float().cpu()
+    return float((a - b).abs().max() / b.abs().max().clamp_min(1e-30))
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("out_dtype", DTYPES)
+def test_qk_norm_rope_matches_reference(K, dtype, out_dtype):
+    fx = golden("ops")["qk_norm_rope"]
+    x = fx["x"].to("cuda", dtype)
+    out = torch.zeros(2, fx["heads"], 42, 128, device="cuda", dtype=out_dtype)
+    K.qk_norm_rope(x, fx["weight"].cuda(), fx["cos"].cuda(), fx["sin"].cuda(), 1e-6, fx["heads"],
+                   col_offset=fx["col_offset"], out=out, offset=fx["offset"])  # fmt: skip
+    expected = ops.qk_norm_rope_reference(x[..., fx["col_offset"] :].float().cpu(), fx["weight"], fx["cos"][5:],
+                                          fx["sin"][5:], 1e-6)  # fmt: skip
+    tol = {torch.float32: 1e-5, torch.float16: 2e-3, torch.bfloat16: 8e-3}[out_dtype]
+    torch.testing.assert_close(out[:, :, 5:].float().cpu(), expected, rtol=tol, atol=1e-5)
+    assert torch.all(out[:, :, :5] == 0)
+    if dtype == torch.float32 and out_dtype == torch.float32:
+        torch.testing.assert_close(out.cpu(), fx["out"], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("branch_dtype", [torch.float32, torch.bfloat16])
+def test_row_kernels_match_reference(K, branch_dtype):
+    fx = golden("ops")
+    r = fx["rms_norm_modulate"]
+    args = [t.cuda() for t in (r["x"], r["weight"], r["shift"], r["scale"])]
+    out = K.rms_norm_modulate(*args, 1e-6, torch.bfloat16)
+    torch.testing.assert_close(out.float().cpu(), r["out_bf16"].float(), rtol=8e-3, atol=1e-5)
+    out = K.rms_norm_modulate(*args, 1e-6, torch.float32)
+    torch.testing.assert_close(out.cpu(), r["out_f32"], rtol=1e-5, atol=1e-5)
+    g = fx["gated_residual"]
+    branch = g["branch"].to(branch_dtype)
+    expected = ops.gated_residual_rms_norm_reference(g["residual"], branch, g["weight"], g["gate"], 1e-6)
+    actual = K.gated_residual_rms_norm_(g["residual"].cuda(), branch.cuda(), g["weight"].cuda(), g["gate"].cuda(), 1e-6)
+    torch.testing.assert_close(actual.cpu(), expected, rtol=1e-5, atol=1e-5)
+    if branch_dtype == torch.float32:
+        torch.testing.assert_close(actual.cpu(), g["out"], rtol=1e-5, atol=1e-5)
+
+
+def _modulation_layouts(batch, width, gen):
+    mods = torch.randn(batch, 1, 6 * width, generator=gen).cuda()
+    chunks = list(mods.chunk(6, dim=-1)[:3])
+    one = torch.randn(1, 1, 3 * width, generator=gen).cuda()
+    padded = torch.randn(batch * 3 * width + 1, generator=gen).cuda()
+    misaligned = [padded[1 + i * batch * width :][: batch * width].view(batch, 1, width) for i in range(3)]
+    return {
+        "contiguous": [c.contiguous() for c in chunks],
+        "chunks": chunks,
+        "expanded": [c.expand(batch, 1, width) for c in one.chunk(3, dim=-1)],
+        "misaligned": misaligned,
+    }
+
+
+@pytest.mark.parametrize("batch", [1, 2, 3])
+def test_row_kernels_read_strided_modulation_exactly(K, batch):
+    """tests/test_metal_engine.py:226-246: every modulation layout gives bit-identical rows."""
+    gen = torch.Generator().manual_seed(batch)
+    width = 384
+    x = torch.randn(batch, 5, width, generator=gen).cuda()
+    branch = torch.randn(batch, 5, width, generator=gen).to("cuda", torch.bfloat16)
+    weight = (torch.rand(width, generator=gen) + 0.5).cuda()
+    for name, (shift, scale, gate) in _modulation_layouts(batch, width, gen).items():
+        dense = [t.contiguous() for t in (shift, scale, gate)]
+        expected = K.rms_norm_modulate(x, weight, dense[0], dense[1], 1e-6, torch.float16)
+        actual = K.rms_norm_modulate(x, weight, shift, scale, 1e-6, torch.float16)
+        assert actual.view(torch.int16).equal(expected.view(torch.int16)), name
+        expected = K.gated_residual_rms_norm_(x.clone(), branch, weight, dense[2], 1e-6)
+        actual = K.gated_residual_rms_norm_(x.clone(), branch, weight, gate, 1e-6)
+        assert actual.view(torch.int32).equal(expected.view(torch.int32)), name
+        rows, _ = K._per_batch(gate, batch, width)
+        in_place = rows.untyped_storage().data_ptr() == gate.untyped_storage().data_ptr()
+        assert in_place == (name != "misaligned"), name
+
+
+def test_kernels_reject_non_fp32_gains(K):
+    x = torch.randn(1, 4, 128, device="cuda")
+    gain = torch.ones(128, device="cuda", dtype=torch.bfloat16)
+    zeros = torch.zeros(1, 1, 128, device="cuda")
+    with pytest.raises(ValueError, match="FP32"):
+        K.rms_norm_modulate(x, gain, zeros, zeros, 1e-6, torch.bfloat16)
+
+
+@pytest.mark.parametrize("pixel_dtype", [torch.bfloat16, torch.float32])
+def test_pixel_kernels_match_reference(K, pixel_dtype):
+    m = golden("ops")["pixel_mlp"]
+
+    class Lin:
+        def __init__(self, w, b):
+            self.weight, self.bias = w.cuda(), b.cuda()
+
+    pixels = m["pixels"].to("cuda", pixel_dtype)
+    nxt = K.pixel_mlp_(pixels, m["branch"].cuda(), m["mods"].cuda(), m["norm_weight"].cuda(),
+                       Lin(m["fc1_w"], m["fc1_b"]), Lin(m["fc2_w"], m["fc2_b"]), m["next_norm_weight"].cuda(), 1e-6)  # fmt: skip
+    # one BF16 ulp where rounding order differs (tests/test_metal_engine.py:281-289)
+    tol = 1e-2 if pixel_dtype == torch.bfloat16 else 2e-2
+    torch.testing.assert_close(pixels.float().cpu(), m["new_pixels"].float(), rtol=tol, atol=tol)
+    torch.testing.assert_close(nxt.float().cpu(), m["next_input"].float(), rtol=tol, atol=tol)
+    rms = K.pixel_rms_norm(m["pixels"].cuda(), m["norm_weight"].cuda(), 1e-6)
+    torch.testing.assert_close(rms.float().cpu(), m["rms"].float(), rtol=1e-2, atol=1e-2)
+
+
+def test_pixel_kernels_reject_short_parameter_buffers(K):
+    pixels = torch.zeros(1, 1, 16, device="cuda", dtype=torch.bfloat16)
+    gain = torch.ones(16, device="cuda")
+    with pytest.raises(ValueError, match="gain width"):
+        K.pixel_rms_norm(pixels, gain[:1], 1e-6)
+    mods = torch.zeros(1, 1, 64, device="cuda", dtype=torch.bfloat16)
+    fc1 = torch.nn.Linear(16, 64, device="cuda", dtype=torch.bfloat16)
+    fc2 = torch.nn.Linear(64, 16, device="cuda", dtype=torch.bfloat16)
+    fc1.bias = torch.nn.Parameter(fc1.bias[:1])
+    with pytest.raises(ValueError, match="pixel-stage widths"):
+        K.pixel_mlp_(pixels, pixels.clone(), mods, gain, fc1, fc2, gain, 1e-6)
+
+
+# ------------------------------------------------------------------------- GEMM
+GEMM_SHAPES = [(128, 256, 64), (200, 96, 48), (1000, 544, 312), (8704 // 8, 9216 // 8, 3072 // 4), (64, 1280, 1280)]
+
+
+@pytest.mark.parametrize("M,N,K_", GEMM_SHAPES)
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
+def test_gemm_matches_fp32_reference(K, M, N, K_, out_dtype):
+    gen = torch.Generator(device="cuda").manual_seed(M + N + K_)
+    a = torch.randn(M, K_, device="cuda", generator=gen).to(torch.bfloat16)
+    w = (torch.randn(N, K_, device="cuda", generator=gen) * 0.05).to(torch.bfloat16)
+    bias = torch.randn(N, device="cuda", generator=gen)
+    out = torch.empty(M, N, device="cuda", dtype=out_dtype)
+    K.gemm(a, w, out, bias=bias)
+    expected = a.float() @ w.float().T + bias
+    assert rel_err(out, expected) < (1e-2 if out_dtype == torch.bfloat16 else 1e-4)
+
+
+def test_gemm_row_map_writes_only_mapped_rows(K):
+    """Image rows into a joint [text | image] buffer: rows (b, T + i)."""
+    T, L, B, N, D = 7, 45, 2, 52, 256
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    a = torch.randn(B * L, 64, device="cuda", generator=gen).to(torch.bfloat16)
+    w = torch.randn(D, 64, device="cuda", generator=gen).to(torch.bfloat16)
+    out = torch.full((B * N, D), -7.0, device="cuda")
+    K.gemm(a, w, out, out_rows=(L, N, T))
+    expected = (a.float() @ w.float().T).view(B, L, D)
+    got = out.view(B, N, D)
+    assert rel_err(got[:, T:], expected) < 1e-4
+    assert torch.all(got[:, :T] == -7.0)
+
+
+def test_gemm_swiglu_epilogue(K):
+    from iris_b200._lib import EPI_SWIGLU
+    from iris_b200.model import pack_swiglu
+
+    M, D, F_ = 300, 256, 682
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    a = torch.randn(M, D, device="cuda", generator=gen).to(torch.bfloat16)
+    w1, w3 = ((torch.randn(F_, D, device="cuda", generator=gen) * 0.05).to(torch.bfloat16) for _ in range(2))
+    w2 = (torch.randn(D, F_, device="cuda", generator=gen) * 0.05).to(torch.bfloat16)
+    w13, w2p = pack_swiglu(w1, w3, w2)
+    act = torch.empty(M, w2p.shape[1], device="cuda", dtype=torch.bfloat16)
+    K.gemm(a, w13, act, epilogue=EPI_SWIGLU)
+    out = torch.empty(M, D, device="cuda", dtype=torch.bfloat16)
+    K.gemm(act, w2p, out)
+    h = F.silu(a.float() @ w1.float().T) * (a.float() @ w3.float().T)
+    assert rel_err(act[:, :F_], h) < 1e-2
+    assert torch.all(act[:, F_:] == 0)
+    assert rel_err(out, h @ w2.float().T) < 2e-2
+
+
+def test_gemm_gate_epilogue_with_aux_rows(K):
+    from iris_b200._lib import EPI_GATE
+
+    T, L, B, D = 16, 36, 2, 256
+    N = T + L
+    gen = torch.Generator(device="cuda").manual_seed(9)
+    h = torch.randn(B * L, D, device="cuda", generator=gen).to(torch.bfloat16)
+    wg = (torch.randn(D, D, device="cuda", generator=gen) * 0.05).to(torch.bfloat16)
+    attn = torch.randn(B * N, D, device="cuda", generator=gen).to(torch.bfloat16)
+    out = torch.empty(B * L, D, device="cuda", dtype=torch.bfloat16)
+    K.gemm(h, wg, out, epilogue=EPI_GATE, aux=attn, aux_rows=(L, N, T))
+    expected = attn.view(B, N, D)[:, T:].reshape(B * L, D).float() * torch.sigmoid(h.float() @ wg.float().T)
+    assert rel_err(out, expected) < 1e-2
+
+
+# -------------------------------------------------------------------- attention
+@pytest.mark.parametrize("B,H,Hkv,N", [(1, 1, 1, 128), (2, 2, 1, 52), (2, 3, 3, 300), (1, 2, 2, 4352)])
+def test_flash_attention_matches_fp32_sdpa(K, B, H, Hkv, N):
+    gen = torch.Generator(device="cuda").manual_seed(B * 100 + N)
+    q = torch.randn(B, H, N, 128, device="cuda", generator=gen).to(torch.bfloat16)
+    k = torch.randn(B, Hkv, N, 128, device="cuda", generator=gen).to(torch.bfloat16)
+    v = torch.randn(B, Hkv, N, 128, device="cuda", generator=gen).to(torch.bfloat16)
+    out = torch.empty(B, N, H * 128, device="cuda", dtype=torch.bfloat16)
+    K.flash_attention(q, k, v, out)
+    expected = ops.sdpa(q.float(), k.float(), v.float()).transpose(1, 2).reshape(B, N, H * 128)
+    assert rel_err(out, expected) < 2e-2
+    assert K.device_error() == 0
+
+
+def test_flash_attention_sharp_softmax(K):
+    """Large logits exercise the lazy rescale path (row max growing by > 2^8)."""
+    B, H, N = 1, 1, 640
+    gen = torch.Generator(device="cuda").manual_seed(11)
+    q = (torch.randn(B, H, N, 128, device="cuda", generator=gen) * 4).to(torch.bfloat16)
+    k = (torch.randn(B, H, N, 128, device="cuda", generator=gen) * 4).to(torch.bfloat16)
+    k[:, :, 400:] *= 3  # later key blocks carry larger scores
+    v = torch.randn(B, H, N, 128, device="cuda", generator=gen).to(torch.bfloat16)
+    out = torch.empty(B, N, H * 128, device="cuda", dtype=torch.bfloat16)
+    K.flash_attention(q, k, v, out)
+    expected = ops.sdpa(q.float(), k.float(), v.float()).transpose(1, 2).reshape(B, N, H * 128)
+    assert rel_err(out, expected) < 2e-2
+
+
+# ---------------------------------------------------------- heads, layout, small
+def test_qkv_heads_matches_oracle(K):
+    from iris_b200 import _lib
+
+    B, N, T, hq, hkv = 2, 40, 9, 3, 1
+    gen = torch.Generator().manual_seed(2)
+    qkv = torch.randn(B, N, (hq + 2 * hkv) * 128, generator=gen).to(torch.bfloat16)
+    qw, kw = torch.rand(128, generator=gen) + 0.5, torch.rand(128, generator=gen) + 0.5
+    cis = ops.rope_2d(128, 4, 10, 1e4, 16.0, "isotropic")
+    cis = torch.cat([ops.rope_1d(128, T, 1e4), cis])
+    cos, sin = torch.view_as_real(cis)[..., 0].contiguous(), torch.view_as_real(cis)[..., 1].contiguous()
+    q = torch.zeros(B, hq, T + N, 128, device="cuda", dtype=torch.bfloat16)
+    k = torch.zeros(B, hkv, T + N, 128, device="cuda", dtype=torch.bfloat16)
+    v = torch.zeros(B, hkv, T + N, 128, device="cuda", dtype=torch.bfloat16)
+    # device copies held in variables: the launch is asynchronous
+    g, qw_d, kw_d, cos_d, sin_d = (t.cuda() for t in (qkv, qw, kw, cos, sin))
+    _lib.call("iris_qkv_heads", g.data_ptr(), B, N, g.shape[-1], hq, hkv, qw_d.data_ptr(), kw_d.data_ptr(),
+              cos_d.data_ptr(), sin_d.data_ptr(), 1e-6, q.data_ptr(), k.data_ptr(), v.data_ptr(), T + N, T,
+              torch.cuda.current_stream().cuda_stream)  # fmt: skip
+    torch.cuda.synchronize()
+    c, s = cos[T:], sin[T:]
+    eq = ops.qk_norm_rope_reference(qkv[..., : hq * 128].float(), qw, c, s, 1e-6)
+    ek = ops.qk_norm_rope_reference(qkv[..., hq * 128 : (hq + hkv) * 128].float(), kw, c, s, 1e-6)
+    ev = qkv[..., (hq + hkv) * 128 :].reshape(B, N, hkv, 128).transpose(1, 2)
+    torch.testing.assert_close(q[:, :, T:].float().cpu(), eq, rtol=8e-3, atol=1e-2)
+    torch.testing.assert_close(k[:, :, T:].float().cpu(), ek, rtol=8e-3, atol=1e-2)
+    assert torch.equal(v[:, :, T:].cpu(), ev)
+    assert torch.all(q[:, :, :T] == 0)
+
+
+def test_patchify_and_unpatchify_are_bit_exact(K):
+    from iris_b200 import _lib
+
+    st = torch.cuda.current_stream().cuda_stream
+    for (B, H, W, p) in ((2, 32, 48, 16), (1, 24, 16, 4)):
+        x = (torch.arange(B * 3 * H * W, dtype=torch.float32) % 251).reshape(B, 3, H, W)
+        out = torch.empty(B * (H // p) * (W // p), 3 * p * p, device="cuda", dtype=torch.bfloat16)
+        xc = x.cuda()
+        _lib.call("iris_patchify", xc.data_ptr(), out.data_ptr(), B, 3, H, W, p, st)
+        assert torch.equal(out.float().cpu(), ops.patchify(x, p).reshape(-1, 3 * p * p))
+        pix = torch.randn(B * (H // p) * (W // p), p * p, 3)
+        v = torch.empty(B, 3, H, W, device="cuda")
+        pc = pix.cuda()
+        _lib.call("iris_unpatchify", pc.data_ptr(), v.data_ptr(), B, 3, H, W, p, st)
+        assert torch.equal(v.cpu(), ops.unpatchify_pixels(pix, B, H, W, p))
+
+
+def test_timestep_gemv_and_cfg_euler(K):
+    from iris_b200 import _lib
+
+    st = torch.cuda.current_stream().cuda_stream
+    t = torch.tensor([0.0, 125.0, 625.0, 938.0, 1000.0])
+    feats = torch.empty(5, 256, device="cuda")
+    tc = t.cuda()
+    _lib.call("iris_timestep_embedding", tc.data_ptr(), feats.data_ptr(), 5, 256, 10.0, st)
+    torch.testing.assert_close(feats.cpu(), ops.timestep_embedding(t, 256, 10.0), rtol=1e-5, atol=2e-5)
+    gen = torch.Generator(device="cuda").manual_seed(1)
+    x = torch.randn(5, 512, device="cuda", generator=gen)
+    w = torch.randn(384, 512, device="cuda", generator=gen) * 0.05
+    b = torch.randn(384, device="cuda", generator=gen)
+    out = torch.empty(5, 384, device="cuda")
+    _lib.call("iris_gemv", x.data_ptr(), 5, 512, w.data_ptr(), _lib.F32, b.data_ptr(), out.data_ptr(), 384, 1, 1, st)
+    torch.testing.assert_close(out, F.silu(F.silu(x) @ w.T + b), rtol=1e-4, atol=1e-5)
+    v = torch.randn(4, 3, 8, 8, device="cuda", generator=gen)
+    xs = torch.randn(2, 3, 8, 8, device="cuda", generator=gen)
+    nxt = torch.empty_like(xs)
+    _lib.call("iris_cfg_euler", v.data_ptr(), xs.data_ptr(), nxt.data_ptr(), 2, 192, 3.0, 0.938, 0.833, 1, st)
+    vg = v[:2] + 3.0 * (v[2:] - v[:2])
+    clean = xs - 0.938 * vg
+    expected = (1 - 0.833) * clean + 0.833 * (xs - (1 - 0.938) * clean) / 0.938
+    torch.testing.assert_close(nxt, expected, rtol=1e-5, atol=1e-5)
+
+
+def test_require_finite_on_device(K):
+    from iris_b200.model import require_finite
+
+    ok = torch.zeros(2, 3, device="cuda")
+    assert require_finite(ok) is ok
+    for bad in (float("inf"), float("nan")):
+        with pytest.raises(FloatingPointError):
+            require_finite(torch.tensor([0.0, bad], device="cuda"))

@@ -30,7 +30,8 @@ def test_oracle_forward_matches_reference(name):
     model = OracleModel(cfg, params)
     with torch.no_grad():
         text = model.embed_text(fx["y"])
-        torch.testing.assert_close(text, fx["prepared_text"], rtol=1e-5, atol=1e-6)
+        # fp32 sums over 2560 features: the thread count changes the last bits
+        torch.testing.assert_close(text, fx["prepared_text"], rtol=1e-4, atol=1e-5)
         capture = {}
         v = model(fx["x"], fx["t"], text, capture=capture)
     torch.testing.assert_close(v, fx["v"], rtol=1e-4, atol=1e-5)
