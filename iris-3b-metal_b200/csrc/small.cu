@@ -59,11 +59,14 @@ __global__ void timestep_kernel(const float* __restrict__ t, float* __restrict__
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t b = i / half;
     const int k = static_cast<int>(i % half);
-    // exp(-ln(max_period) * k / n), then the fp32 product with t, as the reference evaluates it
-    const float freq = expf(-log_period * static_cast<float>(k) / static_cast<float>(half));
+    // the fp32 argument -ln(max_period) * k / n as the reference forms it; exp,
+    // cos and sin evaluated in double and rounded once, so phases of up to
+    // 1000 rad match the reference's fp32 values to the last ulp
+    const float arg = (-log_period * static_cast<float>(k)) / static_cast<float>(half);
+    const float freq = static_cast<float>(exp(static_cast<double>(arg)));
     const float phase = t[b] * freq;
-    out[b * 2 * half + k] = cosf(phase);
-    out[b * 2 * half + half + k] = sinf(phase);
+    out[b * 2 * half + k] = static_cast<float>(cos(static_cast<double>(phase)));
+    out[b * 2 * half + half + k] = static_cast<float>(sin(static_cast<double>(phase)));
   }
 }
 

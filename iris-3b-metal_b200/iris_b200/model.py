@@ -319,7 +319,8 @@ class CudaIris:
         ws = {
             "tokens": e(batch * N, d, dtype=torch.float32),
             "patches": e(batch * L, self.s_embed[0].shape[1]),
-            "h": e(batch * N, d),
+            "h": e(batch * N, d),  # dual-stream branch inputs (text rows, then image rows)
+            "hj": e(batch * N, d),  # single-stream branch inputs ([text | image] per sample)
             "h2": e(batch * N, d),
             "qkv": e(batch * N, wq),
             "q": e(batch, hq, N, HEAD_DIM),
@@ -355,9 +356,16 @@ class CudaIris:
 
     # -- forward ----------------------------------------------------------------------
     @torch.no_grad()
-    def __call__(self, x: torch.Tensor, t: torch.Tensor, text: torch.Tensor) -> torch.Tensor:
+    def __call__(
+        self, x: torch.Tensor, t: torch.Tensor, text: torch.Tensor, capture: dict | None = None
+    ) -> torch.Tensor:
         """``x``: ``[B, 3, H, W]``; ``t``: model time ``[B]``; ``text``: ``[B, T, D]``
-        from :meth:`encode_text`. Returns the FP32 velocity ``[B, 3, H, W]``."""
+        from :meth:`encode_text`. Returns the FP32 velocity ``[B, 3, H, W]``.
+
+        ``capture`` (diagnostics only): when a dict is given, copies of the image
+        tokens after every block (``block{i}``), ``s_cond``, the embedded pixels
+        (``pixels_in``) and the pixel stream after every pixel block but the last
+        are stored in it."""
         cfg = self.cfg
         p = cfg.patch_size
         batch, channels, height, width = x.shape
@@ -411,10 +419,14 @@ class CudaIris:
                 self._dual_block(block, nxt, ws, geom, cos, sin, eps, st)
             else:
                 self._single_block(block, nxt, ws, geom, cos, sin, eps, st)
+            if capture is not None:
+                capture[f"block{i}"] = tokens.view(batch, N, d)[:, T:].clone()
+        if capture is not None:
+            capture["s_cond"] = ws["s_cond"].float().clone()
 
         # pixel stage
         v = torch.empty(batch, channels, height, width, device=dev, dtype=torch.float32)
-        self._pixel_stage(x, ws, geom, grid, pcos, psin, pos, v, eps, st)
+        self._pixel_stage(x, ws, geom, grid, pcos, psin, pos, v, eps, st, capture)
         return v
 
     # -- trunk --------------------------------------------------------------------------
@@ -439,7 +451,7 @@ class CudaIris:
         for stream, rows, rpb, tmap, off in self._segments(block, g):
             mods = self._mods(ws, block, stream)
             _lib.call(
-                "iris_rms_norm_modulate", ws["tokens"].data_ptr(), _lib.F32, *tmap, ws["h"][off:].data_ptr(), _lib.BF16,
+                "iris_rms_norm_modulate", ws["tokens"].data_ptr(), _lib.F32, *tmap, ws[_hkey(block)][off:].data_ptr(), _lib.BF16,
                 block.norms[stream]["norm1"].data_ptr(), self._chunk(mods, 0, g.d), self._chunk(mods, 1, g.d), 6 * g.d,
                 rows, rpb, g.d, eps, st,
             )  # fmt: skip
@@ -464,7 +476,7 @@ class CudaIris:
     def _single_block(self, block, nxt, ws, g, cos, sin, eps, st) -> None:
         cfg = self.cfg
         rows = g.batch * g.N
-        K.gemm(ws["h"], block.qkv["j"], ws["qkv"])
+        K.gemm(ws["hj"], block.qkv["j"], ws["qkv"])
         qn, kn = block.qk_norm["j"]
         _lib.call(
             "iris_qkv_heads", ws["qkv"].data_ptr(), g.batch, g.N, block.qkv["j"].shape[0], cfg.num_heads, cfg.kv_heads,
@@ -479,7 +491,7 @@ class CudaIris:
         d = g.d
         mods = self._mods(ws, block, stream)
         norms = block.norms[stream]
-        h, h2 = ws["h"][off : off + rows], ws["h2"][off : off + rows]
+        h, h2 = ws[_hkey(block)][off : off + rows], ws["h2"][off : off + rows]
         gbuf, branch = ws["g"][off : off + rows], ws["branch"][off : off + rows]
         # attention output rows of this stream live in the joint [B, N, D] tensor
         aux_rows = tmap if stream != "j" else (rows, 0, 0)
@@ -514,7 +526,8 @@ class CudaIris:
             next_out = ws["h"][off:]
         else:
             next_map = tmap if stream != "j" else (rows, 0, 0)
-            next_out = ws["h"]
+            # a separate buffer: the other stream of this dual block may still read ws["h"]
+            next_out = ws["hj"]
         _lib.call(
             "iris_gated_residual_rms_norm", tok, *tmap, branch.data_ptr(), _lib.BF16, rows, 0, 0,
             norms["post_mlp"].data_ptr(), self._chunk(mods, 5, d), 6 * d, rows, rpb, d, eps, _lib.NEXT_NORM_MODULATE,
@@ -523,7 +536,7 @@ class CudaIris:
         )  # fmt: skip
 
     # -- pixel stage ------------------------------------------------------------------
-    def _pixel_stage(self, x, ws, g, grid, pcos, psin, pos, v, eps, st) -> None:
+    def _pixel_stage(self, x, ws, g, grid, pcos, psin, pos, v, eps, st, capture=None) -> None:
         cfg = self.cfg
         pix = cfg.pixel
         p = cfg.patch_size
@@ -537,7 +550,11 @@ class CudaIris:
             width, p, st,
         )  # fmt: skip
         heads = pix.num_heads
+        if capture is not None:
+            capture["pixels_in"] = ws["pixels"].float().view(g.batch * g.L, -1, pix.hidden_size).clone()
         for i, blk in enumerate(blocks):
+            if capture is not None and i > 0:
+                capture[f"pixel_block{i - 1}"] = ws["pixels"].float().view(g.batch * g.L, -1, pix.hidden_size).clone()
             K.gemm(ws["s_cond"], blk["adaln"][0], ws["pmods"], bias=blk["adaln"][1])
             K.gemm(ws["ph"], blk["compress"][0], ws["comp"], bias=blk["compress"][1])
             K.gemm(ws["comp"], blk["qkv"], ws["pqkv"])
@@ -565,6 +582,11 @@ class CudaIris:
                     b2.data_ptr(), fn.data_ptr(), fw.data_ptr(), fb.data_ptr(), v.data_ptr(), g.batch, height, width,
                     p, eps, st,
                 )  # fmt: skip
+
+
+def _hkey(block: _Block) -> str:
+    """Workspace key of a block's branch-input buffer."""
+    return "h" if block.dual else "hj"
 
 
 @dataclass

@@ -288,7 +288,8 @@ def test_timestep_gemv_and_cfg_euler(K):
     feats = torch.empty(5, 256, device="cuda")
     tc = t.cuda()
     _lib.call("iris_timestep_embedding", tc.data_ptr(), feats.data_ptr(), 5, 256, 10.0, st)
-    torch.testing.assert_close(feats.cpu(), ops.timestep_embedding(t, 256, 10.0), rtol=1e-5, atol=2e-5)
+    # phases reach 1000 rad, whose fp32 ulp is 6.1e-5: allow 2.5 ulp of phase
+    torch.testing.assert_close(feats.cpu(), ops.timestep_embedding(t, 256, 10.0), rtol=1e-5, atol=1.5e-4)
     gen = torch.Generator(device="cuda").manual_seed(1)
     x = torch.randn(5, 512, device="cuda", generator=gen)
     w = torch.randn(384, 512, device="cuda", generator=gen) * 0.05
