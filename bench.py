@@ -206,6 +206,36 @@ def reference_arm(args, rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def profile_run(kind: str) -> None:
+    """Workloads for ncu: two warm B = 2 denoiser calls at 1024^2, then one call
+    inside the NVTX range ``profiled`` (select it with ``--nvtx --nvtx-include
+    profiled/``). ``forward``: the benchmark model. ``small``: the same shapes
+    with one dual and one single-stream block and one pixel block (< 1 GB of
+    weights), for multi-pass captures."""
+    from dataclasses import replace
+
+    from iris_b200 import CudaIris, IrisWeights, baseline_step_config, synthetic_state
+    from iris_b200.config import PixelStageConfig
+
+    cfg = baseline_step_config()
+    if kind == "small":
+        cfg = replace(cfg, depth=2, dual_depth=1, pixel=PixelStageConfig(depth=1))
+    device = torch.device("cuda", 0)
+    engine = CudaIris(IrisWeights(cfg, synthetic_state(cfg, device, seed=0)))
+    noise, cond_states, uncond_states = make_inputs()
+    x = noise[:1].repeat(2, 1, 1, 1).to(device)
+    text = torch.cat([engine.encode_text(uncond_states.to(device)), engine.encode_text(cond_states[:1].to(device))])
+    t = torch.full((2,), 625.0, device=device)
+    for _ in range(2):
+        engine(x, t, text)
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("profiled")
+    v = engine(x, t, text)
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    print(json.dumps({"profile": kind, "finite": bool(torch.isfinite(v).all())}))
+
+
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--gpus", type=int, default=1)
@@ -213,10 +243,14 @@ def main() -> None:
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", default="ours", choices=["ours", "reference"])
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--profile", choices=["forward", "small"], help="one NVTX-marked B=2 call for ncu")
     args = parser.parse_args()
     from iris_b200.parallel import env_world, gather_images, image_shard, init_process_group  # noqa: F401
 
     rank, world, local = env_world()
+    if args.profile:
+        profile_run(args.profile)
+        return
     if args.impl == "reference":
         reference_arm(args, rank)
         return
