@@ -3,41 +3,43 @@
 // (src/iris_metal/model.py:243-250; src/iris3b/nn/attention.py:61-91) and the
 // pixel-stage patch tokens (src/iris3b/models/blocks/pit.py:66-72).
 //
-// One CTA per (128-query tile, head, batch). Warp roles:
-//   warp 0      TMA: Q once (two 64-dim halves, 128B swizzle), then K_j and V_j
-//               (128 keys each) into 2-stage rings;
-//   warp 1      TMEM allocator + MMA issuer (one thread):
-//                 S[j % 2]  = Q K_j^T          (SS MMA, M=N=128, K=128)
-//                 O        += P[j % 2] V_j     (TS MMA, P read from TMEM)
-//               S_{j+1} is issued before O += P_j V_j so the tensor pipe
-//               works on the next scores while the softmax warps run;
-//   warps 2..5  softmax, one query row per thread (TMEM lane = row): load the
-//               row of S, running max / sum in fp32 (exp2 domain), write P as
-//               packed bf16 into TMEM; rescale O in TMEM only when the row max
-//               grew by more than 2^8 (the stale max is exact at the end since
-//               O and l share it); final O / l -> bf16 -> [b, n, h*128 + d].
-// TMEM: S0 [0,128) S1 [128,256) O [256,384) P0 [384,448) P1 [448,512).
+// One CTA per (256 queries = two 128-row tiles, head, batch). Warp roles:
+//   warp 0      TMA: both Q tiles once (two 64-dim halves each, 128B swizzle),
+//               then K_j and V_j (128 keys each) into 2-stage rings;
+//   warp 1      TMEM allocator + MMA issuer (one thread). Per key block j the
+//               tensor pipe runs, in order,
+//                 O_0 += P_0 V_j,  S_0 = Q_0 K_{j+1}^T,  O_1 += P_1 V_j,  S_1 = Q_1 K_{j+1}^T
+//               so one tile's softmax overlaps the other tile's MMAs;
+//   warps 2..5  softmax of tile 0, warps 6..9 softmax of tile 1: one query row
+//               per thread (TMEM lane = row); running max / sum in fp32 in the
+//               exp2 domain; P is written as packed bf16 over the first 64
+//               columns of its own S in TMEM (read by the next TS MMA, which
+//               completes before the following S MMA overwrites them: the MMAs
+//               of one thread execute in issue order); O is rescaled in TMEM only
+//               when a row max grew by more than 2^8 (O and l share the stale
+//               max, so the result is exact); final O / l -> bf16 [b, n, h*128+d].
+// TMEM: S_0 [0,128) S_1 [128,256) O_0 [256,384) O_1 [384,512).
 #include "common.cuh"
 #include "iris_abi_internal.h"
 
 namespace iris {
 namespace attn {
 
-constexpr int BQ = 128;
+constexpr int BQ = 128;       // rows per query tile
+constexpr int TILES = 2;      // query tiles per CTA
 constexpr int BKV = 128;
 constexpr int D = 128;
 constexpr int HALF_BYTES = 128 * 64 * 2;  // 128 rows x 64 dims, 16 KB
 constexpr int TILE_BYTES = 2 * HALF_BYTES;  // 32 KB
-constexpr int THREADS = 192;
-constexpr uint32_t COL_S = 0, COL_O = 256, COL_P = 384;
+constexpr int THREADS = 64 + TILES * 128;   // 320
+constexpr uint32_t COL_S = 0, COL_O = 256;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
-constexpr size_t SMEM_BYTES = 1024 + 5 * TILE_BYTES + 256;
+constexpr size_t SMEM_BYTES = 1024 + (TILES + 4) * TILE_BYTES + 256;
 
 struct Smem {
   uint64_t q_full;
   uint64_t k_full[2], k_free[2], v_full[2], v_free[2];
-  uint64_t s_full[2], s_free[2], p_full[2];
-  uint64_t o_done;
+  uint64_t s_full[TILES], p_full[TILES], o_final[TILES];
   uint64_t teardown;
   uint32_t tmem_base;
   int abort;
@@ -60,20 +62,20 @@ __global__ void __launch_bounds__(THREADS, 1)
                       const __grid_constant__ CUtensorMap tv, const Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* q_tile = base;
-  uint8_t* k_tile = base + TILE_BYTES;      // 2 stages
-  uint8_t* v_tile = base + 3 * TILE_BYTES;  // 2 stages
-  Smem* s = reinterpret_cast<Smem*>(base + 5 * TILE_BYTES);
+  uint8_t* q_tile = base;                             // TILES x 32 KB
+  uint8_t* k_tile = base + TILES * TILE_BYTES;        // 2 stages
+  uint8_t* v_tile = base + (TILES + 2) * TILE_BYTES;  // 2 stages
+  Smem* s = reinterpret_cast<Smem*>(base + (TILES + 4) * TILE_BYTES);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int q_tile_idx = blockIdx.x;
   const int h = blockIdx.y;
   const int b = blockIdx.z;
   const int group = static_cast<int>(p.heads_q / p.heads_kv);
   const int hk = h / group;
   const int n = static_cast<int>(p.n);
   const int nkv = (n + BKV - 1) / BKV;
-  const int q_row0 = static_cast<int>((static_cast<int64_t>(b) * p.heads_q + h) * n) + q_tile_idx * BQ;
+  const int q0 = blockIdx.x * (TILES * BQ);  // first query of the CTA
+  const int q_row0 = static_cast<int>((static_cast<int64_t>(b) * p.heads_q + h) * n) + q0;
   const int kv_row0 = static_cast<int>((static_cast<int64_t>(b) * p.heads_kv + hk) * n);
 
   if (threadIdx.x == 0) {
@@ -83,11 +85,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&s->k_free[i], 1);
       mbar_init(&s->v_full[i], 1);
       mbar_init(&s->v_free[i], 1);
-      mbar_init(&s->s_full[i], 1);
-      mbar_init(&s->s_free[i], 4);
-      mbar_init(&s->p_full[i], 4);
     }
-    mbar_init(&s->o_done, 1);
+    for (int t = 0; t < TILES; ++t) {
+      mbar_init(&s->s_full[t], 1);
+      mbar_init(&s->p_full[t], 4);
+      mbar_init(&s->o_final[t], 1);
+    }
     mbar_init(&s->teardown, 1);
     s->abort = 0;
     fence_barrier_init();
@@ -105,9 +108,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       tma_prefetch_desc(&tq);
       tma_prefetch_desc(&tk);
       tma_prefetch_desc(&tv);
-      mbar_arrive_expect_tx(&s->q_full, TILE_BYTES);
-      tma_load_2d(&tq, &s->q_full, q_tile, 0, q_row0);
-      tma_load_2d(&tq, &s->q_full, q_tile + HALF_BYTES, 64, q_row0);
+      mbar_arrive_expect_tx(&s->q_full, TILES * TILE_BYTES);
+      for (int t = 0; t < TILES; ++t) {
+        tma_load_2d(&tq, &s->q_full, q_tile + t * TILE_BYTES, 0, q_row0 + t * BQ);
+        tma_load_2d(&tq, &s->q_full, q_tile + t * TILE_BYTES + HALF_BYTES, 64, q_row0 + t * BQ);
+      }
       int issued_k[2] = {-1, -1}, issued_v[2] = {-1, -1};
       bool ok = true;
       for (int j = 0; j < nkv && ok; ++j) {
@@ -139,43 +144,53 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       const uint32_t idesc_s = idesc_bf16_f32(BQ, BKV);
       const uint32_t idesc_o = idesc_bf16_f32(BQ, D, false, true);  // V is MN-major (dims contiguous)
-      const uint32_t q_addr = smem_addr(q_tile);
-      bool ok = mbar_wait(&s->q_full, 0, abort);
-      // S_j = Q K_j^T into S[j % 2]
-      auto issue_s = [&](int j) -> bool {
-        const int st = j & 1;
-        const uint32_t ph = static_cast<uint32_t>((j >> 1) & 1);
-        if (!mbar_wait(&s->k_full[st], ph, abort)) return false;
-        if (!mbar_wait(&s->s_free[st], ph ^ 1u, abort)) return false;
-        tc_fence_after();
-        const uint32_t k_addr = smem_addr(k_tile + st * TILE_BYTES);
+      // S_t = Q_t K_j^T into S_t
+      auto issue_s = [&](int t, int j) {
+        const uint32_t q_addr = smem_addr(q_tile + t * TILE_BYTES);
+        const uint32_t k_addr = smem_addr(k_tile + (j & 1) * TILE_BYTES);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * HALF_BYTES + (kk & 3) * 32;
           const uint64_t ad = umma_desc(q_addr + off, 16, 1024, kLayoutSw128);
           const uint64_t bd = umma_desc(k_addr + off, 16, 1024, kLayoutSw128);
-          umma_ss(tmem + COL_S + st * BKV, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+          umma_ss(tmem + COL_S + t * BKV, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
         }
-        umma_commit(&s->s_full[st]);
-        umma_commit(&s->k_free[st]);
-        return true;
+        umma_commit(&s->s_full[t]);
       };
-      if (ok) ok = issue_s(0);
-      for (int j = 0; j < nkv && ok; ++j) {
-        if (j + 1 < nkv && !issue_s(j + 1)) { ok = false; break; }
-        const int st = j & 1;
-        const uint32_t ph = static_cast<uint32_t>((j >> 1) & 1);
-        if (!mbar_wait(&s->p_full[st], ph, abort) || !mbar_wait(&s->v_full[st], ph, abort)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t v_addr = smem_addr(v_tile + st * TILE_BYTES);
+      // O_t += P_t V_j, P_t packed bf16 in the first 64 columns of S_t
+      auto issue_pv = [&](int t, int j) {
+        const uint32_t v_addr = smem_addr(v_tile + (j & 1) * TILE_BYTES);
 #pragma unroll
         for (int kk = 0; kk < BKV / 16; ++kk) {
-          // 16 keys per MMA: 16 rows of 128 B in the swizzled V tile, 8 packed P columns
           const uint64_t bd = umma_desc(v_addr + kk * 16 * 128, HALF_BYTES, 1024, kLayoutSw128);
-          umma_ts(tmem + COL_O, tmem + COL_P + st * 64 + kk * 8, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          umma_ts(tmem + COL_O + t * D, tmem + COL_S + t * BKV + kk * 8, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&s->o_done);
+      };
+      bool ok = mbar_wait(&s->q_full, 0, abort) && mbar_wait(&s->k_full[0], 0, abort);
+      if (ok) {
+        tc_fence_after();
+        for (int t = 0; t < TILES; ++t) issue_s(t, 0);
+        umma_commit(&s->k_free[0]);
+      }
+      for (int j = 0; j < nkv && ok; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = static_cast<uint32_t>((j >> 1) & 1);
+        const bool more = j + 1 < nkv;
+        if (!mbar_wait(&s->v_full[st], ph, abort)) { ok = false; break; }
+        if (more && !mbar_wait(&s->k_full[(j + 1) & 1], static_cast<uint32_t>(((j + 1) >> 1) & 1), abort)) {
+          ok = false;
+          break;
+        }
+        for (int t = 0; t < TILES; ++t) {
+          if (!mbar_wait(&s->p_full[t], static_cast<uint32_t>(j & 1), abort)) { ok = false; break; }
+          tc_fence_after();
+          issue_pv(t, j);
+          if (!more) umma_commit(&s->o_final[t]);
+          if (more) issue_s(t, j + 1);
+        }
+        if (!ok) break;
         umma_commit(&s->v_free[st]);
+        if (more) umma_commit(&s->k_free[(j + 1) & 1]);
       }
       umma_commit(&s->teardown);
       int dummy = 0;
@@ -183,71 +198,50 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------- softmax
+    const int tile = (warp - 2) / 4;
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t s_col = COL_S + tile * BKV, o_col = COL_O + tile * D;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
-      const int st = j & 1;
-      const uint32_t ph = static_cast<uint32_t>((j >> 1) & 1);
-      if (!__all_sync(0xffffffffu, mbar_wait(&s->s_full[st], ph, abort))) { ok = false; break; }
+      if (!__all_sync(0xffffffffu, mbar_wait(&s->s_full[tile], static_cast<uint32_t>(j & 1), abort))) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       float sv[BKV];
       {
-        uint32_t r[32];
+        uint32_t r[4][32];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          tmem_ld32(tmem + lane_addr + COL_S + st * BKV + c * 32, r);
-          tmem_wait_ld();
+        for (int c = 0; c < 4; ++c) tmem_ld32(tmem + lane_addr + s_col + c * 32, r[c]);
+        tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 32; ++e) sv[c * 32 + e] = __uint_as_float(r[e]);
-        }
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) sv[c * 32 + e] = __uint_as_float(r[c][e]);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s->s_free[st]);
-      // scores in log2 units, keys past the sequence end masked out
       const int valid = n - j * BKV;
+      if (valid < BKV) {  // last key block: keys past the sequence end do not exist
+#pragma unroll
+        for (int e = 0; e < BKV; ++e)
+          if (e >= valid) sv[e] = -INFINITY;
+      }
       float mx = -INFINITY;
 #pragma unroll
-      for (int e = 0; e < BKV; ++e) {
-        sv[e] = e < valid ? sv[e] * p.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, sv[e]);
-      }
-      const bool grow = mx > m_run + RESCALE_THRESHOLD;
-      const bool rescale = __any_sync(0xffffffffu, grow) && j > 0;
-      float m_new = m_run;
-      if (grow || j == 0) m_new = fmaxf(m_run, mx);
-      if (rescale && !grow) m_new = m_run;  // this row keeps its max; the warp rescales O together
-      const float corr = (j == 0) ? 0.f : ex2(m_run - m_new);
-      float rs = 0.f;
-      // PV_{j-1} must be done before O is rescaled or P[st] (read by PV_{j-2}) is overwritten
-      if (j > 0) {
-        if (!__all_sync(0xffffffffu, mbar_wait(&s->o_done, static_cast<uint32_t>((j - 1) & 1), abort))) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-      }
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const float p0 = ex2(sv[c * 32 + 2 * e] - m_new);
-          const float p1 = ex2(sv[c * 32 + 2 * e + 1] - m_new);
-          rs += p0 + p1;
-          pk[e] = pack_bf16x2(p0, p1);
-        }
-        tmem_st16(tmem + lane_addr + COL_P + st * 64 + c * 16, pk);
-      }
-      l_run = (j == 0) ? rs : l_run * corr + rs;
-      if (rescale) {
-#pragma unroll
+      for (int e = 0; e < BKV; ++e) mx = fmaxf(mx, sv[e]);
+      mx *= p.scale_log2;
+      // lazy rescale: keep the stale max unless it grew by more than 2^8
+      const bool grow = j == 0 || mx > m_run + RESCALE_THRESHOLD;
+      const float m_new = grow ? fmaxf(m_run, mx) : m_run;
+      const float corr = ex2(m_run - m_new);  // 0 on the first block
+      if (j > 0 && __any_sync(0xffffffffu, grow)) {
+        // O_t holds the P V of earlier blocks: S_t(j) completing implies they completed
+#pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t r[32];
-          tmem_ld32(tmem + lane_addr + COL_O + c * 32, r);
+          tmem_ld32(tmem + lane_addr + o_col + c * 32, r);
           tmem_wait_ld();
           uint32_t lo[16], hi[16];
 #pragma unroll
@@ -255,25 +249,39 @@ __global__ void __launch_bounds__(THREADS, 1)
             lo[e] = __float_as_uint(__uint_as_float(r[e]) * corr);
             hi[e] = __float_as_uint(__uint_as_float(r[16 + e]) * corr);
           }
-          tmem_st16(tmem + lane_addr + COL_O + c * 32, lo);
-          tmem_st16(tmem + lane_addr + COL_O + c * 32 + 16, hi);
+          tmem_st16(tmem + lane_addr + o_col + c * 32, lo);
+          tmem_st16(tmem + lane_addr + o_col + c * 32 + 16, hi);
         }
       }
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float p0 = ex2(fmaf(sv[c * 32 + 2 * e], p.scale_log2, -m_new));
+          const float p1 = ex2(fmaf(sv[c * 32 + 2 * e + 1], p.scale_log2, -m_new));
+          rs += p0 + p1;
+          pk[e] = pack_bf16x2(p0, p1);
+        }
+        tmem_st16(tmem + lane_addr + s_col + c * 16, pk);
+      }
+      l_run = l_run * corr + rs;
       m_run = m_new;
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&s->p_full[st]);
+      if (lane == 0) mbar_arrive(&s->p_full[tile]);
     }
-    if (ok && __all_sync(0xffffffffu, mbar_wait(&s->o_done, static_cast<uint32_t>((nkv - 1) & 1), abort))) {
+    if (ok && __all_sync(0xffffffffu, mbar_wait(&s->o_final[tile], 0, abort))) {
       tc_fence_after();
-      const int q = q_tile_idx * BQ + row;
+      const int q = q0 + tile * BQ + row;
       const float inv = 1.f / l_run;
       __nv_bfloat16* dst = p.o + (static_cast<int64_t>(b) * p.n + q) * p.o_row_stride + static_cast<int64_t>(h) * D;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t r[32];
-        tmem_ld32(tmem + lane_addr + COL_O + c * 32, r);
+        tmem_ld32(tmem + lane_addr + o_col + c * 32, r);
         tmem_wait_ld();
         if (q < n) {
           uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
@@ -332,7 +340,9 @@ extern "C" int iris_flash_attn_fwd(const void* q, const void* k, const void* v, 
                                    static_cast<int>(SMEM_BYTES)));
     configured[dev] = true;
   }
-  dim3 grid(static_cast<unsigned>((n + BQ - 1) / BQ), static_cast<unsigned>(heads_q), static_cast<unsigned>(batch));
+  const int per_cta = TILES * BQ;
+  dim3 grid(static_cast<unsigned>((n + per_cta - 1) / per_cta), static_cast<unsigned>(heads_q),
+            static_cast<unsigned>(batch));
   flash_attn_kernel<<<grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
   IRIS_CUDA(cudaGetLastError());
   return IRIS_OK;
