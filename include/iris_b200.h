@@ -111,6 +111,29 @@ int iris_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw, void*
                    int64_t out_seg_rows, int64_t out_seg_stride, int64_t out_seg_offset, int64_t aux_seg_rows,
                    int64_t aux_seg_stride, int64_t aux_seg_offset, void* stream);
 
+/* One problem of a grouped launch: the arguments of iris_gemm_bf16 as plain data. */
+typedef struct iris_gemm_problem {
+  const void* a;
+  int64_t lda;
+  const void* w;
+  int64_t ldw;
+  void* out;
+  int out_dtype;
+  int64_t ldc;
+  int64_t M, N, K;
+  int epilogue;
+  const float* bias;
+  const void* aux;
+  int64_t ldaux;
+  int64_t out_seg_rows, out_seg_stride, out_seg_offset;
+  int64_t aux_seg_rows, aux_seg_stride, aux_seg_offset;
+} iris_gemm_problem;
+
+/* 1 to 4 independent GEMMs in one persistent launch (the text- and
+ * image-stream linears of a dual block, src/iris_metal/model.py:277-289:
+ * same op, separate weights); their output tiles share one tile list. */
+int iris_gemm_bf16_grouped(const iris_gemm_problem* problems, int count, void* stream);
+
 /* F.scaled_dot_product_attention, non-causal, unmasked
  * (src/iris_metal/model.py:243-250, src/iris3b/nn/attention.py:61-91):
  * q [b, heads_q, n, 128], k/v [b, heads_kv, n, 128] bf16 contiguous;
@@ -118,6 +141,17 @@ int iris_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw, void*
 int iris_flash_attn_fwd(const void* q, const void* k, const void* v, void* o, int64_t batch, int64_t heads_q,
                         int64_t heads_kv, int64_t n, int64_t head_dim, float scale, int64_t o_row_stride,
                         void* stream);
+
+/* The same attention with the block's sigmoid gate applied and each stream's
+ * rows written densely (src/iris_metal/model.py:281-283,309): token i < split
+ * of sample b goes to row b * split + i of o_text, token i >= split to row
+ * b * (n - split) + i - split of o_image; o = attn * sigmoid(gate logit), the
+ * bf16 logits read from the same rows of gate_text / gate_image (both null:
+ * no gate). split = 0 writes every token to o_image. */
+int iris_flash_attn_fwd_split(const void* q, const void* k, const void* v, int64_t batch, int64_t heads_q,
+                              int64_t heads_kv, int64_t n, int64_t head_dim, float scale, int64_t split, void* o_text,
+                              void* o_image, const void* gate_text, const void* gate_image, int64_t row_stride,
+                              void* stream);
 
 /* ---- pixel stage -------------------------------------------------------- */
 /* pixel_rms_norm, src/iris_metal/kernels.py:486-498 (MSL :217-232): bf16 out. */

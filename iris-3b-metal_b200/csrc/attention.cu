@@ -46,9 +46,12 @@ struct Smem {
 };
 
 struct Params {
-  int64_t batch, heads_q, heads_kv, n, o_row_stride;
+  int64_t batch, heads_q, heads_kv, n, row_stride, split;
   float scale_log2;
-  __nv_bfloat16* o;
+  __nv_bfloat16* o_text;   // rows b * split + i       (i < split)
+  __nv_bfloat16* o_image;  // rows b * (n - split) + i - split
+  const __nv_bfloat16* gate_text;  // bf16 gate logits in the same rows, or null
+  const __nv_bfloat16* gate_image;
 };
 
 IRIS_DEVICE float ex2(float x) {
@@ -56,6 +59,69 @@ IRIS_DEVICE float ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+
+// Packed FP32 pair arithmetic (sm_100 f32x2 instructions): one issue, two lanes of work.
+IRIS_DEVICE float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+IRIS_DEVICE float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.f32x2 rd, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+IRIS_DEVICE float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x on the FMA pipe for x >= -126 (a share of the softmax exponentials, so
+// the MUFU unit is not the only source of them). Range reduction: adding
+// 1.5 * 2^23 rounds x to the nearest integer j, left in the low mantissa bits
+// of t; f = x - j lies in [-0.5, 0.5]. 2^f is a degree-3 polynomial whose
+// coefficients were fitted to 2^f on [-0.5, 0.5] by iteratively reweighted
+// least squares on the relative error (Lawson's algorithm; max relative error
+// 7.5e-5, far below the bf16 rounding of P). 2^j is added to the exponent field
+// as (bits of t) << 23, which equals j << 23 modulo 2^32.
+IRIS_DEVICE float2 exp2_poly2(float2 x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  x.x = fmaxf(x.x, -126.f);
+  x.y = fmaxf(x.y, -126.f);
+  const float2 t = add2(x, make_float2(kRound, kRound));
+  const float2 j = add2(t, make_float2(-kRound, -kRound));
+  const float2 f = fma2(j, make_float2(-1.f, -1.f), x);
+  float2 p = fma2(f, make_float2(0.0551716685295105f, 0.0551716685295105f),
+                  make_float2(0.2426111400127411f, 0.2426111400127411f));
+  p = fma2(p, f, make_float2(0.6932609677314758f, 0.6932609677314758f));
+  p = fma2(p, f, make_float2(0.9999280571937561f, 0.9999280571937561f));
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+}
+// Of every 16 exponential pairs, how many exp2_poly2 computes (the rest go to
+// MUFU). The polynomial costs ~6 issue slots per element against 1 for MUFU,
+// so it only pays when the MUFU pipe, not issue, limits the softmax.
+#ifndef IRIS_ATTN_EMU_PAIRS
+#define IRIS_ATTN_EMU_PAIRS 0
+#endif
+constexpr int EMU_PAIRS = IRIS_ATTN_EMU_PAIRS;
+// 1: scale/shift and row sums as packed f32x2 instructions; 0: scalar FFMA/FADD.
+#ifndef IRIS_ATTN_PACKED
+#define IRIS_ATTN_PACKED 1
+#endif
 
 __global__ void __launch_bounds__(THREADS, 1)
     flash_attn_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
@@ -211,27 +277,33 @@ __global__ void __launch_bounds__(THREADS, 1)
         break;
       }
       tc_fence_after();
-      float sv[BKV];
-      {
-        uint32_t r[4][32];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld32(tmem + lane_addr + s_col + c * 32, r[c]);
-        tmem_wait_ld();
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-          for (int e = 0; e < 32; ++e) sv[c * 32 + e] = __uint_as_float(r[c][e]);
-      }
+      // Two passes over the scores in TMEM keep ~64 of them in registers at a
+      // time: pass 1 the row max, pass 2 exp / sum / pack per 32-column chunk.
       const int valid = n - j * BKV;
-      if (valid < BKV) {  // last key block: keys past the sequence end do not exist
+      const bool tail = valid < BKV;  // last key block: keys past the sequence end do not exist
+      float mx;
+      {
+        uint32_t r[32];
+        float ma = -INFINITY, mb = -INFINITY, mc = -INFINITY, md = -INFINITY;
 #pragma unroll
-        for (int e = 0; e < BKV; ++e)
-          if (e >= valid) sv[e] = -INFINITY;
+        for (int c = 0; c < 4; ++c) {
+          tmem_ld32(tmem + lane_addr + s_col + c * 32, r);
+          tmem_wait_ld();
+          if (tail) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (c * 32 + e >= valid) r[e] = __float_as_uint(-INFINITY);
+          }
+#pragma unroll
+          for (int e = 0; e < 32; e += 8) {
+            ma = max3(ma, __uint_as_float(r[e]), __uint_as_float(r[e + 1]));
+            mb = max3(mb, __uint_as_float(r[e + 2]), __uint_as_float(r[e + 3]));
+            mc = max3(mc, __uint_as_float(r[e + 4]), __uint_as_float(r[e + 5]));
+            md = max3(md, __uint_as_float(r[e + 6]), __uint_as_float(r[e + 7]));
+          }
+        }
+        mx = fmaxf(max3(ma, mb, mc), md) * p.scale_log2;
       }
-      float mx = -INFINITY;
-#pragma unroll
-      for (int e = 0; e < BKV; ++e) mx = fmaxf(mx, sv[e]);
-      mx *= p.scale_log2;
       // lazy rescale: keep the stale max unless it grew by more than 2^8
       const bool grow = j == 0 || mx > m_run + RESCALE_THRESHOLD;
       const float m_new = grow ? fmaxf(m_run, mx) : m_run;
@@ -253,45 +325,100 @@ __global__ void __launch_bounds__(THREADS, 1)
           tmem_st16(tmem + lane_addr + o_col + c * 32 + 16, hi);
         }
       }
-      float rs = 0.f;
+      const float2 scale2 = make_float2(p.scale_log2, p.scale_log2);
+      const float2 shift2 = make_float2(-m_new, -m_new);
+      float2 rs2 = make_float2(0.f, 0.f);
+      // chunk c + 1 is loaded while chunk c is processed; P of chunk c goes to
+      // columns [16c, 16c + 16), whose scores were read by an earlier chunk
+      uint32_t buf[2][32];
+      tmem_ld32(tmem + lane_addr + s_col, buf[0]);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
+        tmem_wait_ld();
+        if (c + 1 < 4) tmem_ld32(tmem + lane_addr + s_col + (c + 1) * 32, buf[(c + 1) & 1]);
+        uint32_t(&r)[32] = buf[c & 1];
+        if (tail) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (c * 32 + e >= valid) r[e] = __float_as_uint(-INFINITY);
+        }
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const float p0 = ex2(fmaf(sv[c * 32 + 2 * e], p.scale_log2, -m_new));
-          const float p1 = ex2(fmaf(sv[c * 32 + 2 * e + 1], p.scale_log2, -m_new));
-          rs += p0 + p1;
-          pk[e] = pack_bf16x2(p0, p1);
+          const float2 s = make_float2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
+#if IRIS_ATTN_PACKED
+          const float2 x = fma2(s, scale2, shift2);
+#else
+          const float2 x = make_float2(fmaf(s.x, scale2.x, shift2.x), fmaf(s.y, scale2.y, shift2.y));
+#endif
+          float2 pe;
+          if (e < EMU_PAIRS && !tail) {
+            pe = exp2_poly2(x);
+          } else {  // MUFU; also every masked key block, where ex2(-inf) gives exact zeros
+            pe.x = ex2(x.x);
+            pe.y = ex2(x.y);
+          }
+#if IRIS_ATTN_PACKED
+          rs2 = add2(rs2, pe);
+#else
+          rs2.x += pe.x;
+          rs2.y += pe.y;
+#endif
+          pk[e] = pack_bf16x2(pe.x, pe.y);
         }
         tmem_st16(tmem + lane_addr + s_col + c * 16, pk);
       }
-      l_run = l_run * corr + rs;
+      l_run = l_run * corr + (rs2.x + rs2.y);
       m_run = m_new;
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s->p_full[tile]);
     }
+    // output row of this query and its gate logits, fetched while the last P V runs
+    const int q = q0 + tile * BQ + row;
+    const bool text = q < p.split;
+    const int64_t orow = text ? static_cast<int64_t>(b) * p.split + q
+                              : static_cast<int64_t>(b) * (p.n - p.split) + (q - p.split);
+    const int64_t off = orow * p.row_stride + static_cast<int64_t>(h) * D;
+    const __nv_bfloat16* gate = text ? p.gate_text : p.gate_image;
+    uint4 gate_row[16];
+    if (gate != nullptr && q < n) {
+      const uint4* g4 = reinterpret_cast<const uint4*>(gate + off);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) gate_row[e] = g4[e];
+    }
     if (ok && __all_sync(0xffffffffu, mbar_wait(&s->o_final[tile], 0, abort))) {
       tc_fence_after();
-      const int q = q0 + tile * BQ + row;
+      __nv_bfloat16* dst = (text ? p.o_text : p.o_image) + off;
       const float inv = 1.f / l_run;
-      __nv_bfloat16* dst = p.o + (static_cast<int64_t>(b) * p.n + q) * p.o_row_stride + static_cast<int64_t>(h) * D;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t r[32];
         tmem_ld32(tmem + lane_addr + o_col + c * 32, r);
         tmem_wait_ld();
         if (q < n) {
+          float val[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) val[e] = __uint_as_float(r[e]) * inv;
+          if (gate != nullptr) {  // out = attn * sigmoid(gate logit), src/iris_metal/model.py:282-283
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const uint4 gv = gate_row[c * 4 + e];
+              const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+              for (int hh = 0; hh < 4; ++hh) {
+                const float2 lg = unpack_bf16x2(gw[hh]);
+                val[8 * e + 2 * hh] *= 1.f / (1.f + __expf(-lg.x));
+                val[8 * e + 2 * hh + 1] *= 1.f / (1.f + __expf(-lg.y));
+              }
+            }
+          }
           uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            d4[e] = make_uint4(pack_bf16x2(__uint_as_float(r[8 * e]) * inv, __uint_as_float(r[8 * e + 1]) * inv),
-                               pack_bf16x2(__uint_as_float(r[8 * e + 2]) * inv, __uint_as_float(r[8 * e + 3]) * inv),
-                               pack_bf16x2(__uint_as_float(r[8 * e + 4]) * inv, __uint_as_float(r[8 * e + 5]) * inv),
-                               pack_bf16x2(__uint_as_float(r[8 * e + 6]) * inv, __uint_as_float(r[8 * e + 7]) * inv));
-          }
+          for (int e = 0; e < 4; ++e)
+            d4[e] = make_uint4(pack_bf16x2(val[8 * e], val[8 * e + 1]), pack_bf16x2(val[8 * e + 2], val[8 * e + 3]),
+                               pack_bf16x2(val[8 * e + 4], val[8 * e + 5]), pack_bf16x2(val[8 * e + 6], val[8 * e + 7]));
         }
       }
     }
@@ -308,17 +435,25 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 using namespace iris;
 
-extern "C" int iris_flash_attn_fwd(const void* q, const void* k, const void* v, void* o, int64_t batch,
-                                   int64_t heads_q, int64_t heads_kv, int64_t n, int64_t head_dim, float scale,
-                                   int64_t o_row_stride, void* stream) {
+extern "C" int iris_flash_attn_fwd_split(const void* q, const void* k, const void* v, int64_t batch,
+                                         int64_t heads_q, int64_t heads_kv, int64_t n, int64_t head_dim, float scale,
+                                         int64_t split, void* o_text, void* o_image, const void* gate_text,
+                                         const void* gate_image, int64_t row_stride, void* stream) {
   using namespace iris::attn;
-  IRIS_REQUIRE(q && k && v && o, "flash_attn_fwd: null pointer");
+  IRIS_REQUIRE(q && k && v && o_image, "flash_attn_fwd: null pointer");
   IRIS_REQUIRE(head_dim == D, "flash_attn_fwd: head_dim must be 128");
   IRIS_REQUIRE(batch > 0 && heads_q > 0 && heads_kv > 0 && heads_q % heads_kv == 0,
                "flash_attn_fwd: heads_q must be a positive multiple of heads_kv");
   IRIS_REQUIRE(n > 0 && batch * heads_q * n < (1ll << 31), "flash_attn_fwd: sequence too long");
-  IRIS_REQUIRE(o_row_stride >= heads_q * D && o_row_stride % 8 == 0, "flash_attn_fwd: o_row_stride");
-  IRIS_REQUIRE(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o), "flash_attn_fwd: alignment");
+  IRIS_REQUIRE(split >= 0 && split <= n && (split == 0 || o_text != nullptr), "flash_attn_fwd: bad split");
+  IRIS_REQUIRE(row_stride >= heads_q * D && row_stride % 8 == 0, "flash_attn_fwd: o_row_stride");
+  IRIS_REQUIRE(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o_image) &&
+                   (o_text == nullptr || aligned16(o_text)),
+               "flash_attn_fwd: alignment");
+  IRIS_REQUIRE(split == 0 || (gate_text == nullptr) == (gate_image == nullptr),
+               "flash_attn_fwd: gate both streams or neither");
+  IRIS_REQUIRE((gate_image == nullptr || aligned16(gate_image)) && (gate_text == nullptr || aligned16(gate_text)),
+               "flash_attn_fwd: gate alignment");
   IRIS_REQUIRE(batch <= 65535 && heads_q <= 65535, "flash_attn_fwd: grid too large");
   CUtensorMap tq, tk, tv;
   IRIS_CHECK_STATUS(make_tmap_2d_bf16(&tq, q, D, batch * heads_q * n, D, 64, BQ));
@@ -329,9 +464,13 @@ extern "C" int iris_flash_attn_fwd(const void* q, const void* k, const void* v, 
   p.heads_q = heads_q;
   p.heads_kv = heads_kv;
   p.n = n;
-  p.o_row_stride = o_row_stride;
+  p.row_stride = row_stride;
+  p.split = split;
   p.scale_log2 = scale * 1.4426950408889634f;
-  p.o = reinterpret_cast<__nv_bfloat16*>(o);
+  p.o_text = reinterpret_cast<__nv_bfloat16*>(o_text);
+  p.o_image = reinterpret_cast<__nv_bfloat16*>(o_image);
+  p.gate_text = reinterpret_cast<const __nv_bfloat16*>(gate_text);
+  p.gate_image = reinterpret_cast<const __nv_bfloat16*>(gate_image);
   static bool configured[64] = {false};
   int dev = 0;
   IRIS_CUDA(cudaGetDevice(&dev));
@@ -346,4 +485,11 @@ extern "C" int iris_flash_attn_fwd(const void* q, const void* k, const void* v, 
   flash_attn_kernel<<<grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
   IRIS_CUDA(cudaGetLastError());
   return IRIS_OK;
+}
+
+extern "C" int iris_flash_attn_fwd(const void* q, const void* k, const void* v, void* o, int64_t batch,
+                                   int64_t heads_q, int64_t heads_kv, int64_t n, int64_t head_dim, float scale,
+                                   int64_t o_row_stride, void* stream) {
+  return iris_flash_attn_fwd_split(q, k, v, batch, heads_q, heads_kv, n, head_dim, scale, 0, nullptr, o, nullptr,
+                                   nullptr, o_row_stride, stream);
 }

@@ -4,7 +4,10 @@
 //
 // This is every Linear of the denoiser step (F.linear in the reference:
 // src/iris_metal/model.py:46-52, SwiGLU :51-52, gate :282-283,309, projections
-// :284-285,310, pixel stage :332-341).
+// :284-285,310, pixel stage :332-341). One launch may run up to four
+// independent problems (the text- and image-stream projections of a dual
+// block, with their own weights): their 128 x 256 output tiles form one
+// persistent tile list, so a small problem fills the last wave of a large one.
 //
 // Per CTA (one per SM, persistent over output tiles of 128 x 256):
 //   warp 0      TMA producer: A and W tiles (64-wide K slabs, 128B swizzle)
@@ -19,9 +22,8 @@
 // Epilogues: STORE (optional bias, fp32 or bf16 out), SWIGLU (each 256-wide
 // W tile holds 128 rows of w1 then the matching 128 rows of w3; writes
 // silu(a) * b as bf16, 128 columns per tile), GATE (out = aux * sigmoid(acc),
-// bf16; aux is the attention output). Output and aux rows go through a
-// segmented row map so a stream's rows can live inside a joint
-// [text | image] token buffer.
+// bf16). Output and aux rows go through a segmented row map so a stream's
+// rows can live inside a joint [text | image] token buffer.
 #include "common.cuh"
 #include "iris_abi_internal.h"
 
@@ -38,12 +40,14 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int TMEM_COLS = 512;        // two 256-column fp32 accumulators
 constexpr int THREADS = 192;
 constexpr int GROUP_M = 16;           // tile rasterisation: 16 M-blocks per group
+constexpr int MAX_PROBLEMS = 4;
 constexpr size_t SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + 256 /*barriers*/;
 
 enum Epilogue : int { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_GATE = 2 };
 
-struct Params {
+struct Problem {
   int M, N, K;
+  int num_m, num_n, nk;
   int epilogue;
   int out_dtype;  // 0 f32, 1 bf16
   void* out;
@@ -53,6 +57,17 @@ struct Params {
   const __nv_bfloat16* aux;     // GATE: [*, ldaux]
   int64_t ldaux;
   RowMap aux_map;
+};
+
+struct Batch {
+  Problem prob[MAX_PROBLEMS];
+  int tile_start[MAX_PROBLEMS + 1];  // prefix sums of the problems' tile counts
+  int count;
+};
+
+struct TensorMaps {
+  CUtensorMap a[MAX_PROBLEMS];
+  CUtensorMap b[MAX_PROBLEMS];
 };
 
 struct Smem {
@@ -65,19 +80,28 @@ struct Smem {
   int abort;
 };
 
-IRIS_DEVICE void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
-  const int per_group = GROUP_M * num_n;
-  const int group = t / per_group;
+struct Tile {
+  int p, mb, nb;
+};
+
+// Tile t of the batch -> (problem, M block, N block); within a problem the
+// tiles go in groups of 16 M blocks so concurrent CTAs share A rows and W rows in L2.
+IRIS_DEVICE Tile locate(const Batch& bt, int t) {
+  int p = 0;
+  while (p + 1 < bt.count && t >= bt.tile_start[p + 1]) ++p;
+  const Problem& pr = bt.prob[p];
+  const int local = t - bt.tile_start[p];
+  const int per_group = GROUP_M * pr.num_n;
+  const int group = local / per_group;
   const int first_m = group * GROUP_M;
-  const int gm = min(GROUP_M, num_m - first_m);
-  const int local = t - group * per_group;
-  mb = first_m + local % gm;
-  nb = local / gm;
+  const int gm = min(GROUP_M, pr.num_m - first_m);
+  const int in_group = local - group * per_group;
+  return Tile{p, first_m + in_group % gm, in_group / gm};
 }
 
 IRIS_DEVICE float sigmoidf_fast(float x) { return 1.0f / (1.0f + __expf(-x)); }
 
-IRIS_DEVICE void store_row32(const Params& p, int64_t prow, int col0, const float (&v)[32]) {
+IRIS_DEVICE void store_row32(const Problem& p, int64_t prow, int col0, const float (&v)[32]) {
   if (p.out_dtype == 1) {
     __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + prow * p.ldc + col0;
     uint32_t packed[16];
@@ -94,8 +118,7 @@ IRIS_DEVICE void store_row32(const Params& p, int64_t prow, int col0, const floa
 }
 
 __global__ void __launch_bounds__(THREADS, 1)
-    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                     const Params p) {
+    gemm_bf16_kernel(const __grid_constant__ TensorMaps maps, const __grid_constant__ Batch bt) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the 128B-swizzled tiles
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -104,10 +127,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  const int num_m = (p.M + BM - 1) / BM;
-  const int num_n = (p.N + BN - 1) / BN;
-  const int num_tiles = num_m * num_n;
-  const int nk = (p.K + BK - 1) / BK;
+  const int num_tiles = bt.tile_start[bt.count];
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
@@ -123,8 +143,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tmap_a);
-    tma_prefetch_desc(&tmap_b);
+    for (int p = 0; p < bt.count; ++p) {
+      tma_prefetch_desc(&maps.a[p]);
+      tma_prefetch_desc(&maps.b[p]);
+    }
   }
   if (warp == 1) tmem_alloc(&s->tmem_base, TMEM_COLS);
   tc_fence_before();
@@ -143,8 +165,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int i = 0; i < STAGES; ++i) issued_phase[i] = -1;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        int mb, nb;
-        tile_coords(t, num_m, num_n, mb, nb);
+        const Tile tl = locate(bt, t);
+        const CUtensorMap* ma = &maps.a[tl.p];
+        const CUtensorMap* mw = &maps.b[tl.p];
+        const int nk = bt.prob[tl.p].nk;
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&s->empty[stage], phase ^ 1u, abort)) {
             ok = false;
@@ -153,8 +177,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           uint8_t* a_dst = tiles + stage * STAGE_BYTES;
           uint8_t* b_dst = a_dst + A_BYTES;
           mbar_arrive_expect_tx(&s->full[stage], STAGE_BYTES);
-          tma_load_2d(&tmap_a, &s->full[stage], a_dst, kb * BK, mb * BM);
-          tma_load_2d(&tmap_b, &s->full[stage], b_dst, kb * BK, nb * BN);
+          tma_load_2d(ma, &s->full[stage], a_dst, kb * BK, tl.mb * BM);
+          tma_load_2d(mw, &s->full[stage], b_dst, kb * BK, tl.nb * BN);
           issued_phase[stage] = static_cast<int>(phase);
           if (++stage == STAGES) {
             stage = 0;
@@ -178,6 +202,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       int it = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
+        const int nk = bt.prob[locate(bt, t).p].nk;
         const int acc = it & 1;
         const uint32_t acc_phase = static_cast<uint32_t>((it >> 1) & 1);
         if (!mbar_wait(&s->tmem_empty[acc], acc_phase ^ 1u, abort)) break;
@@ -216,15 +241,15 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int row_in_tile = quarter * 32 + lane;
     int it = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
-      int mb, nb;
-      tile_coords(t, num_m, num_n, mb, nb);
+      const Tile tl = locate(bt, t);
+      const Problem& p = bt.prob[tl.p];
       const int acc = it & 1;
       const uint32_t acc_phase = static_cast<uint32_t>((it >> 1) & 1);
       // warp-uniform decision: tcgen05.ld below is a .sync.aligned warp instruction
       if (!__all_sync(0xffffffffu, mbar_wait(&s->tmem_full[acc], acc_phase, abort))) break;
       tc_fence_after();
       const uint32_t t_base = tmem + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(quarter * 32) << 16);
-      const int64_t m = static_cast<int64_t>(mb) * BM + row_in_tile;
+      const int64_t m = static_cast<int64_t>(tl.mb) * BM + row_in_tile;
       const bool row_ok = m < p.M;
       if (p.epilogue == EPI_SWIGLU) {
         const int64_t prow = row_ok ? p.out_map(m) : 0;
@@ -234,7 +259,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           tmem_ld32(t_base + c * 32, ra);
           tmem_ld32(t_base + 128 + c * 32, rb);
           tmem_wait_ld();
-          const int col0 = nb * (BN / 2) + c * 32;
+          const int col0 = tl.nb * (BN / 2) + c * 32;
           if (row_ok && col0 < p.N / 2) {
             float v[32];
 #pragma unroll
@@ -253,7 +278,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           uint32_t r[32];
           tmem_ld32(t_base + c * 32, r);
           tmem_wait_ld();
-          const int col0 = nb * BN + c * 32;
+          const int col0 = tl.nb * BN + c * 32;
           if (row_ok && col0 < p.N) {
             float v[32];
             if (p.epilogue == EPI_GATE) {
@@ -293,58 +318,71 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
 }
 
+int check_problem(const iris_gemm_problem& q) {
+  IRIS_REQUIRE(q.a && q.w && q.out, "iris_gemm_bf16: null pointer");
+  IRIS_REQUIRE(q.M > 0 && q.N > 0 && q.K > 0, "iris_gemm_bf16: empty problem");
+  IRIS_REQUIRE(q.M < (1ll << 31) && q.N < (1ll << 31) && q.K < (1ll << 31), "iris_gemm_bf16: dimension too large");
+  IRIS_REQUIRE(q.K % 8 == 0 && q.lda % 8 == 0 && q.ldw % 8 == 0 && q.lda >= q.K && q.ldw >= q.K,
+               "iris_gemm_bf16: K and leading dimensions must be multiples of 8 (16-byte TMA rows)");
+  IRIS_REQUIRE(q.N % 32 == 0, "iris_gemm_bf16: N must be a multiple of 32");
+  IRIS_REQUIRE(q.epilogue >= EPI_STORE && q.epilogue <= EPI_GATE, "iris_gemm_bf16: unknown epilogue");
+  IRIS_REQUIRE(q.out_dtype == 0 || q.out_dtype == 1, "iris_gemm_bf16: out dtype must be f32 or bf16");
+  IRIS_REQUIRE(aligned16(q.a) && aligned16(q.w) && aligned16(q.out), "iris_gemm_bf16: pointers must be 16-byte aligned");
+  IRIS_REQUIRE(q.ldc % 8 == 0, "iris_gemm_bf16: ldc must be a multiple of 8");
+  if (q.epilogue == EPI_SWIGLU) {
+    IRIS_REQUIRE(q.N % BN == 0 && q.out_dtype == 1 && q.ldc >= q.N / 2,
+                 "iris_gemm_bf16: SwiGLU needs N % 256 == 0 (paired 128-row w1/w3 blocks) and bf16 out");
+  } else {
+    IRIS_REQUIRE(q.ldc >= q.N, "iris_gemm_bf16: ldc < N");
+  }
+  if (q.epilogue == EPI_GATE) {
+    IRIS_REQUIRE(q.aux != nullptr && aligned16(q.aux) && q.ldaux % 8 == 0 && q.ldaux >= q.N && q.out_dtype == 1,
+                 "iris_gemm_bf16: gate epilogue needs an aligned bf16 aux with ldaux % 8 == 0");
+    IRIS_REQUIRE(q.bias == nullptr, "iris_gemm_bf16: gate epilogue takes no bias");
+  }
+  IRIS_REQUIRE(q.out_seg_rows > 0 && q.aux_seg_rows > 0, "iris_gemm_bf16: row maps need seg_rows > 0");
+  return IRIS_OK;
+}
+
 }  // namespace gemm
 }  // namespace iris
 
 using namespace iris;
 
-extern "C" int iris_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw, void* out, int out_dtype,
-                              int64_t ldc, int64_t M, int64_t N, int64_t K, int epilogue, const float* bias,
-                              const void* aux, int64_t ldaux, int64_t out_seg_rows, int64_t out_seg_stride,
-                              int64_t out_seg_offset, int64_t aux_seg_rows, int64_t aux_seg_stride,
-                              int64_t aux_seg_offset, void* stream) {
+extern "C" int iris_gemm_bf16_grouped(const iris_gemm_problem* problems, int count, void* stream) {
   using namespace iris::gemm;
-  IRIS_REQUIRE(a && w && out, "iris_gemm_bf16: null pointer");
-  IRIS_REQUIRE(M > 0 && N > 0 && K > 0, "iris_gemm_bf16: empty problem");
-  IRIS_REQUIRE(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "iris_gemm_bf16: dimension too large");
-  IRIS_REQUIRE(K % 8 == 0 && lda % 8 == 0 && ldw % 8 == 0 && lda >= K && ldw >= K,
-               "iris_gemm_bf16: K and leading dimensions must be multiples of 8 (16-byte TMA rows)");
-  IRIS_REQUIRE(N % 32 == 0, "iris_gemm_bf16: N must be a multiple of 32");
-  IRIS_REQUIRE(epilogue >= EPI_STORE && epilogue <= EPI_GATE, "iris_gemm_bf16: unknown epilogue");
-  IRIS_REQUIRE(out_dtype == 0 || out_dtype == 1, "iris_gemm_bf16: out dtype must be f32 or bf16");
-  IRIS_REQUIRE(aligned16(a) && aligned16(w) && aligned16(out), "iris_gemm_bf16: pointers must be 16-byte aligned");
-  IRIS_REQUIRE(ldc % 8 == 0, "iris_gemm_bf16: ldc must be a multiple of 8");
-  if (epilogue == EPI_SWIGLU) {
-    IRIS_REQUIRE(N % BN == 0 && out_dtype == 1 && ldc >= N / 2,
-                 "iris_gemm_bf16: SwiGLU needs N % 256 == 0 (paired 128-row w1/w3 blocks) and bf16 out");
-  } else {
-    IRIS_REQUIRE(ldc >= N, "iris_gemm_bf16: ldc < N");
+  IRIS_REQUIRE(problems != nullptr && count >= 1 && count <= MAX_PROBLEMS,
+               "iris_gemm_bf16_grouped: 1 to 4 problems per launch");
+  TensorMaps maps;
+  Batch bt;
+  bt.count = count;
+  bt.tile_start[0] = 0;
+  int64_t total = 0;
+  for (int i = 0; i < count; ++i) {
+    const iris_gemm_problem& q = problems[i];
+    IRIS_CHECK_STATUS(check_problem(q));
+    IRIS_CHECK_STATUS(make_tmap_2d_bf16(&maps.a[i], q.a, q.K, q.M, q.lda, BK, BM));
+    IRIS_CHECK_STATUS(make_tmap_2d_bf16(&maps.b[i], q.w, q.K, q.N, q.ldw, BK, BN));
+    Problem& p = bt.prob[i];
+    p.M = static_cast<int>(q.M);
+    p.N = static_cast<int>(q.N);
+    p.K = static_cast<int>(q.K);
+    p.num_m = static_cast<int>((q.M + BM - 1) / BM);
+    p.num_n = static_cast<int>((q.N + BN - 1) / BN);
+    p.nk = static_cast<int>((q.K + BK - 1) / BK);
+    p.epilogue = q.epilogue;
+    p.out_dtype = q.out_dtype;
+    p.out = q.out;
+    p.ldc = q.ldc;
+    p.out_map = RowMap{q.out_seg_rows, q.out_seg_stride, q.out_seg_offset};
+    p.bias = q.bias;
+    p.aux = reinterpret_cast<const __nv_bfloat16*>(q.aux);
+    p.ldaux = q.ldaux;
+    p.aux_map = RowMap{q.aux_seg_rows, q.aux_seg_stride, q.aux_seg_offset};
+    total += static_cast<int64_t>(p.num_m) * p.num_n;
+    IRIS_REQUIRE(total < (1ll << 31), "iris_gemm_bf16_grouped: too many tiles");
+    bt.tile_start[i + 1] = static_cast<int>(total);
   }
-  if (epilogue == EPI_GATE) {
-    IRIS_REQUIRE(aux != nullptr && aligned16(aux) && ldaux % 8 == 0 && ldaux >= N && out_dtype == 1,
-                 "iris_gemm_bf16: gate epilogue needs an aligned bf16 aux with ldaux % 8 == 0");
-    IRIS_REQUIRE(bias == nullptr, "iris_gemm_bf16: gate epilogue takes no bias");
-  }
-  IRIS_REQUIRE(out_seg_rows > 0 && aux_seg_rows > 0, "iris_gemm_bf16: row maps need seg_rows > 0");
-
-  CUtensorMap ta, tb;
-  IRIS_CHECK_STATUS(make_tmap_2d_bf16(&ta, a, K, M, lda, BK, BM));
-  IRIS_CHECK_STATUS(make_tmap_2d_bf16(&tb, w, K, N, ldw, BK, BN));
-
-  Params p;
-  p.M = static_cast<int>(M);
-  p.N = static_cast<int>(N);
-  p.K = static_cast<int>(K);
-  p.epilogue = epilogue;
-  p.out_dtype = out_dtype;
-  p.out = out;
-  p.ldc = ldc;
-  p.out_map = RowMap{out_seg_rows, out_seg_stride, out_seg_offset};
-  p.bias = bias;
-  p.aux = reinterpret_cast<const __nv_bfloat16*>(aux);
-  p.ldaux = ldaux;
-  p.aux_map = RowMap{aux_seg_rows, aux_seg_stride, aux_seg_offset};
-
   static bool configured[64] = {false};
   int dev = 0;
   IRIS_CUDA(cudaGetDevice(&dev));
@@ -353,9 +391,37 @@ extern "C" int iris_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t
                                    static_cast<int>(SMEM_BYTES)));
     configured[dev] = true;
   }
-  const int tiles = static_cast<int>(((M + BM - 1) / BM) * ((N + BN - 1) / BN));
-  const int grid = tiles < num_sms() ? tiles : num_sms();
-  gemm_bf16_kernel<<<grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(ta, tb, p);
+  const int grid = total < num_sms() ? static_cast<int>(total) : num_sms();
+  gemm_bf16_kernel<<<grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(maps, bt);
   IRIS_CUDA(cudaGetLastError());
   return IRIS_OK;
+}
+
+extern "C" int iris_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw, void* out, int out_dtype,
+                              int64_t ldc, int64_t M, int64_t N, int64_t K, int epilogue, const float* bias,
+                              const void* aux, int64_t ldaux, int64_t out_seg_rows, int64_t out_seg_stride,
+                              int64_t out_seg_offset, int64_t aux_seg_rows, int64_t aux_seg_stride,
+                              int64_t aux_seg_offset, void* stream) {
+  iris_gemm_problem q;
+  q.a = a;
+  q.lda = lda;
+  q.w = w;
+  q.ldw = ldw;
+  q.out = out;
+  q.out_dtype = out_dtype;
+  q.ldc = ldc;
+  q.M = M;
+  q.N = N;
+  q.K = K;
+  q.epilogue = epilogue;
+  q.bias = bias;
+  q.aux = aux;
+  q.ldaux = ldaux;
+  q.out_seg_rows = out_seg_rows;
+  q.out_seg_stride = out_seg_stride;
+  q.out_seg_offset = out_seg_offset;
+  q.aux_seg_rows = aux_seg_rows;
+  q.aux_seg_stride = aux_seg_stride;
+  q.aux_seg_offset = aux_seg_offset;
+  return iris_gemm_bf16_grouped(&q, 1, stream);
 }

@@ -139,6 +139,192 @@ IRIS_DEVICE void pit_tail(float (&x)[C], const float (&attn)[C], const __nv_bflo
   for (int c = 0; c < C; ++c) x[c] = r(x[c] + r(r(out[c]) * (1.f + m[2 * C + c]) + m[3 * C + c]));
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core form of the pixel tail: one warp per 16-pixel tile. The MLP
+// (16 -> 64 -> 16) runs as mma.sync m16n8k16 BF16 -> FP32 (8 MMAs each way);
+// fc1's accumulator fragments are, after bias + GELU, exactly fc2's A
+// fragments. Every per-pixel elementwise step happens in the fragment layout:
+// lane = 4 g + c holds pixels g and g + 8 of the tile, channels
+// {2c, 2c+1, 2c+8, 2c+9}; 16-channel sums reduce over the lane quad.
+IRIS_DEVICE void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+IRIS_DEVICE float quad_sum(float v) {
+  v += __shfl_xor_sync(0xffffffffu, v, 1);
+  v += __shfl_xor_sync(0xffffffffu, v, 2);
+  return v;
+}
+
+IRIS_DEVICE uint32_t ld_bf16x2(const __nv_bfloat16* p) { return *reinterpret_cast<const uint32_t*>(p); }
+
+// channel of slot j (0..3) for lane quad position c
+IRIS_DEVICE int frag_channel(int c, int j) { return 2 * c + (j & 1) + ((j >> 1) << 3); }
+
+template <bool F32, bool HEAD>
+__global__ void __launch_bounds__(THREADS) pixel_mlp_mma_kernel(
+    void* pixels, const __nv_bfloat16* __restrict__ branch, const __nv_bfloat16* __restrict__ mods,
+    const float* __restrict__ nw, const __nv_bfloat16* __restrict__ w1, const __nv_bfloat16* __restrict__ b1,
+    const __nv_bfloat16* __restrict__ w2, const __nv_bfloat16* __restrict__ b2, const float* __restrict__ nnw,
+    __nv_bfloat16* __restrict__ next_input, const float* __restrict__ fw, const float* __restrict__ fb,
+    float* __restrict__ v, int64_t n, int64_t height, int64_t width, int patch, float eps) {
+  constexpr bool ROUND = !F32;
+  auto r = [](float x) { return ROUND ? round_bf16(x) : x; };
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+  // B fragments of W1^T (k = in channel, n = hidden) and W2^T (k = hidden, n = out channel)
+  uint32_t bw1[8][2], bw2[4][2][2];
+#pragma unroll
+  for (int nt = 0; nt < 8; ++nt) {
+    const __nv_bfloat16* row = w1 + (nt * 8 + g) * C;
+    bw1[nt][0] = ld_bf16x2(row + 2 * c);
+    bw1[nt][1] = ld_bf16x2(row + 2 * c + 8);
+  }
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks)
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const __nv_bfloat16* row = w2 + (nt * 8 + g) * HID + ks * 16;
+      bw2[ks][nt][0] = ld_bf16x2(row + 2 * c);
+      bw2[ks][nt][1] = ld_bf16x2(row + 2 * c + 8);
+    }
+  float bias1[8][2], bias2[4], gain[4], gain_next[4];
+#pragma unroll
+  for (int nt = 0; nt < 8; ++nt) {
+    bias1[nt][0] = __bfloat162float(b1[nt * 8 + 2 * c]);
+    bias1[nt][1] = __bfloat162float(b1[nt * 8 + 2 * c + 1]);
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int ch = frag_channel(c, j);
+    bias2[j] = __bfloat162float(b2[ch]);
+    gain[j] = nw[ch];
+    gain_next[j] = nnw[ch];
+  }
+  const int pp = patch * patch;
+  const int64_t gw = width / patch;
+  const int64_t L = (height / patch) * gw;
+  const int64_t tiles = n / 16;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
+  for (int64_t tile = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5); tile < tiles;
+       tile += warps) {
+    float x[2][4], h[2][4];
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int64_t px = tile * 16 + g + 8 * half;
+      const __nv_bfloat16* md = mods + px * 4 * C;
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) {  // channel pairs (2c, 2c+1) and (2c+8, 2c+9)
+        const int ch = 2 * c + 8 * jj;
+        float p0, p1;
+        if (F32) {
+          const float2 pv = *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(pixels) + px * C + ch);
+          p0 = pv.x;
+          p1 = pv.y;
+        } else {
+          const float2 pv = unpack_bf16x2(ld_bf16x2(reinterpret_cast<const __nv_bfloat16*>(pixels) + px * C + ch));
+          p0 = pv.x;
+          p1 = pv.y;
+        }
+        const float2 at = unpack_bf16x2(ld_bf16x2(branch + px * C + ch));
+        const float2 s1 = unpack_bf16x2(ld_bf16x2(md + ch));
+        const float2 t1 = unpack_bf16x2(ld_bf16x2(md + C + ch));
+        x[half][2 * jj] = r(p0 + r(at.x * (1.f + s1.x) + t1.x));
+        x[half][2 * jj + 1] = r(p1 + r(at.y * (1.f + s1.y) + t1.y));
+      }
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) ss += x[half][j] * x[half][j];
+      const float inv = rsqrtf(quad_sum(ss) / C + eps);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) h[half][j] = x[half][j] * inv * gain[j];
+    }
+    // A fragment of the normed pixels (bf16)
+    const uint32_t a[4] = {pack_bf16x2(h[0][0], h[0][1]), pack_bf16x2(h[1][0], h[1][1]),
+                           pack_bf16x2(h[0][2], h[0][3]), pack_bf16x2(h[1][2], h[1][3])};
+    uint32_t ga[4][4];  // fc2 A fragments: GELU(fc1) in bf16
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      mma_bf16_16816(acc, a, bw1[nt][0], bw1[nt][1]);
+      float gl[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) gl[j] = gelu_erf(r(acc[j] + bias1[nt][j & 1]));
+      const int ks = nt >> 1, hi = nt & 1;
+      ga[ks][2 * hi] = pack_bf16x2(gl[0], gl[1]);      // row g
+      ga[ks][2 * hi + 1] = pack_bf16x2(gl[2], gl[3]);  // row g + 8
+    }
+    float out[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) mma_bf16_16816(acc, ga[ks], bw2[ks][nt][0], bw2[ks][nt][1]);
+      // acc: (g, 8nt + 2c), (g, 8nt + 2c + 1), (g + 8, ...) -> slots 2nt, 2nt + 1
+      out[0][2 * nt] = acc[0];
+      out[0][2 * nt + 1] = acc[1];
+      out[1][2 * nt] = acc[2];
+      out[1][2 * nt + 1] = acc[3];
+    }
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int64_t px = tile * 16 + g + 8 * half;
+      const __nv_bfloat16* md = mods + px * 4 * C;
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) {
+        const int ch = 2 * c + 8 * jj;
+        const float2 s2 = unpack_bf16x2(ld_bf16x2(md + 2 * C + ch));
+        const float2 t2 = unpack_bf16x2(ld_bf16x2(md + 3 * C + ch));
+        const float m0 = r(out[half][2 * jj] + bias2[2 * jj]), m1 = r(out[half][2 * jj + 1] + bias2[2 * jj + 1]);
+        x[half][2 * jj] = r(x[half][2 * jj] + r(m0 * (1.f + s2.x) + t2.x));
+        x[half][2 * jj + 1] = r(x[half][2 * jj + 1] + r(m1 * (1.f + s2.y) + t2.y));
+      }
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) ss += x[half][j] * x[half][j];
+      const float inv = rsqrtf(quad_sum(ss) / C + eps);
+      if (!HEAD) {
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+          const int ch = 2 * c + 8 * jj;
+          if (F32) {
+            *reinterpret_cast<float2*>(reinterpret_cast<float*>(pixels) + px * C + ch) =
+                make_float2(x[half][2 * jj], x[half][2 * jj + 1]);
+          } else {
+            *reinterpret_cast<uint32_t*>(reinterpret_cast<__nv_bfloat16*>(pixels) + px * C + ch) =
+                pack_bf16x2(x[half][2 * jj], x[half][2 * jj + 1]);
+          }
+          *reinterpret_cast<uint32_t*>(next_input + px * C + ch) =
+              pack_bf16x2(x[half][2 * jj] * inv * gain_next[2 * jj], x[half][2 * jj + 1] * inv * gain_next[2 * jj + 1]);
+        }
+      } else {
+        float part[3] = {0.f, 0.f, 0.f};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float hn = F32 ? x[half][j] * inv * gain_next[j] : round_bf16(x[half][j] * inv * gain_next[j]);
+          const int ch = frag_channel(c, j);
+#pragma unroll
+          for (int o = 0; o < 3; ++o) part[o] = fmaf(hn, __ldg(fw + o * C + ch), part[o]);
+        }
+#pragma unroll
+        for (int o = 0; o < 3; ++o) part[o] = quad_sum(part[o]);
+        if (c == 0) {
+          const int64_t patch_idx = px / pp;
+          const int k = static_cast<int>(px % pp);
+          const int64_t bb = patch_idx / L, l = patch_idx % L;
+          const int64_t y = (l / gw) * patch + k / patch, xx = (l % gw) * patch + k % patch;
+#pragma unroll
+          for (int o = 0; o < 3; ++o) v[((bb * 3 + o) * height + y) * width + xx] = part[o] + __ldg(fb + o);
+        }
+      }
+    }
+  }
+}
+
 __global__ void __launch_bounds__(THREADS) pixel_rms_norm_kernel(const void* pixels, bool f32,
                                                                   __nv_bfloat16* __restrict__ out,
                                                                   const float* __restrict__ weight, int64_t n,
@@ -272,6 +458,13 @@ inline unsigned grid_for(int64_t n) {
   return static_cast<unsigned>(blocks < cap ? blocks : cap);
 }
 
+// 16-pixel tiles, one per warp, 8 warps per block, grid-stride beyond 8 blocks / SM
+inline unsigned mma_grid_for(int64_t n) {
+  const int64_t blocks = (n / 16 + THREADS / 32 - 1) / (THREADS / 32);
+  const int64_t cap = static_cast<int64_t>(num_sms()) * 8;
+  return static_cast<unsigned>(blocks < cap ? blocks : cap);
+}
+
 }  // namespace pixel
 }  // namespace iris
 
@@ -310,6 +503,20 @@ extern "C" int iris_pixel_mlp(void* pixels, int pixel_dtype, const void* branch,
   if (n_pixels == 0) return IRIS_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   auto bf = [](const void* p) { return reinterpret_cast<const __nv_bfloat16*>(p); };
+  if (n_pixels % 16 == 0) {  // whole 16-pixel tiles: tensor-core MLP
+    const unsigned grid = mma_grid_for(n_pixels);
+    auto nxt = reinterpret_cast<__nv_bfloat16*>(next_input);
+    if (pixel_dtype == IRIS_F32)
+      pixel_mlp_mma_kernel<true, false><<<grid, THREADS, 0, st>>>(
+          pixels, bf(branch), bf(mods), norm_weight, bf(fc1_w), bf(fc1_b), bf(fc2_w), bf(fc2_b), next_norm_weight,
+          nxt, nullptr, nullptr, nullptr, n_pixels, 16, 16, 16, eps);
+    else
+      pixel_mlp_mma_kernel<false, false><<<grid, THREADS, 0, st>>>(
+          pixels, bf(branch), bf(mods), norm_weight, bf(fc1_w), bf(fc1_b), bf(fc2_w), bf(fc2_b), next_norm_weight,
+          nxt, nullptr, nullptr, nullptr, n_pixels, 16, 16, 16, eps);
+    IRIS_CUDA(cudaGetLastError());
+    return IRIS_OK;
+  }
   if (pixel_dtype == IRIS_F32)
     pixel_mlp_kernel<true><<<grid_for(n_pixels), THREADS, 0, st>>>(
         pixels, bf(branch), bf(mods), norm_weight, bf(fc1_w), bf(fc1_b), bf(fc2_w), bf(fc2_b), next_norm_weight,
@@ -337,6 +544,20 @@ extern "C" int iris_pixel_mlp_head(void* pixels, int pixel_dtype, const void* br
   if (n == 0) return IRIS_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   auto bf = [](const void* p) { return reinterpret_cast<const __nv_bfloat16*>(p); };
+  if (n % 16 == 0) {  // whole 16-pixel tiles: tensor-core MLP
+    const unsigned grid = mma_grid_for(n);
+    const int pt = static_cast<int>(patch);
+    if (pixel_dtype == IRIS_F32)
+      pixel_mlp_mma_kernel<true, true><<<grid, THREADS, 0, st>>>(
+          pixels, bf(branch), bf(mods), norm_weight, bf(fc1_w), bf(fc1_b), bf(fc2_w), bf(fc2_b), final_norm_weight,
+          nullptr, final_w, final_b, v, n, height, width, pt, eps);
+    else
+      pixel_mlp_mma_kernel<false, true><<<grid, THREADS, 0, st>>>(
+          pixels, bf(branch), bf(mods), norm_weight, bf(fc1_w), bf(fc1_b), bf(fc2_w), bf(fc2_b), final_norm_weight,
+          nullptr, final_w, final_b, v, n, height, width, pt, eps);
+    IRIS_CUDA(cudaGetLastError());
+    return IRIS_OK;
+  }
   if (pixel_dtype == IRIS_F32)
     pixel_mlp_head_kernel<true><<<grid_for(n), THREADS, 0, st>>>(
         pixels, bf(branch), bf(mods), norm_weight, bf(fc1_w), bf(fc1_b), bf(fc2_w), bf(fc2_b), final_norm_weight,

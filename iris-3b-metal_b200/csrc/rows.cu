@@ -172,6 +172,88 @@ __global__ void __launch_bounds__(WARPS * 32) gated_residual_kernel(
   }
 }
 
+// The same update with one 128-thread CTA per row (widths that are a multiple
+// of 512: thread t owns the 4-vectors t, t + 128, ...). Few registers per
+// thread keep up to 16 rows per SM in flight, which the warp-per-row form
+// cannot at 3072 columns; sums are reduced across the 4 warps in shared memory.
+constexpr int ROW_THREADS = 128;
+
+IRIS_DEVICE float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  return red[0] + red[1] + red[2] + red[3];
+}
+
+template <typename TB, typename TO, int VPT>
+__global__ void __launch_bounds__(ROW_THREADS) gated_residual_row_kernel(
+    float* __restrict__ residual, RowMap rmap, const TB* __restrict__ branch, RowMap bmap,
+    const float* __restrict__ weight, const float* __restrict__ gate, int64_t mod_stride, int64_t rows_per_batch,
+    int width, float eps, int next_mode, const float* __restrict__ next_weight, const float* __restrict__ next_shift,
+    const float* __restrict__ next_scale, int64_t next_mod_stride, TO* __restrict__ next_out, RowMap nmap) {
+  __shared__ float red[2][4];
+  const int64_t r = blockIdx.x;
+  const int t = threadIdx.x;
+  const TB* br = branch + bmap(r) * width;
+  float* xr = residual + rmap(r) * width;
+  float4 v[VPT], x[VPT];
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int e = (i * ROW_THREADS + t) * 4;
+    v[i] = Vec4<TB>::load(br + e);
+    x[i] = *reinterpret_cast<const float4*>(xr + e);
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) ss += sumsq(v[i]);
+  const float inv = rsqrtf(block_sum(ss, red[0]) / static_cast<float>(width) + eps);
+  const int64_t b = r / rows_per_batch;
+  const float* g = gate + b * mod_stride;
+  float ss2 = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int e = (i * ROW_THREADS + t) * 4;
+    const float4 w = ld4(weight + e), g4 = ld4(g + e);
+    x[i].x += g4.x * (v[i].x * inv * w.x);
+    x[i].y += g4.y * (v[i].y * inv * w.y);
+    x[i].z += g4.z * (v[i].z * inv * w.z);
+    x[i].w += g4.w * (v[i].w * inv * w.w);
+    *reinterpret_cast<float4*>(xr + e) = x[i];
+    ss2 += sumsq(x[i]);
+  }
+  if (next_mode == IRIS_NEXT_NONE) return;
+  TO* o = next_out + nmap(r) * width;
+  const float* sh = next_shift + b * next_mod_stride;
+  if (next_mode == IRIS_NEXT_NORM_MODULATE) {
+    const float inv2 = rsqrtf(block_sum(ss2, red[1]) / static_cast<float>(width) + eps);
+    const float* sc = next_scale + b * next_mod_stride;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int e = (i * ROW_THREADS + t) * 4;
+      const float4 w = ld4(next_weight + e), s4 = ld4(sh + e), c4 = ld4(sc + e);
+      float4 h;
+      h.x = x[i].x * inv2 * w.x * (1.f + c4.x) + s4.x;
+      h.y = x[i].y * inv2 * w.y * (1.f + c4.y) + s4.y;
+      h.z = x[i].z * inv2 * w.z * (1.f + c4.z) + s4.z;
+      h.w = x[i].w * inv2 * w.w * (1.f + c4.w) + s4.w;
+      Vec4<TO>::store(o + e, h);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int e = (i * ROW_THREADS + t) * 4;
+      const float4 t4 = ld4(sh + e);
+      const float a0 = t4.x + x[i].x, a1 = t4.y + x[i].y, a2 = t4.z + x[i].z, a3 = t4.w + x[i].w;
+      float4 h;
+      h.x = a0 / (1.f + __expf(-a0));
+      h.y = a1 / (1.f + __expf(-a1));
+      h.z = a2 / (1.f + __expf(-a2));
+      h.w = a3 / (1.f + __expf(-a3));
+      Vec4<TO>::store(o + e, h);
+    }
+  }
+}
+
 template <int NV>
 __global__ void __launch_bounds__(WARPS * 32) rms_norm_add_kernel(float* __restrict__ x,
                                                                    const float* __restrict__ weight,
@@ -244,6 +326,26 @@ template <typename TB, typename TO>
 int launch_residual(float* res, RowMap rm, const void* branch, RowMap bm, const float* w, const float* gate,
                     int64_t ms, int64_t rows, int64_t rpb, int width, float eps, int mode, const float* nw,
                     const float* nsh, const float* nsc, int64_t nms, void* nout, RowMap nm, cudaStream_t st) {
+  if (width % (4 * ROW_THREADS) == 0 && width / (4 * ROW_THREADS) <= 8 && rows < (1ll << 31)) {
+    const int vpt = width / (4 * ROW_THREADS);
+#define IRIS_ROW(VPT)                                                                                              \
+  gated_residual_row_kernel<TB, TO, VPT><<<static_cast<unsigned>(rows), ROW_THREADS, 0, st>>>(                     \
+      res, rm, reinterpret_cast<const TB*>(branch), bm, w, gate, ms, rpb, width, eps, mode, nw, nsh, nsc, nms,     \
+      reinterpret_cast<TO*>(nout), nm)
+    switch (vpt) {
+      case 1: IRIS_ROW(1); break;
+      case 2: IRIS_ROW(2); break;
+      case 3: IRIS_ROW(3); break;
+      case 4: IRIS_ROW(4); break;
+      case 5: IRIS_ROW(5); break;
+      case 6: IRIS_ROW(6); break;
+      case 7: IRIS_ROW(7); break;
+      default: IRIS_ROW(8); break;
+    }
+#undef IRIS_ROW
+    IRIS_CUDA(cudaGetLastError());
+    return IRIS_OK;
+  }
   const int nv = width / 128;
   const unsigned grid = static_cast<unsigned>((rows + WARPS - 1) / WARPS);
 #define IRIS_LAUNCH(NV)                                                                                            \

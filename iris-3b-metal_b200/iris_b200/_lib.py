@@ -44,6 +44,20 @@ SIGNATURES: dict[str, list] = {
     "iris_all_finite": [P, I64, P, P],
 }
 
+class GemmProblem(ctypes.Structure):
+    """``iris_gemm_problem`` of include/iris_b200.h."""
+
+    _fields_ = [
+        ("a", P), ("lda", I64), ("w", P), ("ldw", I64), ("out", P), ("out_dtype", I32), ("ldc", I64),
+        ("M", I64), ("N", I64), ("K", I64), ("epilogue", I32), ("bias", P), ("aux", P), ("ldaux", I64),
+        ("out_seg_rows", I64), ("out_seg_stride", I64), ("out_seg_offset", I64),
+        ("aux_seg_rows", I64), ("aux_seg_stride", I64), ("aux_seg_offset", I64),
+    ]  # fmt: skip
+
+
+SIGNATURES["iris_gemm_bf16_grouped"] = [ctypes.POINTER(GemmProblem), I32, P]
+SIGNATURES["iris_flash_attn_fwd_split"] = [P, P, P, I64, I64, I64, I64, I64, F, I64, P, P, P, P, I64, P]
+
 _lib: ctypes.CDLL | None = None
 
 

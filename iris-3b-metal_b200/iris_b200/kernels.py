@@ -242,7 +242,7 @@ def pixel_mlp_(
 
 
 # ----------------------------------------------------------- engine entry points
-def gemm(
+def gemm_problem(
     a: torch.Tensor,
     w: torch.Tensor,
     out: torch.Tensor,
@@ -252,34 +252,45 @@ def gemm(
     aux: torch.Tensor | None = None,
     out_rows: tuple[int, int, int] | None = None,
     aux_rows: tuple[int, int, int] | None = None,
-) -> torch.Tensor:
-    """``out = epilogue(a @ w.T)`` on the tensor cores; ``a``: bf16 ``[M, K]``
-    (row stride may exceed K), ``w``: bf16 ``[N, K]``; ``out`` rows through the
-    row map ``(seg_rows, seg_stride, seg_offset)`` (identity by default)."""
+) -> "_lib.GemmProblem":
+    """Validate one ``out = epilogue(a @ w.T)`` and describe it for the library:
+    ``a``: bf16 ``[M, K]`` (row stride may exceed K), ``w``: bf16 ``[N, K]``;
+    ``out`` rows through the row map ``(seg_rows, seg_stride, seg_offset)``."""
     _require(a.dim() == 2 and w.dim() == 2 and a.dtype == w.dtype == torch.bfloat16, "gemm needs bf16 [M, K] x [N, K]")
     _require(a.stride(1) == 1 and w.stride(1) == 1 and out.stride(-1) == 1, "gemm operands must be row-major")
     M, K = a.shape
     N = w.shape[0]
     _require(w.shape[1] == K, "gemm: inner dimensions differ")
-    ldc = out.stride(-2) if out.dim() >= 2 else N
-    out_rows = out_rows or (M, 0, 0)
-    aux_rows = aux_rows or (M, 0, 0)
     if bias is not None:
         _require_fp32(bias=bias)
         _require(bias.numel() == N, "gemm: bias width")
     _require_cuda(a, w, out)
+    out_rows = out_rows or (M, 0, 0)
+    aux_rows = aux_rows or (M, 0, 0)
+    return _lib.GemmProblem(
+        a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), out.data_ptr(), _dtype(out),
+        out.stride(-2) if out.dim() >= 2 else N, M, N, K, epilogue, _ptr(bias), _ptr(aux),
+        aux.stride(-2) if aux is not None else 0, *out_rows, *aux_rows,
+    )  # fmt: skip
+
+
+def gemm_grouped(problems: list, stream: int) -> None:
+    """Run 1 to 4 problems from :func:`gemm_problem` in one persistent launch."""
+    _require(1 <= len(problems) <= 4, "gemm_grouped takes 1 to 4 problems")
+    array = (_lib.GemmProblem * len(problems))(*problems)
     timing = _gemm_profile is not None
     if timing:
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record()
-    _lib.call(
-        "iris_gemm_bf16", a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), out.data_ptr(), _dtype(out), ldc,
-        M, N, K, epilogue, _ptr(bias), _ptr(aux), aux.stride(-2) if aux is not None else 0, *out_rows, *aux_rows,
-        stream_of(a),
-    )  # fmt: skip
+    _lib.call("iris_gemm_bf16_grouped", array, len(problems), stream)
     if timing:
         end.record()
-        _gemm_profile.append((start, end, 2.0 * M * N * K))
+        _gemm_profile.append((start, end, sum(2.0 * q.M * q.N * q.K for q in problems)))
+
+
+def gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor, **kwargs) -> torch.Tensor:
+    """``out = epilogue(a @ w.T)`` on the tensor cores (see :func:`gemm_problem`)."""
+    gemm_grouped([gemm_problem(a, w, out, **kwargs)], stream_of(a))
     return out
 
 
@@ -316,6 +327,36 @@ def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torc
         float(scale if scale is not None else d**-0.5), out.stride(1), stream_of(q),
     )  # fmt: skip
     return out
+
+
+def flash_attention_split(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    split: int,
+    o_text: torch.Tensor | None,
+    o_image: torch.Tensor,
+    gate_text: torch.Tensor | None = None,
+    gate_image: torch.Tensor | None = None,
+    scale: float | None = None,
+) -> None:
+    """Attention whose token ``i < split`` rows land densely in ``o_text`` (row
+    ``b * split + i``) and the rest in ``o_image`` (row ``b * (N - split) + i - split``),
+    each multiplied by ``sigmoid`` of the bf16 gate logits in the same rows."""
+    _require(q.dim() == 4 and k.shape == v.shape and q.shape[0] == k.shape[0] and q.shape[2:] == k.shape[2:],
+             "flash_attention: q [B, H, N, D], k/v [B, H_kv, N, D]")  # fmt: skip
+    _require(all(t.dtype == torch.bfloat16 and t.is_contiguous() for t in (q, k, v)), "flash_attention: contiguous bf16")
+    batch, heads, n, d = q.shape
+    outs = [t for t in (o_text, o_image, gate_text, gate_image) if t is not None]
+    _require(all(t.dtype == torch.bfloat16 and t.stride(-1) == 1 for t in outs), "flash_attention: bf16 row-major outputs")
+    stride = o_image.stride(-2)
+    _require(all(t.stride(-2) == stride for t in outs), "flash_attention: outputs and gates share one row stride")
+    _require_cuda(q, k, v, *outs)
+    _lib.call(
+        "iris_flash_attn_fwd_split", q.data_ptr(), k.data_ptr(), v.data_ptr(), batch, heads, k.shape[1], n, d,
+        float(scale if scale is not None else d**-0.5), split, _ptr(o_text), o_image.data_ptr(), _ptr(gate_text),
+        _ptr(gate_image), stride, stream_of(q),
+    )  # fmt: skip
 
 
 def device_error(clear: bool = True, device: torch.device | None = None) -> int:

@@ -326,8 +326,8 @@ class CudaIris:
             "q": e(batch, hq, N, HEAD_DIM),
             "k": e(batch, hkv, N, HEAD_DIM),
             "v": e(batch, hkv, N, HEAD_DIM),
-            "o": e(batch * N, d),
-            "g": e(batch * N, d),
+            "glog": e(batch * N, d),  # gate logits, dense per stream (text rows, then image rows)
+            "og": e(batch * N, d),  # gated attention output, same rows
             "branch": e(batch * N, d),
             "act": e(batch * N, self.ffn_pad),
             "s_cond": e(batch * L, d),
@@ -415,10 +415,7 @@ class CudaIris:
         self._first_norm(self.blocks[0], ws, geom, eps, st)
         for i, block in enumerate(self.blocks):
             nxt = self.blocks[i + 1] if i + 1 < len(self.blocks) else None
-            if block.dual:
-                self._dual_block(block, nxt, ws, geom, cos, sin, eps, st)
-            else:
-                self._single_block(block, nxt, ws, geom, cos, sin, eps, st)
+            self._block(block, nxt, ws, geom, cos, sin, eps, st)
             if capture is not None:
                 capture[f"block{i}"] = tokens.view(batch, N, d)[:, T:].clone()
         if capture is not None:
@@ -456,59 +453,72 @@ class CudaIris:
                 rows, rpb, g.d, eps, st,
             )  # fmt: skip
 
-    def _dual_block(self, block, nxt, ws, g, cos, sin, eps, st) -> None:
+    def _block(self, block, nxt, ws, g, cos, sin, eps, st) -> None:
+        """One trunk block. Dual-stream blocks run each linear as one grouped
+        launch over both streams (image problem first, so the small text problem
+        fills the tail of its tile list); the sigmoid gate is applied in the
+        attention epilogue, which writes each stream's rows densely."""
         cfg = self.cfg
-        hq, hkv = cfg.num_heads, cfg.kv_heads
         segs = self._segments(block, g)
-        wq = block.qkv["x"].shape[0]
-        for stream, rows, rpb, tmap, off in segs:
-            K.gemm(ws["h"][off : off + rows], block.qkv[stream], ws["qkv"][off : off + rows])
-            qn, kn = block.qk_norm[stream]
+        order = segs[::-1]
+        h = ws[_hkey(block)]
+
+        def grouped(a_key, weights, out_key, **kw):
+            problems = []
+            for s, rows, _, _, off in order:
+                w = weights[s]
+                extra = dict(kw)
+                if isinstance(w, tuple):
+                    w, extra["bias"] = w
+                a = h if a_key is None else ws[a_key]
+                problems.append(K.gemm_problem(a[off : off + rows], w, ws[out_key][off : off + rows], **extra))
+            K.gemm_grouped(problems, st)
+
+        grouped(None, block.qkv, "qkv")
+        for s, rows, rpb, tmap, off in segs:
+            qn, kn = block.qk_norm[s]
             _lib.call(
-                "iris_qkv_heads", ws["qkv"][off:].data_ptr(), g.batch, rpb, wq, hq, hkv, qn.data_ptr(), kn.data_ptr(),
-                cos.data_ptr(), sin.data_ptr(), eps, ws["q"].data_ptr(), ws["k"].data_ptr(), ws["v"].data_ptr(), g.N,
-                tmap[2], st,
+                "iris_qkv_heads", ws["qkv"][off:].data_ptr(), g.batch, rpb, block.qkv[s].shape[0], cfg.num_heads,
+                cfg.kv_heads, qn.data_ptr(), kn.data_ptr(), cos.data_ptr(), sin.data_ptr(), eps, ws["q"].data_ptr(),
+                ws["k"].data_ptr(), ws["v"].data_ptr(), g.N, tmap[2], st,
             )  # fmt: skip
-        K.flash_attention(ws["q"], ws["k"], ws["v"], ws["o"].view(g.batch, g.N, g.d))
-        for stream, rows, rpb, tmap, off in segs:
-            self._branch_tail(block, nxt, stream, rows, rpb, tmap, off, ws, g, eps, st)
-
-    def _single_block(self, block, nxt, ws, g, cos, sin, eps, st) -> None:
-        cfg = self.cfg
-        rows = g.batch * g.N
-        K.gemm(ws["hj"], block.qkv["j"], ws["qkv"])
-        qn, kn = block.qk_norm["j"]
-        _lib.call(
-            "iris_qkv_heads", ws["qkv"].data_ptr(), g.batch, g.N, block.qkv["j"].shape[0], cfg.num_heads, cfg.kv_heads,
-            qn.data_ptr(), kn.data_ptr(), cos.data_ptr(), sin.data_ptr(), eps, ws["q"].data_ptr(), ws["k"].data_ptr(),
-            ws["v"].data_ptr(), g.N, 0, st,
+        grouped(None, block.gate, "glog")  # gate logits; sigmoid in the attention epilogue
+        split = g.T if block.dual else 0
+        bt = g.batch * split
+        K.flash_attention_split(
+            ws["q"], ws["k"], ws["v"], split, ws["og"][:bt] if bt else None, ws["og"][bt:],
+            ws["glog"][:bt] if bt else None, ws["glog"][bt:],
         )  # fmt: skip
-        K.flash_attention(ws["q"], ws["k"], ws["v"], ws["o"].view(g.batch, g.N, g.d))
-        self._branch_tail(block, nxt, "j", rows, g.N, (rows, 0, 0), 0, ws, g, eps, st)
+        grouped("og", block.proj, "branch")
+        for s, rows, rpb, tmap, off in segs:
+            self._attn_residual(block, s, rows, rpb, tmap, off, ws, g, eps, st)
+        grouped("h2", block.w13, "act", epilogue=_lib.EPI_SWIGLU)
+        grouped("act", block.w2, "branch")
+        for s, rows, rpb, tmap, off in segs:
+            self._mlp_residual(block, nxt, s, rows, rpb, tmap, off, ws, g, eps, st)
 
-    def _branch_tail(self, block, nxt, stream, rows, rpb, tmap, off, ws, g, eps, st) -> None:
-        """gate -> out proj -> post-norm residual (+ norm2) -> SwiGLU -> post-norm residual (+ next input)."""
+    def _attn_residual(self, block, stream, rows, rpb, tmap, off, ws, g, eps, st) -> None:
+        """Post-norm + gate + residual of the attention branch, fused with the
+        MLP branch's input norm-modulate (written to ``h2``)."""
         d = g.d
         mods = self._mods(ws, block, stream)
         norms = block.norms[stream]
-        h, h2 = ws[_hkey(block)][off : off + rows], ws["h2"][off : off + rows]
-        gbuf, branch = ws["g"][off : off + rows], ws["branch"][off : off + rows]
-        # attention output rows of this stream live in the joint [B, N, D] tensor
-        aux_rows = tmap if stream != "j" else (rows, 0, 0)
-        K.gemm(h, block.gate[stream], gbuf, epilogue=_lib.EPI_GATE, aux=ws["o"], aux_rows=aux_rows)
-        w, b = block.proj[stream]
-        K.gemm(gbuf, w, branch, bias=b)
-        tok = ws["tokens"].data_ptr()
+        h2, branch = ws["h2"][off : off + rows], ws["branch"][off : off + rows]
         _lib.call(
-            "iris_gated_residual_rms_norm", tok, *tmap, branch.data_ptr(), _lib.BF16, rows, 0, 0,
+            "iris_gated_residual_rms_norm", ws["tokens"].data_ptr(), *tmap, branch.data_ptr(), _lib.BF16, rows, 0, 0,
             norms["post_attn"].data_ptr(), self._chunk(mods, 2, d), 6 * d, rows, rpb, d, eps, _lib.NEXT_NORM_MODULATE,
             norms["norm2"].data_ptr(), self._chunk(mods, 3, d), self._chunk(mods, 4, d), 6 * d, h2.data_ptr(),
             _lib.BF16, rows, 0, 0, st,
         )  # fmt: skip
-        act = ws["act"][off : off + rows]
-        K.gemm(h2, block.w13[stream], act, epilogue=_lib.EPI_SWIGLU)
-        K.gemm(act, block.w2[stream], branch)
-        # the mlp residual also writes the next block's input
+
+    def _mlp_residual(self, block, nxt, stream, rows, rpb, tmap, off, ws, g, eps, st) -> None:
+        """Post-norm + gate + residual of the MLP branch; it also writes the next
+        block's input (or, after the last block, ``silu(t_emb + x)`` of the image rows)."""
+        d = g.d
+        mods = self._mods(ws, block, stream)
+        norms = block.norms[stream]
+        branch = ws["branch"][off : off + rows]
+        tok = ws["tokens"].data_ptr()
         if nxt is None:
             # last block: only image rows continue; they leave as s = silu(t_emb + x)
             image_map = (g.L, g.N, g.T)

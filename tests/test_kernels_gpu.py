@@ -205,7 +205,49 @@ def test_gemm_gate_epilogue_with_aux_rows(K):
     assert rel_err(out, expected) < 1e-2
 
 
+def test_gemm_grouped_runs_independent_problems(K):
+    """Text and image problems of a dual block in one launch, each with its own
+    weights, bias and epilogue, match separate reference products."""
+    from iris_b200._lib import EPI_SWIGLU
+    from iris_b200.model import pack_swiglu
+
+    gen = torch.Generator(device="cuda").manual_seed(21)
+    shapes = [(1000, 768, 256), (72, 512, 256), (300, 256, 384)]
+    a = [torch.randn(m, k, device="cuda", generator=gen).to(torch.bfloat16) for m, _, k in shapes]
+    w = [(torch.randn(n, k, device="cuda", generator=gen) * 0.05).to(torch.bfloat16) for _, n, k in shapes]
+    bias = torch.randn(768, device="cuda", generator=gen)
+    outs = [torch.empty(m, n, device="cuda", dtype=torch.bfloat16) for m, n, _ in shapes]
+    w13, _ = pack_swiglu(w[2][:128], w[2][128:], torch.zeros(8, 128, device="cuda", dtype=torch.bfloat16))
+    act = torch.empty(300, 128, device="cuda", dtype=torch.bfloat16)
+    problems = [
+        K.gemm_problem(a[0], w[0], outs[0], bias=bias),
+        K.gemm_problem(a[1], w[1], outs[1]),
+        K.gemm_problem(a[2], w13, act, epilogue=EPI_SWIGLU),
+    ]
+    K.gemm_grouped(problems, torch.cuda.current_stream().cuda_stream)
+    assert rel_err(outs[0], a[0].float() @ w[0].float().T + bias) < 1e-2
+    assert rel_err(outs[1], a[1].float() @ w[1].float().T) < 1e-2
+    ref = F.silu(a[2].float() @ w[2][:128].float().T) * (a[2].float() @ w[2][128:].float().T)
+    assert rel_err(act, ref) < 1e-2
+
+
 # -------------------------------------------------------------------- attention
+def test_flash_attention_split_gate_writes_each_stream_densely(K):
+    B, H, T, N = 2, 2, 16, 52
+    L = N - T
+    gen = torch.Generator(device="cuda").manual_seed(13)
+    q, k, v = (torch.randn(B, H, N, 128, device="cuda", generator=gen).to(torch.bfloat16) for _ in range(3))
+    gate = torch.randn(B * N, H * 128, device="cuda", generator=gen).to(torch.bfloat16)  # [text rows | image rows]
+    out = torch.full((B * N, H * 128), 7.0, device="cuda", dtype=torch.bfloat16)
+    K.flash_attention_split(q, k, v, T, out[: B * T], out[B * T :], gate[: B * T], gate[B * T :])
+    attn = ops.sdpa(q.float(), k.float(), v.float()).transpose(1, 2)  # [B, N, H, 128]
+    text = attn[:, :T].reshape(B * T, -1) * torch.sigmoid(gate[: B * T].float())
+    image = attn[:, T:].reshape(B * L, -1) * torch.sigmoid(gate[B * T :].float())
+    assert rel_err(out[: B * T], text) < 2e-2
+    assert rel_err(out[B * T :], image) < 2e-2
+
+
+
 @pytest.mark.parametrize("B,H,Hkv,N", [(1, 1, 1, 128), (2, 2, 1, 52), (2, 3, 3, 300), (1, 2, 2, 4352)])
 def test_flash_attention_matches_fp32_sdpa(K, B, H, Hkv, N):
     gen = torch.Generator(device="cuda").manual_seed(B * 100 + N)
