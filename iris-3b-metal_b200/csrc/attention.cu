@@ -10,14 +10,17 @@
 //               tensor pipe runs, in order,
 //                 O_0 += P_0 V_j,  S_0 = Q_0 K_{j+1}^T,  O_1 += P_1 V_j,  S_1 = Q_1 K_{j+1}^T
 //               so one tile's softmax overlaps the other tile's MMAs;
-//   warps 2..5  softmax of tile 0, warps 6..9 softmax of tile 1: one query row
-//               per thread (TMEM lane = row); running max / sum in fp32 in the
-//               exp2 domain; P is written as packed bf16 over the first 64
-//               columns of its own S in TMEM (read by the next TS MMA, which
-//               completes before the following S MMA overwrites them: the MMAs
-//               of one thread execute in issue order); O is rescaled in TMEM only
-//               when a row max grew by more than 2^8 (O and l share the stale
-//               max, so the result is exact); final O / l -> bf16 [b, n, h*128+d].
+//   warps 2..9  softmax of tile 0, warps 10..17 softmax of tile 1. A query row
+//               (TMEM lane) is shared by two warps, one per half of the 128 key
+//               columns; they combine the row max and sum through shared memory
+//               (a 64-thread named barrier per lane quarter). Running max / sum
+//               in fp32 in the exp2 domain; each half writes its P as packed
+//               bf16 over the first 32 of its own 64 score columns in TMEM (read
+//               by the next TS MMA, which completes before the following S MMA
+//               overwrites them: the MMAs of one thread execute in issue order);
+//               O is rescaled in TMEM only when a row max grew by more than 2^8
+//               (O and l share the stale max, so the result is exact); final
+//               O / l (times the sigmoid gate, if any) -> bf16 rows per stream.
 // TMEM: S_0 [0,128) S_1 [128,256) O_0 [256,384) O_1 [384,512).
 #include "common.cuh"
 #include "iris_abi_internal.h"
@@ -31,10 +34,11 @@ constexpr int BKV = 128;
 constexpr int D = 128;
 constexpr int HALF_BYTES = 128 * 64 * 2;  // 128 rows x 64 dims, 16 KB
 constexpr int TILE_BYTES = 2 * HALF_BYTES;  // 32 KB
-constexpr int THREADS = 64 + TILES * 128;   // 320
+constexpr int SOFTMAX_WARPS_PER_TILE = 8;  // two warps per TMEM lane quarter, one per key-column half
+constexpr int THREADS = 64 + TILES * SOFTMAX_WARPS_PER_TILE * 32;  // 576
 constexpr uint32_t COL_S = 0, COL_O = 256;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
-constexpr size_t SMEM_BYTES = 1024 + (TILES + 4) * TILE_BYTES + 256;
+constexpr size_t SMEM_BYTES = 1024 + (TILES + 4) * TILE_BYTES + 8192;
 
 struct Smem {
   uint64_t q_full;
@@ -43,6 +47,8 @@ struct Smem {
   uint64_t teardown;
   uint32_t tmem_base;
   int abort;
+  float row_max[2][TILES][2][BQ];  // [iteration parity][tile][column half][row]
+  float row_sum[TILES][2][BQ];
 };
 
 struct Params {
@@ -81,6 +87,10 @@ IRIS_DEVICE float2 add2(float2 a, float2 b) {
       : "=f"(d.x), "=f"(d.y)
       : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
   return d;
+}
+
+IRIS_DEVICE void named_barrier_sync(uint32_t id, uint32_t threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
 IRIS_DEVICE float max3(float a, float b, float c) {
@@ -154,7 +164,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int t = 0; t < TILES; ++t) {
       mbar_init(&s->s_full[t], 1);
-      mbar_init(&s->p_full[t], 4);
+      mbar_init(&s->p_full[t], SOFTMAX_WARPS_PER_TILE);
       mbar_init(&s->o_final[t], 1);
     }
     mbar_init(&s->teardown, 1);
@@ -223,13 +233,15 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         umma_commit(&s->s_full[t]);
       };
-      // O_t += P_t V_j, P_t packed bf16 in the first 64 columns of S_t
+      // O_t += P_t V_j. P of keys [0, 64) is packed bf16 in S_t columns [0, 32),
+      // keys [64, 128) in columns [64, 96): each softmax half overwrites its own scores
       auto issue_pv = [&](int t, int j) {
         const uint32_t v_addr = smem_addr(v_tile + (j & 1) * TILE_BYTES);
 #pragma unroll
         for (int kk = 0; kk < BKV / 16; ++kk) {
           const uint64_t bd = umma_desc(v_addr + kk * 16 * 128, HALF_BYTES, 1024, kLayoutSw128);
-          umma_ts(tmem + COL_O + t * D, tmem + COL_S + t * BKV + kk * 8, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          const uint32_t p_col = COL_S + t * BKV + (kk >> 2) * 64 + (kk & 3) * 8;
+          umma_ts(tmem + COL_O + t * D, tmem + p_col, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
         }
       };
       bool ok = mbar_wait(&s->q_full, 0, abort) && mbar_wait(&s->k_full[0], 0, abort);
@@ -264,11 +276,19 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------- softmax
-    const int tile = (warp - 2) / 4;
+    // Warp w >= 2: tile (w - 2) / 8, column half ((w - 2) / 4) % 2, TMEM lane
+    // quarter w % 4 (its rows). The two warps of a (tile, quarter) hold the
+    // same 32 query rows, key columns [0, 64) and [64, 128) respectively, and
+    // combine row maxima and sums through shared memory.
+    const int sw = warp - 2;
+    const int tile = sw / SOFTMAX_WARPS_PER_TILE;
+    const int half = (sw / 4) & 1;
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
+    const uint32_t bar_id = 1 + tile * 4 + quarter;  // named barrier of the two warps
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t s_col = COL_S + tile * BKV, o_col = COL_O + tile * D;
+    const uint32_t s_col = COL_S + tile * BKV + half * 64;  // this half's 64 score columns
+    const uint32_t o_col = COL_O + tile * D + half * 64;    // and 64 output columns
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
@@ -277,32 +297,36 @@ __global__ void __launch_bounds__(THREADS, 1)
         break;
       }
       tc_fence_after();
-      // Two passes over the scores in TMEM keep ~64 of them in registers at a
-      // time: pass 1 the row max, pass 2 exp / sum / pack per 32-column chunk.
-      const int valid = n - j * BKV;
-      const bool tail = valid < BKV;  // last key block: keys past the sequence end do not exist
+      const int valid = n - j * BKV - half * 64;  // keys of this half that exist
+      const bool tail = valid < 64;
+      // pass 1: this half's row max, combined with the other half's
       float mx;
       {
-        uint32_t r[32];
+        uint32_t r[2][32];
+        tmem_ld32(tmem + lane_addr + s_col, r[0]);
+        tmem_ld32(tmem + lane_addr + s_col + 32, r[1]);
+        tmem_wait_ld();
         float ma = -INFINITY, mb = -INFINITY, mc = -INFINITY, md = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          tmem_ld32(tmem + lane_addr + s_col + c * 32, r);
-          tmem_wait_ld();
+        for (int c = 0; c < 2; ++c) {
           if (tail) {
 #pragma unroll
             for (int e = 0; e < 32; ++e)
-              if (c * 32 + e >= valid) r[e] = __float_as_uint(-INFINITY);
+              if (c * 32 + e >= valid) r[c][e] = __float_as_uint(-INFINITY);
           }
 #pragma unroll
           for (int e = 0; e < 32; e += 8) {
-            ma = max3(ma, __uint_as_float(r[e]), __uint_as_float(r[e + 1]));
-            mb = max3(mb, __uint_as_float(r[e + 2]), __uint_as_float(r[e + 3]));
-            mc = max3(mc, __uint_as_float(r[e + 4]), __uint_as_float(r[e + 5]));
-            md = max3(md, __uint_as_float(r[e + 6]), __uint_as_float(r[e + 7]));
+            ma = max3(ma, __uint_as_float(r[c][e]), __uint_as_float(r[c][e + 1]));
+            mb = max3(mb, __uint_as_float(r[c][e + 2]), __uint_as_float(r[c][e + 3]));
+            mc = max3(mc, __uint_as_float(r[c][e + 4]), __uint_as_float(r[c][e + 5]));
+            md = max3(md, __uint_as_float(r[c][e + 6]), __uint_as_float(r[c][e + 7]));
           }
         }
-        mx = fmaxf(max3(ma, mb, mc), md) * p.scale_log2;
+        const float part = fmaxf(max3(ma, mb, mc), md);
+        float* xchg = s->row_max[j & 1][tile][half];
+        xchg[row] = part;
+        named_barrier_sync(bar_id, 64);
+        mx = fmaxf(part, s->row_max[j & 1][tile][half ^ 1][row]) * p.scale_log2;
       }
       // lazy rescale: keep the stale max unless it grew by more than 2^8
       const bool grow = j == 0 || mx > m_run + RESCALE_THRESHOLD;
@@ -311,7 +335,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (j > 0 && __any_sync(0xffffffffu, grow)) {
         // O_t holds the P V of earlier blocks: S_t(j) completing implies they completed
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t r[32];
           tmem_ld32(tmem + lane_addr + o_col + c * 32, r);
           tmem_wait_ld();
@@ -325,18 +349,17 @@ __global__ void __launch_bounds__(THREADS, 1)
           tmem_st16(tmem + lane_addr + o_col + c * 32 + 16, hi);
         }
       }
+      // pass 2: P = 2^(s * scale - m) for this half; packed bf16 over its first 32 columns
       const float2 scale2 = make_float2(p.scale_log2, p.scale_log2);
       const float2 shift2 = make_float2(-m_new, -m_new);
       float2 rs2 = make_float2(0.f, 0.f);
-      // chunk c + 1 is loaded while chunk c is processed; P of chunk c goes to
-      // columns [16c, 16c + 16), whose scores were read by an earlier chunk
       uint32_t buf[2][32];
       tmem_ld32(tmem + lane_addr + s_col, buf[0]);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         tmem_wait_ld();
-        if (c + 1 < 4) tmem_ld32(tmem + lane_addr + s_col + (c + 1) * 32, buf[(c + 1) & 1]);
-        uint32_t(&r)[32] = buf[c & 1];
+        if (c == 0) tmem_ld32(tmem + lane_addr + s_col + 32, buf[1]);
+        uint32_t(&r)[32] = buf[c];
         if (tail) {
 #pragma unroll
           for (int e = 0; e < 32; ++e)
@@ -345,11 +368,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const float2 s = make_float2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
+          const float2 sv = make_float2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
 #if IRIS_ATTN_PACKED
-          const float2 x = fma2(s, scale2, shift2);
+          const float2 x = fma2(sv, scale2, shift2);
 #else
-          const float2 x = make_float2(fmaf(s.x, scale2.x, shift2.x), fmaf(s.y, scale2.y, shift2.y));
+          const float2 x = make_float2(fmaf(sv.x, scale2.x, shift2.x), fmaf(sv.y, scale2.y, shift2.y));
 #endif
           float2 pe;
           if (e < EMU_PAIRS && !tail) {
@@ -366,6 +389,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #endif
           pk[e] = pack_bf16x2(pe.x, pe.y);
         }
+        // chunk c's P goes to columns [16c, 16c + 16) of this half, scores already read
         tmem_st16(tmem + lane_addr + s_col + c * 16, pk);
       }
       l_run = l_run * corr + (rs2.x + rs2.y);
@@ -375,25 +399,29 @@ __global__ void __launch_bounds__(THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&s->p_full[tile]);
     }
+    // the row sum over both halves
+    s->row_sum[tile][half][row] = l_run;
+    named_barrier_sync(bar_id, 64);
+    const float l_total = l_run + s->row_sum[tile][half ^ 1][row];
     // output row of this query and its gate logits, fetched while the last P V runs
     const int q = q0 + tile * BQ + row;
     const bool text = q < p.split;
     const int64_t orow = text ? static_cast<int64_t>(b) * p.split + q
                               : static_cast<int64_t>(b) * (p.n - p.split) + (q - p.split);
-    const int64_t off = orow * p.row_stride + static_cast<int64_t>(h) * D;
+    const int64_t off = orow * p.row_stride + static_cast<int64_t>(h) * D + half * 64;
     const __nv_bfloat16* gate = text ? p.gate_text : p.gate_image;
-    uint4 gate_row[16];
+    uint4 gate_row[8];
     if (gate != nullptr && q < n) {
       const uint4* g4 = reinterpret_cast<const uint4*>(gate + off);
 #pragma unroll
-      for (int e = 0; e < 16; ++e) gate_row[e] = g4[e];
+      for (int e = 0; e < 8; ++e) gate_row[e] = g4[e];
     }
     if (ok && __all_sync(0xffffffffu, mbar_wait(&s->o_final[tile], 0, abort))) {
       tc_fence_after();
       __nv_bfloat16* dst = (text ? p.o_text : p.o_image) + off;
-      const float inv = 1.f / l_run;
+      const float inv = 1.f / l_total;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t r[32];
         tmem_ld32(tmem + lane_addr + o_col + c * 32, r);
         tmem_wait_ld();

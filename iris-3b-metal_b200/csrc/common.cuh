@@ -248,6 +248,97 @@ IRIS_DEVICE void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
       : "memory");
 }
 
+// ------------------------------------------------- CTA pairs (cta_group::2)
+IRIS_DEVICE uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// shared::cluster address of the same shared variable in CTA `rank` of the cluster
+IRIS_DEVICE uint32_t map_to_cta(const void* p, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_addr(p)), "r"(rank));
+  return out;
+}
+
+IRIS_DEVICE void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+IRIS_DEVICE void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+IRIS_DEVICE bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait (see mbar_wait) with cluster-scope acquire, for barriers that
+// the other CTA of a pair arrives on.
+IRIS_DEVICE bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t start = global_timer_ns();
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (*abort) return false;
+    if ((i & 63u) == 63u && global_timer_ns() - start > kWaitLimitNs) {
+      *abort = 1;
+      atomicOr(&g_device_error, kErrWaitTimeout);
+      return false;
+    }
+  }
+}
+
+// TMA load issued by either CTA of a pair; completion bytes are counted on the
+// mbarrier at `bar_cluster_addr` (the leader CTA's barrier).
+IRIS_DEVICE void tma_load_2d_pair(const CUtensorMap* map, uint32_t bar_cluster_addr, void* dst, int32_t c0,
+                                  int32_t c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+      "%4}], [%2];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+IRIS_DEVICE void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst_smem)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+IRIS_DEVICE void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// D[tmem of both CTAs] (+)= A[smem of both CTAs] * B[smem of both CTAs]^T, M = 256, issued by the leader.
+IRIS_DEVICE void umma_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on the mbarrier at `bar_cluster_addr` (either CTA of the pair) once the
+// pair MMAs issued so far by this thread complete.
+IRIS_DEVICE void umma_commit_pair(uint32_t bar_cluster_addr) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar_cluster_addr)
+               : "memory");
+}
+
 IRIS_DEVICE bool elect_one() {
   uint32_t pred = 0;
   asm volatile(

@@ -27,6 +27,11 @@
 #include "common.cuh"
 #include "iris_abi_internal.h"
 
+// 1: batches whose problems all have M >= 256 run on the CTA-pair kernel.
+#ifndef IRIS_GEMM_PAIR
+#define IRIS_GEMM_PAIR 1
+#endif
+
 namespace iris {
 namespace gemm {
 
@@ -318,6 +323,245 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
 }
 
+// ---------------------------------------------------------------------------
+// CTA-pair form (cta_group::2): a cluster of two CTAs on paired SMs computes a
+// 256 x 256 tile. Each CTA TMA-loads its own 128 rows of A and its half (128
+// rows) of the W tile, 32 KB per 64-wide K slab, into a 6-stage ring. Both
+// CTAs' copies complete on the leader CTA's "full" barrier, whose byte count
+// the leader's producer alone announces for the pair (a remote arrive from the
+// peer's producer on every slab halved the kernel's rate). The leader's
+// MMA thread issues tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 16), which
+// reads A and W from both CTAs' shared memory and writes each CTA's 128 rows x
+// 256 fp32 columns into that CTA's TMEM; its commits are sent to each CTA's
+// barrier separately. Both CTAs run the same epilogue on their own rows; the
+// peer's epilogue warps release an accumulator with remote arrivals on the
+// leader's barrier. Per SM this halves the W bytes each k-slab brings in.
+namespace pair {
+constexpr int BM = 256;  // pair tile rows, 128 per CTA
+constexpr int STAGES = 6;
+constexpr int A_BYTES = 128 * BK * 2;  // 16 KB: this CTA's rows
+constexpr int B_BYTES = 128 * BK * 2;  // 16 KB: this CTA's half of the W tile
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr size_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
+
+struct Smem {
+  uint64_t full[STAGES];  // used in the leader only: both CTAs' copies complete here
+  uint64_t empty[STAGES];
+  uint64_t tmem_full[2];
+  uint64_t tmem_empty[2];  // used in the leader only: 4 local + 4 peer epilogue warps
+  uint64_t teardown;
+  uint32_t tmem_base;
+  int abort;
+};
+}  // namespace pair
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    gemm_bf16_pair_kernel(const __grid_constant__ TensorMaps maps, const __grid_constant__ Batch bt) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* tiles = base;
+  pair::Smem* s = reinterpret_cast<pair::Smem*>(base + pair::STAGES * pair::STAGE_BYTES);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int num_tiles = bt.tile_start[bt.count];
+  const int pair_id = blockIdx.x / 2;
+  const int pairs = gridDim.x / 2;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < pair::STAGES; ++i) {
+      mbar_init(&s->full[i], 1);
+      mbar_init(&s->empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s->tmem_full[i], 1);
+      mbar_init(&s->tmem_empty[i], 8);
+    }
+    mbar_init(&s->teardown, 1);
+    s->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    for (int p = 0; p < bt.count; ++p) {
+      tma_prefetch_desc(&maps.a[p]);
+      tma_prefetch_desc(&maps.b[p]);
+    }
+  }
+  if (warp == 1) tmem_alloc_pair(&s->tmem_base, TMEM_COLS);
+  tc_fence_before();
+  cluster_sync();  // every barrier of both CTAs exists before any remote arrival
+  tc_fence_after();
+  const uint32_t tmem = s->tmem_base;
+  volatile int* abort = &s->abort;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int t = pair_id; t < num_tiles && ok; t += pairs) {
+        const Tile tl = locate(bt, t);
+        const CUtensorMap* ma = &maps.a[tl.p];
+        const CUtensorMap* mw = &maps.b[tl.p];
+        const int nk = bt.prob[tl.p].nk;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&s->empty[stage], phase ^ 1u, abort)) {
+            ok = false;
+            break;
+          }
+          const uint32_t full_leader = map_to_cta(&s->full[stage], 0);
+          uint8_t* a_dst = tiles + stage * pair::STAGE_BYTES;
+          uint8_t* b_dst = a_dst + pair::A_BYTES;
+          // The leader announces both CTAs' bytes; the peer's copies may land
+          // first (the transaction count dips below zero until it does).
+          if (leader) mbar_arrive_expect_tx(&s->full[stage], 2 * pair::STAGE_BYTES);
+          tma_load_2d_pair(ma, full_leader, a_dst, kb * BK, tl.mb * pair::BM + static_cast<int>(rank) * 128);
+          tma_load_2d_pair(mw, full_leader, b_dst, kb * BK, tl.nb * BN + static_cast<int>(rank) * 128);
+          ++issued;
+          if (++stage == pair::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok && issued > 0) {
+        // the loads in flight target both CTAs' shared memory: give them time to land
+        const uint64_t t0 = global_timer_ns();
+        while (global_timer_ns() - t0 < 1000000ull) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader)
+    if (lane == 0 && leader) {
+      const uint32_t idesc = idesc_bf16_f32(pair::BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int t = pair_id; t < num_tiles && ok; t += pairs, ++it) {
+        const int nk = bt.prob[locate(bt, t).p].nk;
+        const int acc = it & 1;
+        const uint32_t acc_phase = static_cast<uint32_t>((it >> 1) & 1);
+        if (!mbar_wait_cluster(&s->tmem_empty[acc], acc_phase ^ 1u, abort)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&s->full[stage], phase, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_addr(tiles + stage * pair::STAGE_BYTES);
+          const uint32_t b_addr = a_addr + pair::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = umma_desc(a_addr + k * 32, 16, 1024, kLayoutSw128);
+            const uint64_t bd = umma_desc(b_addr + k * 32, 16, 1024, kLayoutSw128);
+            umma_ss_pair(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair(map_to_cta(&s->empty[stage], 0));
+          umma_commit_pair(map_to_cta(&s->empty[stage], 1));
+          if (++stage == pair::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) {
+          umma_commit_pair(map_to_cta(&s->tmem_full[acc], 0));
+          umma_commit_pair(map_to_cta(&s->tmem_full[acc], 1));
+        }
+      }
+      umma_commit_pair(map_to_cta(&s->teardown, 0));
+      int dummy = 0;
+      mbar_wait(&s->teardown, 0, &dummy);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    const uint32_t empty_leader = map_to_cta(&s->tmem_empty[0], 0);
+    int it = 0;
+    for (int t = pair_id; t < num_tiles; t += pairs, ++it) {
+      const Tile tl = locate(bt, t);
+      const Problem& p = bt.prob[tl.p];
+      const int acc = it & 1;
+      const uint32_t acc_phase = static_cast<uint32_t>((it >> 1) & 1);
+      if (!__all_sync(0xffffffffu, mbar_wait_cluster(&s->tmem_full[acc], acc_phase, abort))) break;
+      tc_fence_after();
+      const uint32_t t_base = tmem + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(quarter * 32) << 16);
+      const int64_t m = static_cast<int64_t>(tl.mb) * pair::BM + static_cast<int64_t>(rank) * 128 + row_in_tile;
+      const bool row_ok = m < p.M;
+      const int64_t prow = row_ok ? p.out_map(m) : 0;
+      if (p.epilogue == EPI_SWIGLU) {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t ra[32], rb[32];
+          tmem_ld32(t_base + c * 32, ra);
+          tmem_ld32(t_base + 128 + c * 32, rb);
+          tmem_wait_ld();
+          const int col0 = tl.nb * (BN / 2) + c * 32;
+          if (row_ok && col0 < p.N / 2) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float a = __uint_as_float(ra[j]);
+              v[j] = a * sigmoidf_fast(a) * __uint_as_float(rb[j]);
+            }
+            store_row32(p, prow, col0, v);
+          }
+        }
+      } else {
+        const int64_t arow = (row_ok && p.epilogue == EPI_GATE) ? p.aux_map(m) : 0;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(t_base + c * 32, r);
+          tmem_wait_ld();
+          const int col0 = tl.nb * BN + c * 32;
+          if (row_ok && col0 < p.N) {
+            float v[32];
+            if (p.epilogue == EPI_GATE) {
+              const uint4* a4 = reinterpret_cast<const uint4*>(p.aux + arow * p.ldaux + col0);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const uint4 w = a4[j];
+                const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                  const float2 f = unpack_bf16x2(ws[h]);
+                  const int e = j * 8 + h * 2;
+                  v[e] = f.x * sigmoidf_fast(__uint_as_float(r[e]));
+                  v[e + 1] = f.y * sigmoidf_fast(__uint_as_float(r[e + 1]));
+                }
+              }
+            } else if (p.bias != nullptr) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) + __ldg(p.bias + col0 + j);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+            }
+            store_row32(p, prow, col0, v);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(empty_leader + static_cast<uint32_t>(acc) * 8u);
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();  // no CTA leaves while the other may still address its barriers or TMEM
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem, TMEM_COLS);
+}
+
 int check_problem(const iris_gemm_problem& q) {
   IRIS_REQUIRE(q.a && q.w && q.out, "iris_gemm_bf16: null pointer");
   IRIS_REQUIRE(q.M > 0 && q.N > 0 && q.K > 0, "iris_gemm_bf16: empty problem");
@@ -353,6 +597,12 @@ extern "C" int iris_gemm_bf16_grouped(const iris_gemm_problem* problems, int cou
   using namespace iris::gemm;
   IRIS_REQUIRE(problems != nullptr && count >= 1 && count <= MAX_PROBLEMS,
                "iris_gemm_bf16_grouped: 1 to 4 problems per launch");
+  // The CTA-pair kernel runs a batch whose every problem fills at least one
+  // 256-row pair tile; smaller problems keep the one-SM kernel.
+  bool use_pair = IRIS_GEMM_PAIR != 0;
+  for (int i = 0; i < count; ++i) use_pair = use_pair && problems[i].M >= pair::BM;
+  const int bm = use_pair ? pair::BM : BM;
+  const int w_box_rows = use_pair ? BN / 2 : BN;
   TensorMaps maps;
   Batch bt;
   bt.count = count;
@@ -362,12 +612,12 @@ extern "C" int iris_gemm_bf16_grouped(const iris_gemm_problem* problems, int cou
     const iris_gemm_problem& q = problems[i];
     IRIS_CHECK_STATUS(check_problem(q));
     IRIS_CHECK_STATUS(make_tmap_2d_bf16(&maps.a[i], q.a, q.K, q.M, q.lda, BK, BM));
-    IRIS_CHECK_STATUS(make_tmap_2d_bf16(&maps.b[i], q.w, q.K, q.N, q.ldw, BK, BN));
+    IRIS_CHECK_STATUS(make_tmap_2d_bf16(&maps.b[i], q.w, q.K, q.N, q.ldw, BK, w_box_rows));
     Problem& p = bt.prob[i];
     p.M = static_cast<int>(q.M);
     p.N = static_cast<int>(q.N);
     p.K = static_cast<int>(q.K);
-    p.num_m = static_cast<int>((q.M + BM - 1) / BM);
+    p.num_m = static_cast<int>((q.M + bm - 1) / bm);
     p.num_n = static_cast<int>((q.N + BN - 1) / BN);
     p.nk = static_cast<int>((q.K + BK - 1) / BK);
     p.epilogue = q.epilogue;
@@ -380,7 +630,7 @@ extern "C" int iris_gemm_bf16_grouped(const iris_gemm_problem* problems, int cou
     p.ldaux = q.ldaux;
     p.aux_map = RowMap{q.aux_seg_rows, q.aux_seg_stride, q.aux_seg_offset};
     total += static_cast<int64_t>(p.num_m) * p.num_n;
-    IRIS_REQUIRE(total < (1ll << 31), "iris_gemm_bf16_grouped: too many tiles");
+    IRIS_REQUIRE(total < (1ll << 30), "iris_gemm_bf16_grouped: too many tiles");
     bt.tile_start[i + 1] = static_cast<int>(total);
   }
   static bool configured[64] = {false};
@@ -389,10 +639,32 @@ extern "C" int iris_gemm_bf16_grouped(const iris_gemm_problem* problems, int cou
   if (dev < 64 && !configured[dev]) {
     IRIS_CUDA(cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    static_cast<int>(SMEM_BYTES)));
+    IRIS_CUDA(cudaFuncSetAttribute(gemm_bf16_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(pair::SMEM_BYTES)));
     configured[dev] = true;
   }
-  const int grid = total < num_sms() ? static_cast<int>(total) : num_sms();
-  gemm_bf16_kernel<<<grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(maps, bt);
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (use_pair) {
+    // Not every SM has a partner SM that a cluster of two can use: size the
+    // persistent grid to the clusters that are resident at once, or the tiles
+    // of the clusters left over would run as a second wave.
+    static int resident_pairs[64] = {0};
+    int limit = dev < 64 ? resident_pairs[dev] : 0;
+    if (limit == 0) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(static_cast<unsigned>(num_sms()));
+      cfg.blockDim = dim3(THREADS);
+      cfg.dynamicSmemBytes = pair::SMEM_BYTES;
+      IRIS_CUDA(cudaOccupancyMaxActiveClusters(&limit, gemm_bf16_pair_kernel, &cfg));
+      IRIS_REQUIRE(limit > 0, "iris_gemm_bf16_grouped: no CTA pair fits on this device");
+      if (dev < 64) resident_pairs[dev] = limit;
+    }
+    const int pairs = total < limit ? static_cast<int>(total) : limit;
+    gemm_bf16_pair_kernel<<<2 * pairs, THREADS, pair::SMEM_BYTES, st>>>(maps, bt);
+  } else {
+    const int grid = total < num_sms() ? static_cast<int>(total) : num_sms();
+    gemm_bf16_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(maps, bt);
+  }
   IRIS_CUDA(cudaGetLastError());
   return IRIS_OK;
 }

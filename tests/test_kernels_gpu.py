@@ -140,7 +140,16 @@ def test_pixel_kernels_reject_short_parameter_buffers(K):
 
 
 # ------------------------------------------------------------------------- GEMM
-GEMM_SHAPES = [(128, 256, 64), (200, 96, 48), (1000, 544, 312), (8704 // 8, 9216 // 8, 3072 // 4), (64, 1280, 1280)]
+# M >= 256 runs the CTA-pair kernel (256-row tiles); (4096, 2560, 512) gives
+# every SM pair several tiles, so both TMEM accumulators and the ring wrap.
+GEMM_SHAPES = [
+    (128, 256, 64),
+    (200, 96, 48),
+    (1000, 544, 312),
+    (8704 // 8, 9216 // 8, 3072 // 4),
+    (64, 1280, 1280),
+    (4096, 2560, 512),
+]
 
 
 @pytest.mark.parametrize("M,N,K_", GEMM_SHAPES)
@@ -229,6 +238,43 @@ def test_gemm_grouped_runs_independent_problems(K):
     assert rel_err(outs[1], a[1].float() @ w[1].float().T) < 1e-2
     ref = F.silu(a[2].float() @ w[2][:128].float().T) * (a[2].float() @ w[2][128:].float().T)
     assert rel_err(act, ref) < 1e-2
+
+
+def test_gemm_pair_kernel_epilogues_and_row_maps(K):
+    """All problems with M >= 256 take the CTA-pair kernel: bias + row map, gate
+    with aux rows and SwiGLU in one launch, ragged last pair tiles included."""
+    from iris_b200._lib import EPI_GATE, EPI_SWIGLU
+    from iris_b200.model import pack_swiglu
+
+    gen = torch.Generator(device="cuda").manual_seed(33)
+    T, L, B, D = 40, 300, 2, 512
+    N = T + L
+    a0 = torch.randn(B * L, 256, device="cuda", generator=gen).to(torch.bfloat16)
+    w0 = (torch.randn(D, 256, device="cuda", generator=gen) * 0.05).to(torch.bfloat16)
+    bias = torch.randn(D, device="cuda", generator=gen)
+    joint = torch.full((B * N, D), -7.0, device="cuda")
+    wg = (torch.randn(D, 256, device="cuda", generator=gen) * 0.05).to(torch.bfloat16)
+    attn = torch.randn(B * N, D, device="cuda", generator=gen).to(torch.bfloat16)
+    gated = torch.empty(B * L, D, device="cuda", dtype=torch.bfloat16)
+    M2, F_ = 260, 384
+    a2 = torch.randn(M2, 256, device="cuda", generator=gen).to(torch.bfloat16)
+    w1, w3 = ((torch.randn(F_, 256, device="cuda", generator=gen) * 0.05).to(torch.bfloat16) for _ in range(2))
+    w13, _ = pack_swiglu(w1, w3, torch.zeros(8, F_, device="cuda", dtype=torch.bfloat16))
+    act = torch.empty(M2, w13.shape[0] // 2, device="cuda", dtype=torch.bfloat16)
+    problems = [
+        K.gemm_problem(a0, w0, joint, bias=bias, out_rows=(L, N, T)),
+        K.gemm_problem(a0, wg, gated, epilogue=EPI_GATE, aux=attn, aux_rows=(L, N, T)),
+        K.gemm_problem(a2, w13, act, epilogue=EPI_SWIGLU),
+    ]
+    K.gemm_grouped(problems, torch.cuda.current_stream().cuda_stream)
+    got = joint.view(B, N, D)
+    assert rel_err(got[:, T:], (a0.float() @ w0.float().T + bias).view(B, L, D)) < 1e-4
+    assert torch.all(got[:, :T] == -7.0)
+    gate_ref = attn.view(B, N, D)[:, T:].reshape(B * L, D).float() * torch.sigmoid(a0.float() @ wg.float().T)
+    assert rel_err(gated, gate_ref) < 1e-2
+    h = F.silu(a2.float() @ w1.float().T) * (a2.float() @ w3.float().T)
+    assert rel_err(act[:, :F_], h) < 1e-2
+    assert torch.all(act[:, F_:] == 0)
 
 
 # -------------------------------------------------------------------- attention
