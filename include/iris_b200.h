@@ -94,11 +94,16 @@ int iris_qk_norm_rope(const void* x, int x_dtype, int64_t batch, int64_t tokens,
 
 /* One projection [b, n, (heads_q + 2 heads_kv) * 128] (bf16, columns q | k | v,
  * head-major: src/iris3b/models/blocks/single_stream.py:111-117) -> q and k
- * normed + rotated, v re-laid, all bf16 [b, h, offset + n, 128] (the reference
- * does this with qk_norm_rope twice plus a V copy, src/iris_metal/model.py:243-250). */
+ * normed + rotated by cos/sin[offset + n], v re-laid, all bf16: q as
+ * [b, h, offset + n, 128] of n_out tokens per (b, h), k and v likewise of
+ * n_out_kv tokens (the reference does this with qk_norm_rope twice plus a V
+ * copy, src/iris_metal/model.py:243-250). head_major = 1 writes
+ * [h, b, offset + n, 128] instead: each head's rows of every sample are
+ * contiguous, the send layout of a sequence-parallel all-to-all. */
 int iris_qkv_heads(const void* qkv, int64_t batch, int64_t tokens, int64_t row_stride, int64_t heads_q,
                    int64_t heads_kv, const float* q_weight, const float* k_weight, const float* cos, const float* sin,
-                   float eps, void* q_out, void* k_out, void* v_out, int64_t n_out, int64_t offset, void* stream);
+                   float eps, void* q_out, void* k_out, void* v_out, int64_t n_out, int64_t n_out_kv, int64_t offset,
+                   int head_major, void* stream);
 
 /* ---- tensor-core kernels ------------------------------------------------ */
 /* F.linear in the step (src/iris_metal/model.py:46-52): C = epi(A W^T).
@@ -147,11 +152,13 @@ int iris_flash_attn_fwd(const void* q, const void* k, const void* v, void* o, in
  * of sample b goes to row b * split + i of o_text, token i >= split to row
  * b * (n - split) + i - split of o_image; o = attn * sigmoid(gate logit), the
  * bf16 logits read from the same rows of gate_text / gate_image (both null:
- * no gate). split = 0 writes every token to o_image. */
+ * no gate). split = 0 writes every token to o_image. q holds n queries and
+ * k / v hold n_kv keys per (b, h); n_kv may differ from n (a sequence-
+ * parallel rank's own queries over the keys of the whole sequence). */
 int iris_flash_attn_fwd_split(const void* q, const void* k, const void* v, int64_t batch, int64_t heads_q,
-                              int64_t heads_kv, int64_t n, int64_t head_dim, float scale, int64_t split, void* o_text,
-                              void* o_image, const void* gate_text, const void* gate_image, int64_t row_stride,
-                              void* stream);
+                              int64_t heads_kv, int64_t n, int64_t n_kv, int64_t head_dim, float scale, int64_t split,
+                              void* o_text, void* o_image, const void* gate_text, const void* gate_image,
+                              int64_t row_stride, void* stream);
 
 /* ---- pixel stage -------------------------------------------------------- */
 /* pixel_rms_norm, src/iris_metal/kernels.py:486-498 (MSL :217-232): bf16 out. */
@@ -171,26 +178,43 @@ int iris_pixel_mlp(void* pixels, int pixel_dtype, const void* branch, const void
 /* The last pixel block fused with FinalLayer (src/iris3b/models/dit.py:53-62)
  * and the fold (dit.py:367-374): same update as iris_pixel_mlp, then
  * v[b, c, y, x] = final_w[c] . rms_norm(pixels) * final_norm_weight + final_b[c]
- * written straight into the [b, 3, H, W] fp32 velocity. */
+ * written straight into the [b, 3, H, W] fp32 velocity. The pixels belong to
+ * patch tokens [token_start, token_start + tokens) of each sample (all L of
+ * them, or one sequence-parallel rank's share); only their pixels of v are
+ * written. */
 int iris_pixel_mlp_head(void* pixels, int pixel_dtype, const void* branch, const void* mods,
                         const float* norm_weight, const void* fc1_w, const void* fc1_b, const void* fc2_w,
                         const void* fc2_b, const float* final_norm_weight, const float* final_w,
                         const float* final_b, float* v, int64_t batch, int64_t height, int64_t width, int64_t patch,
-                        float eps, void* stream);
+                        int64_t token_start, int64_t tokens, float eps, void* stream);
 
 /* PixelEmbedder.forward, src/iris3b/nn/embeddings.py:319-328, plus the first
- * block's pixel_rms_norm: pixels[(b, gy, gx), ky * p + kx, :] =
- * W x[b, :, y, x] + bias + pos[y * W + x, :] (pos may be null); normed = bf16
+ * block's pixel_rms_norm, for patch tokens l in [token_start, token_start +
+ * tokens): pixels[(b, l - token_start), ky * p + kx, :] = W x[b, :, y, x] +
+ * bias + pos[y * W + x, :] (pos may be null); normed = bf16
  * rms_norm(pixels) * norm_weight. d_pix == 16, channels == 3. */
 int iris_pixel_embed(const float* x, const float* w, const float* bias, const float* pos, void* pixels,
                      int pixel_dtype, void* normed, const float* norm_weight, float eps, int64_t batch,
-                     int64_t height, int64_t width, int64_t patch, void* stream);
+                     int64_t height, int64_t width, int64_t patch, int64_t token_start, int64_t tokens,
+                     void* stream);
 
 /* ---- layout and conditioning -------------------------------------------- */
-/* Patchify, src/iris_metal/model.py:188 / F.unfold in dit.py:326:
- * out[b * L + gy * gw + gx, c * p * p + ky * p + kx] = x[b, c, gy * p + ky, gx * p + kx] (bf16 out). */
+/* Patchify, src/iris_metal/model.py:188 / F.unfold in dit.py:326, for patch
+ * tokens l = gy * gw + gx in [token_start, token_start + tokens):
+ * out[b * tokens + l - token_start, c * p * p + ky * p + kx] = x[b, c, gy * p + ky, gx * p + kx] (bf16 out). */
 int iris_patchify(const float* x, void* out, int64_t batch, int64_t channels, int64_t height, int64_t width,
-                  int64_t patch, void* stream);
+                  int64_t patch, int64_t token_start, int64_t tokens, void* stream);
+
+/* Sequence-parallel (Ulysses) pack / unpack around the all-to-all exchanges
+ * (no reference counterpart: the reference runs on one device): for every
+ * (i0, i1, i2) < (count0, count1,
+ * count2), block_bytes contiguous bytes from src + i0 * src_stride0 + i1 *
+ * src_stride1 + i2 * src_stride2 to dst + i0 * dst_stride0 + ... (byte
+ * strides; pointers, strides and block_bytes multiples of 16; dst and src
+ * must not overlap). */
+int iris_block_copy(void* dst, int64_t dst_stride0, int64_t dst_stride1, int64_t dst_stride2, const void* src,
+                    int64_t src_stride0, int64_t src_stride1, int64_t src_stride2, int64_t count0, int64_t count1,
+                    int64_t count2, int64_t block_bytes, void* stream);
 
 /* Fold of a per-pixel head output, src/iris3b/models/dit.py:367-374:
  * v[b, c, gy * p + ky, gx * p + kx] = out[b * L + gy * gw + gx, ky * p + kx, c] (fp32). */

@@ -1,7 +1,9 @@
 // Flash attention forward on the 5th-generation tensor cores: non-causal,
 // unmasked softmax(Q K^T / sqrt(128)) V over the joint [text | image] sequence
 // (src/iris_metal/model.py:243-250; src/iris3b/nn/attention.py:61-91) and the
-// pixel-stage patch tokens (src/iris3b/models/blocks/pit.py:66-72).
+// pixel-stage patch tokens (src/iris3b/models/blocks/pit.py:66-72). Queries
+// and keys may differ in number (a sequence-parallel rank attends with its own
+// patch tokens over the gathered keys of all of them).
 //
 // One CTA per (256 queries = two 128-row tiles, head, batch). Warp roles:
 //   warp 0      TMA: both Q tiles once (two 64-dim halves each, 128B swizzle),
@@ -52,7 +54,7 @@ struct Smem {
 };
 
 struct Params {
-  int64_t batch, heads_q, heads_kv, n, row_stride, split;
+  int64_t batch, heads_q, heads_kv, n, n_kv, row_stride, split;  // n queries and n_kv keys per (b, h)
   float scale_log2;
   __nv_bfloat16* o_text;   // rows b * split + i       (i < split)
   __nv_bfloat16* o_image;  // rows b * (n - split) + i - split
@@ -149,10 +151,11 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int group = static_cast<int>(p.heads_q / p.heads_kv);
   const int hk = h / group;
   const int n = static_cast<int>(p.n);
-  const int nkv = (n + BKV - 1) / BKV;
+  const int n_kv = static_cast<int>(p.n_kv);
+  const int nkv = (n_kv + BKV - 1) / BKV;
   const int q0 = blockIdx.x * (TILES * BQ);  // first query of the CTA
   const int q_row0 = static_cast<int>((static_cast<int64_t>(b) * p.heads_q + h) * n) + q0;
-  const int kv_row0 = static_cast<int>((static_cast<int64_t>(b) * p.heads_kv + hk) * n);
+  const int kv_row0 = static_cast<int>((static_cast<int64_t>(b) * p.heads_kv + hk) * n_kv);
 
   if (threadIdx.x == 0) {
     mbar_init(&s->q_full, 1);
@@ -297,7 +300,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         break;
       }
       tc_fence_after();
-      const int valid = n - j * BKV - half * 64;  // keys of this half that exist
+      const int valid = n_kv - j * BKV - half * 64;  // keys of this half that exist
       const bool tail = valid < 64;
       // pass 1: this half's row max, combined with the other half's
       float mx;
@@ -464,7 +467,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 using namespace iris;
 
 extern "C" int iris_flash_attn_fwd_split(const void* q, const void* k, const void* v, int64_t batch,
-                                         int64_t heads_q, int64_t heads_kv, int64_t n, int64_t head_dim, float scale,
+                                         int64_t heads_q, int64_t heads_kv, int64_t n, int64_t n_kv,
+                                         int64_t head_dim, float scale,
                                          int64_t split, void* o_text, void* o_image, const void* gate_text,
                                          const void* gate_image, int64_t row_stride, void* stream) {
   using namespace iris::attn;
@@ -473,6 +477,7 @@ extern "C" int iris_flash_attn_fwd_split(const void* q, const void* k, const voi
   IRIS_REQUIRE(batch > 0 && heads_q > 0 && heads_kv > 0 && heads_q % heads_kv == 0,
                "flash_attn_fwd: heads_q must be a positive multiple of heads_kv");
   IRIS_REQUIRE(n > 0 && batch * heads_q * n < (1ll << 31), "flash_attn_fwd: sequence too long");
+  IRIS_REQUIRE(n_kv > 0 && batch * heads_kv * n_kv < (1ll << 31), "flash_attn_fwd: key sequence too long");
   IRIS_REQUIRE(split >= 0 && split <= n && (split == 0 || o_text != nullptr), "flash_attn_fwd: bad split");
   IRIS_REQUIRE(row_stride >= heads_q * D && row_stride % 8 == 0, "flash_attn_fwd: o_row_stride");
   IRIS_REQUIRE(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o_image) &&
@@ -485,13 +490,14 @@ extern "C" int iris_flash_attn_fwd_split(const void* q, const void* k, const voi
   IRIS_REQUIRE(batch <= 65535 && heads_q <= 65535, "flash_attn_fwd: grid too large");
   CUtensorMap tq, tk, tv;
   IRIS_CHECK_STATUS(make_tmap_2d_bf16(&tq, q, D, batch * heads_q * n, D, 64, BQ));
-  IRIS_CHECK_STATUS(make_tmap_2d_bf16(&tk, k, D, batch * heads_kv * n, D, 64, BKV));
-  IRIS_CHECK_STATUS(make_tmap_2d_bf16(&tv, v, D, batch * heads_kv * n, D, 64, BKV));
+  IRIS_CHECK_STATUS(make_tmap_2d_bf16(&tk, k, D, batch * heads_kv * n_kv, D, 64, BKV));
+  IRIS_CHECK_STATUS(make_tmap_2d_bf16(&tv, v, D, batch * heads_kv * n_kv, D, 64, BKV));
   Params p;
   p.batch = batch;
   p.heads_q = heads_q;
   p.heads_kv = heads_kv;
   p.n = n;
+  p.n_kv = n_kv;
   p.row_stride = row_stride;
   p.split = split;
   p.scale_log2 = scale * 1.4426950408889634f;
@@ -518,6 +524,6 @@ extern "C" int iris_flash_attn_fwd_split(const void* q, const void* k, const voi
 extern "C" int iris_flash_attn_fwd(const void* q, const void* k, const void* v, void* o, int64_t batch,
                                    int64_t heads_q, int64_t heads_kv, int64_t n, int64_t head_dim, float scale,
                                    int64_t o_row_stride, void* stream) {
-  return iris_flash_attn_fwd_split(q, k, v, batch, heads_q, heads_kv, n, head_dim, scale, 0, nullptr, o, nullptr,
+  return iris_flash_attn_fwd_split(q, k, v, batch, heads_q, heads_kv, n, n, head_dim, scale, 0, nullptr, o, nullptr,
                                    nullptr, o_row_stride, stream);
 }

@@ -118,7 +118,8 @@ __global__ void __launch_bounds__(ROWS_PER_BLOCK * 16) qkv_heads_kernel(
     const __nv_bfloat16* __restrict__ qkv, int64_t batch, int64_t tokens, int64_t row_stride, int hq, int hkv,
     const float* __restrict__ qw, const float* __restrict__ kw, const float* __restrict__ cos_t,
     const float* __restrict__ sin_t, float eps, __nv_bfloat16* __restrict__ q_out,
-    __nv_bfloat16* __restrict__ k_out, __nv_bfloat16* __restrict__ v_out, int64_t n_out, int64_t offset) {
+    __nv_bfloat16* __restrict__ k_out, __nv_bfloat16* __restrict__ v_out, int64_t n_out, int64_t n_out_kv,
+    int64_t offset, bool head_major) {
   const int sub = threadIdx.x & 15;
   const int slots = hq + 2 * hkv;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * ROWS_PER_BLOCK + (threadIdx.x >> 4);
@@ -129,16 +130,18 @@ __global__ void __launch_bounds__(ROWS_PER_BLOCK * 16) qkv_heads_kernel(
   const int64_t t = offset + n;
   float v[8];
   load8<__nv_bfloat16>(qkv + bn * row_stride + slot * 128 + sub * 8, v);
+  // [b, h, t] or, head-major, [h, b, t] (contiguous per-head slices for an all-to-all)
+  auto at = [&](int h, int heads, int64_t len) { return (head_major ? h * batch + b : b * heads + h) * len + t; };
   if (slot < hq) {
     norm_rope(v, sub, qw, cos_t + t * 64, sin_t + t * 64, eps);
-    store8<__nv_bfloat16>(q_out + ((b * hq + slot) * n_out + t) * 128 + sub * 8, v);
+    store8<__nv_bfloat16>(q_out + at(slot, hq, n_out) * 128 + sub * 8, v);
   } else if (slot < hq + hkv) {
     const int h = slot - hq;
     norm_rope(v, sub, kw, cos_t + t * 64, sin_t + t * 64, eps);
-    store8<__nv_bfloat16>(k_out + ((b * hkv + h) * n_out + t) * 128 + sub * 8, v);
+    store8<__nv_bfloat16>(k_out + at(h, hkv, n_out_kv) * 128 + sub * 8, v);
   } else {
     const int h = slot - hq - hkv;
-    store8<__nv_bfloat16>(v_out + ((b * hkv + h) * n_out + t) * 128 + sub * 8, v);
+    store8<__nv_bfloat16>(v_out + at(h, hkv, n_out_kv) * 128 + sub * 8, v);
   }
 }
 
@@ -201,13 +204,14 @@ extern "C" int iris_qk_norm_rope(const void* x, int x_dtype, int64_t batch, int6
 extern "C" int iris_qkv_heads(const void* qkv, int64_t batch, int64_t tokens, int64_t row_stride, int64_t heads_q,
                               int64_t heads_kv, const float* q_weight, const float* k_weight, const float* cos,
                               const float* sin, float eps, void* q_out, void* k_out, void* v_out, int64_t n_out,
-                              int64_t offset, void* stream) {
+                              int64_t n_out_kv, int64_t offset, int head_major, void* stream) {
   using namespace iris::heads;
   IRIS_REQUIRE(heads_q > 0 && heads_kv >= 0 && offset >= 0, "qkv_heads: bad head counts or offset");
   IRIS_REQUIRE(qkv && q_out && q_weight && cos && sin, "qkv_heads: null pointer");
   IRIS_REQUIRE(heads_kv == 0 || (k_out && v_out && k_weight), "qkv_heads: null k/v pointer");
   IRIS_REQUIRE((heads_q + 2 * heads_kv) * 128 <= row_stride && row_stride % 8 == 0, "qkv_heads: row stride");
-  IRIS_REQUIRE(offset + tokens <= n_out, "qkv_heads: output does not cover the written rows");
+  IRIS_REQUIRE(offset + tokens <= n_out && (heads_kv == 0 || offset + tokens <= n_out_kv),
+               "qkv_heads: output does not cover the written rows");
   IRIS_REQUIRE(aligned16(qkv) && aligned16(q_out) && aligned16(cos) && aligned16(sin) && aligned16(q_weight),
                "qkv_heads: pointers must be 16-byte aligned");
   IRIS_REQUIRE(heads_kv == 0 || (aligned16(k_out) && aligned16(v_out) && aligned16(k_weight)),
@@ -218,7 +222,8 @@ extern "C" int iris_qkv_heads(const void* qkv, int64_t batch, int64_t tokens, in
   qkv_heads_kernel<<<grid, ROWS_PER_BLOCK * 16, 0, static_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const __nv_bfloat16*>(qkv), batch, tokens, row_stride, static_cast<int>(heads_q),
       static_cast<int>(heads_kv), q_weight, k_weight, cos, sin, eps, reinterpret_cast<__nv_bfloat16*>(q_out),
-      reinterpret_cast<__nv_bfloat16*>(k_out), reinterpret_cast<__nv_bfloat16*>(v_out), n_out, offset);
+      reinterpret_cast<__nv_bfloat16*>(k_out), reinterpret_cast<__nv_bfloat16*>(v_out), n_out, n_out_kv, offset,
+      head_major != 0);
   IRIS_CUDA(cudaGetLastError());
   return IRIS_OK;
 }

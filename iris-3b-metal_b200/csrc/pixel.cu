@@ -171,7 +171,8 @@ __global__ void __launch_bounds__(THREADS) pixel_mlp_mma_kernel(
     const float* __restrict__ nw, const __nv_bfloat16* __restrict__ w1, const __nv_bfloat16* __restrict__ b1,
     const __nv_bfloat16* __restrict__ w2, const __nv_bfloat16* __restrict__ b2, const float* __restrict__ nnw,
     __nv_bfloat16* __restrict__ next_input, const float* __restrict__ fw, const float* __restrict__ fb,
-    float* __restrict__ v, int64_t n, int64_t height, int64_t width, int patch, float eps) {
+    float* __restrict__ v, int64_t n, int64_t height, int64_t width, int patch, int64_t token_start,
+    int64_t tokens, float eps) {
   constexpr bool ROUND = !F32;
   auto r = [](float x) { return ROUND ? round_bf16(x) : x; };
   const int lane = threadIdx.x & 31;
@@ -207,7 +208,6 @@ __global__ void __launch_bounds__(THREADS) pixel_mlp_mma_kernel(
   }
   const int pp = patch * patch;
   const int64_t gw = width / patch;
-  const int64_t L = (height / patch) * gw;
   const int64_t tiles = n / 16;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
   for (int64_t tile = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5); tile < tiles;
@@ -315,7 +315,7 @@ __global__ void __launch_bounds__(THREADS) pixel_mlp_mma_kernel(
         if (c == 0) {
           const int64_t patch_idx = px / pp;
           const int k = static_cast<int>(px % pp);
-          const int64_t bb = patch_idx / L, l = patch_idx % L;
+          const int64_t bb = patch_idx / tokens, l = token_start + patch_idx % tokens;
           const int64_t y = (l / gw) * patch + k / patch, xx = (l % gw) * patch + k % patch;
 #pragma unroll
           for (int o = 0; o < 3; ++o) v[((bb * 3 + o) * height + y) * width + xx] = part[o] + __ldg(fb + o);
@@ -370,12 +370,11 @@ __global__ void __launch_bounds__(THREADS) pixel_mlp_head_kernel(
     const void* pixels, const __nv_bfloat16* __restrict__ branch, const __nv_bfloat16* __restrict__ mods,
     const float* nw, const __nv_bfloat16* w1, const __nv_bfloat16* b1, const __nv_bfloat16* w2,
     const __nv_bfloat16* b2, const float* fnw, const float* fw, const float* fb, float* __restrict__ v, int64_t n,
-    int64_t height, int64_t width, int patch, float eps) {
+    int64_t height, int64_t width, int patch, int64_t token_start, int64_t tokens, float eps) {
   __shared__ MlpWeights s;
   load_weights(s, w1, b1, w2, b2, nw, fnw, fw, fb);
   const int pp = patch * patch;
   const int64_t gw = width / patch;
-  const int64_t L = (height / patch) * gw;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     float x[C], attn[C];
@@ -388,7 +387,7 @@ __global__ void __launch_bounds__(THREADS) pixel_mlp_head_kernel(
     for (int c = 0; c < C; ++c) h[c] = F32 ? x[c] * inv * s.nnw[c] : round_bf16(x[c] * inv * s.nnw[c]);
     const int64_t patch_idx = i / pp;
     const int k = static_cast<int>(i % pp);
-    const int64_t b = patch_idx / L, l = patch_idx % L;
+    const int64_t b = patch_idx / tokens, l = token_start + patch_idx % tokens;
     const int64_t y = (l / gw) * patch + k / patch, xx = (l % gw) * patch + k % patch;
 #pragma unroll
     for (int ch = 0; ch < 3; ++ch) {
@@ -405,7 +404,8 @@ __global__ void __launch_bounds__(THREADS) pixel_embed_kernel(const float* __res
                                                                const float* __restrict__ pos, void* pixels, bool f32,
                                                                __nv_bfloat16* __restrict__ normed,
                                                                const float* __restrict__ nw, float eps, int64_t n,
-                                                               int64_t height, int64_t width, int patch) {
+                                                               int64_t height, int64_t width, int patch,
+                                                               int64_t token_start, int64_t tokens) {
   __shared__ float sw[3 * C + C + C];
   for (int i = threadIdx.x; i < 3 * C; i += blockDim.x) sw[i] = w[i];
   for (int i = threadIdx.x; i < C; i += blockDim.x) {
@@ -415,13 +415,12 @@ __global__ void __launch_bounds__(THREADS) pixel_embed_kernel(const float* __res
   __syncthreads();
   const int pp = patch * patch;
   const int64_t gw = width / patch;
-  const int64_t L = (height / patch) * gw;
   const int64_t plane = height * width;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t patch_idx = i / pp;
     const int k = static_cast<int>(i % pp);
-    const int64_t b = patch_idx / L, l = patch_idx % L;
+    const int64_t b = patch_idx / tokens, l = token_start + patch_idx % tokens;
     const int64_t y = (l / gw) * patch + k / patch, xx = (l % gw) * patch + k % patch;
     const float* xp = x + b * 3 * plane + y * width + xx;
     const float x0 = xp[0], x1 = xp[plane], x2 = xp[2 * plane];
@@ -509,11 +508,11 @@ extern "C" int iris_pixel_mlp(void* pixels, int pixel_dtype, const void* branch,
     if (pixel_dtype == IRIS_F32)
       pixel_mlp_mma_kernel<true, false><<<grid, THREADS, 0, st>>>(
           pixels, bf(branch), bf(mods), norm_weight, bf(fc1_w), bf(fc1_b), bf(fc2_w), bf(fc2_b), next_norm_weight,
-          nxt, nullptr, nullptr, nullptr, n_pixels, 16, 16, 16, eps);
+          nxt, nullptr, nullptr, nullptr, n_pixels, 16, 16, 16, 0, 1, eps);
     else
       pixel_mlp_mma_kernel<false, false><<<grid, THREADS, 0, st>>>(
           pixels, bf(branch), bf(mods), norm_weight, bf(fc1_w), bf(fc1_b), bf(fc2_w), bf(fc2_b), next_norm_weight,
-          nxt, nullptr, nullptr, nullptr, n_pixels, 16, 16, 16, eps);
+          nxt, nullptr, nullptr, nullptr, n_pixels, 16, 16, 16, 0, 1, eps);
     IRIS_CUDA(cudaGetLastError());
     return IRIS_OK;
   }
@@ -533,14 +532,16 @@ extern "C" int iris_pixel_mlp_head(void* pixels, int pixel_dtype, const void* br
                                    const float* norm_weight, const void* fc1_w, const void* fc1_b, const void* fc2_w,
                                    const void* fc2_b, const float* final_norm_weight, const float* final_w,
                                    const float* final_b, float* v, int64_t batch, int64_t height, int64_t width,
-                                   int64_t patch, float eps, void* stream) {
+                                   int64_t patch, int64_t token_start, int64_t tokens, float eps, void* stream) {
   using namespace iris::pixel;
   IRIS_REQUIRE(pixels && branch && mods && final_norm_weight && final_w && final_b && v, "pixel_mlp_head: null pointer");
   IRIS_CHECK_STATUS(check_pixel_params(fc1_w, fc1_b, fc2_w, fc2_b, norm_weight));
   IRIS_REQUIRE(pixel_dtype == IRIS_F32 || pixel_dtype == IRIS_BF16, "pixel_mlp_head: pixels must be f32 or bf16");
   IRIS_REQUIRE(patch > 0 && height % patch == 0 && width % patch == 0 && batch >= 0, "pixel_mlp_head: bad geometry");
   IRIS_REQUIRE(aligned16(pixels) && aligned16(branch) && aligned16(mods), "pixel_mlp_head: alignment");
-  const int64_t n = batch * height * width;
+  IRIS_REQUIRE(token_start >= 0 && tokens >= 0 && token_start + tokens <= (height / patch) * (width / patch),
+               "pixel_mlp_head: token range outside the patch grid");
+  const int64_t n = batch * tokens * patch * patch;
   if (n == 0) return IRIS_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   auto bf = [](const void* p) { return reinterpret_cast<const __nv_bfloat16*>(p); };
@@ -550,39 +551,42 @@ extern "C" int iris_pixel_mlp_head(void* pixels, int pixel_dtype, const void* br
     if (pixel_dtype == IRIS_F32)
       pixel_mlp_mma_kernel<true, true><<<grid, THREADS, 0, st>>>(
           pixels, bf(branch), bf(mods), norm_weight, bf(fc1_w), bf(fc1_b), bf(fc2_w), bf(fc2_b), final_norm_weight,
-          nullptr, final_w, final_b, v, n, height, width, pt, eps);
+          nullptr, final_w, final_b, v, n, height, width, pt, token_start, tokens, eps);
     else
       pixel_mlp_mma_kernel<false, true><<<grid, THREADS, 0, st>>>(
           pixels, bf(branch), bf(mods), norm_weight, bf(fc1_w), bf(fc1_b), bf(fc2_w), bf(fc2_b), final_norm_weight,
-          nullptr, final_w, final_b, v, n, height, width, pt, eps);
+          nullptr, final_w, final_b, v, n, height, width, pt, token_start, tokens, eps);
     IRIS_CUDA(cudaGetLastError());
     return IRIS_OK;
   }
   if (pixel_dtype == IRIS_F32)
     pixel_mlp_head_kernel<true><<<grid_for(n), THREADS, 0, st>>>(
         pixels, bf(branch), bf(mods), norm_weight, bf(fc1_w), bf(fc1_b), bf(fc2_w), bf(fc2_b), final_norm_weight,
-        final_w, final_b, v, n, height, width, static_cast<int>(patch), eps);
+        final_w, final_b, v, n, height, width, static_cast<int>(patch), token_start, tokens, eps);
   else
     pixel_mlp_head_kernel<false><<<grid_for(n), THREADS, 0, st>>>(
         pixels, bf(branch), bf(mods), norm_weight, bf(fc1_w), bf(fc1_b), bf(fc2_w), bf(fc2_b), final_norm_weight,
-        final_w, final_b, v, n, height, width, static_cast<int>(patch), eps);
+        final_w, final_b, v, n, height, width, static_cast<int>(patch), token_start, tokens, eps);
   IRIS_CUDA(cudaGetLastError());
   return IRIS_OK;
 }
 
 extern "C" int iris_pixel_embed(const float* x, const float* w, const float* bias, const float* pos, void* pixels,
                                 int pixel_dtype, void* normed, const float* norm_weight, float eps, int64_t batch,
-                                int64_t height, int64_t width, int64_t patch, void* stream) {
+                                int64_t height, int64_t width, int64_t patch, int64_t token_start, int64_t tokens,
+                                void* stream) {
   using namespace iris::pixel;
   IRIS_REQUIRE(x && w && bias && pixels && normed && norm_weight, "pixel_embed: null pointer");
   IRIS_REQUIRE(pixel_dtype == IRIS_F32 || pixel_dtype == IRIS_BF16, "pixel_embed: pixels must be f32 or bf16");
   IRIS_REQUIRE(patch > 0 && height % patch == 0 && width % patch == 0 && batch >= 0, "pixel_embed: bad geometry");
   IRIS_REQUIRE(aligned16(pixels) && aligned16(normed) && (pos == nullptr || aligned16(pos)), "pixel_embed: alignment");
-  const int64_t n = batch * height * width;
+  IRIS_REQUIRE(token_start >= 0 && tokens >= 0 && token_start + tokens <= (height / patch) * (width / patch),
+               "pixel_embed: token range outside the patch grid");
+  const int64_t n = batch * tokens * patch * patch;
   if (n == 0) return IRIS_OK;
   pixel_embed_kernel<<<grid_for(n), THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
       x, w, bias, pos, pixels, pixel_dtype == IRIS_F32, reinterpret_cast<__nv_bfloat16*>(normed), norm_weight, eps, n,
-      height, width, static_cast<int>(patch));
+      height, width, static_cast<int>(patch), token_start, tokens);
   IRIS_CUDA(cudaGetLastError());
   return IRIS_OK;
 }

@@ -1,5 +1,7 @@
 // Layout, conditioning and sampler kernels around the trunk:
 //   patchify / unpatchify    integer index maps (bit-exact), dit.py:326, 367-374
+//   block_copy               strided block gather/scatter: the sequence-parallel
+//                            (Ulysses) packing around the all-to-all exchanges
 //   timestep_embedding       src/iris3b/nn/embeddings.py:41-45
 //   gemv                     small-M linear (conditioning MLP, shared adaLN cores)
 //   add_bias_rows            SharedCoreBias, src/iris3b/nn/modulation.py:284-285
@@ -20,15 +22,17 @@ inline unsigned grid_for(int64_t n, int per_thread = 1) {
   return static_cast<unsigned>(blocks < cap ? blocks : cap);
 }
 
-// out[(b, gy, gx), (c, ky, kx)] = x[b, c, gy p + ky, gx p + kx]
+// out[(b, l - token_start), (c, ky, kx)] = x[b, c, gy p + ky, gx p + kx] for the
+// patch tokens l = gy * gw + gx in [token_start, token_start + tokens)
 __global__ void patchify_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ out, int64_t total,
-                                int channels, int64_t height, int64_t width, int patch) {
-  const int64_t gw = width / patch, L = (height / patch) * gw;
+                                int channels, int64_t height, int64_t width, int patch, int64_t token_start,
+                                int64_t tokens) {
+  const int64_t gw = width / patch;
   const int64_t feat = static_cast<int64_t>(channels) * patch * patch;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t row = i / feat, f = i % feat;
-    const int64_t b = row / L, l = row % L;
+    const int64_t b = row / tokens, l = token_start + row % tokens;
     const int c = static_cast<int>(f / (patch * patch));
     const int k = static_cast<int>(f % (patch * patch));
     const int64_t y = (l / gw) * patch + k / patch, xx = (l % gw) * patch + k % patch;
@@ -171,22 +175,55 @@ __global__ void all_finite_kernel(const float* __restrict__ x, int64_t n, int* f
 
 __global__ void set_int_kernel(int* p, int v) { *p = v; }
 
+// Block (i0, i1, i2) of `vecs` 16-byte vectors: src + i0 s0 + i1 s1 + i2 s2 ->
+// dst + i0 d0 + i1 d1 + i2 d2 (byte strides). One CTA item = 1024 vectors of a
+// block, 4 per thread with all loads issued before the stores.
+constexpr int COPY_VECS_PER_THREAD = 4;
+constexpr int COPY_CHUNK = THREADS * COPY_VECS_PER_THREAD;
+
+__global__ void __launch_bounds__(THREADS) block_copy_kernel(uint8_t* __restrict__ dst,
+                                                              const uint8_t* __restrict__ src, int64_t d0,
+                                                              int64_t d1, int64_t d2, int64_t s0, int64_t s1,
+                                                              int64_t s2, int64_t n1, int64_t n2, int64_t items,
+                                                              int64_t chunks, int64_t vecs) {
+  for (int64_t item = blockIdx.x; item < items; item += gridDim.x) {
+    const int64_t blk = item / chunks, chunk = item % chunks;
+    const int64_t i2 = blk % n2, i1 = (blk / n2) % n1, i0 = blk / (n2 * n1);
+    const uint4* from = reinterpret_cast<const uint4*>(src + i0 * s0 + i1 * s1 + i2 * s2);
+    uint4* to = reinterpret_cast<uint4*>(dst + i0 * d0 + i1 * d1 + i2 * d2);
+    const int64_t first = chunk * COPY_CHUNK + threadIdx.x;
+    uint4 v[COPY_VECS_PER_THREAD];
+#pragma unroll
+    for (int j = 0; j < COPY_VECS_PER_THREAD; ++j) {
+      const int64_t e = first + j * THREADS;
+      if (e < vecs) v[j] = from[e];
+    }
+#pragma unroll
+    for (int j = 0; j < COPY_VECS_PER_THREAD; ++j) {
+      const int64_t e = first + j * THREADS;
+      if (e < vecs) to[e] = v[j];
+    }
+  }
+}
+
 }  // namespace small
 }  // namespace iris
 
 using namespace iris;
 
 extern "C" int iris_patchify(const float* x, void* out, int64_t batch, int64_t channels, int64_t height,
-                             int64_t width, int64_t patch, void* stream) {
+                             int64_t width, int64_t patch, int64_t token_start, int64_t tokens, void* stream) {
   using namespace iris::small;
   IRIS_REQUIRE(x && out, "patchify: null pointer");
   IRIS_REQUIRE(patch > 0 && height % patch == 0 && width % patch == 0 && batch >= 0 && channels > 0,
                "input is not divisible by patch_size");
-  const int64_t total = batch * channels * height * width;
+  IRIS_REQUIRE(token_start >= 0 && tokens >= 0 && token_start + tokens <= (height / patch) * (width / patch),
+               "patchify: token range outside the patch grid");
+  const int64_t total = batch * tokens * channels * patch * patch;
   if (total == 0) return IRIS_OK;
   patchify_kernel<<<grid_for(total), THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
       x, reinterpret_cast<__nv_bfloat16*>(out), total, static_cast<int>(channels), height, width,
-      static_cast<int>(patch));
+      static_cast<int>(patch), token_start, tokens);
   IRIS_CUDA(cudaGetLastError());
   return IRIS_OK;
 }
@@ -272,6 +309,30 @@ extern "C" int iris_all_finite(const float* x, int64_t n, int* flag, void* strea
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   set_int_kernel<<<1, 1, 0, st>>>(flag, 1);
   if (n > 0) all_finite_kernel<<<grid_for(n, 8), THREADS, 0, st>>>(x, n, flag);
+  IRIS_CUDA(cudaGetLastError());
+  return IRIS_OK;
+}
+
+extern "C" int iris_block_copy(void* dst, int64_t dst_stride0, int64_t dst_stride1, int64_t dst_stride2,
+                               const void* src, int64_t src_stride0, int64_t src_stride1, int64_t src_stride2,
+                               int64_t count0, int64_t count1, int64_t count2, int64_t block_bytes, void* stream) {
+  using namespace iris::small;
+  IRIS_REQUIRE(dst && src, "block_copy: null pointer");
+  IRIS_REQUIRE(count0 >= 0 && count1 >= 0 && count2 >= 0 && block_bytes >= 0, "block_copy: negative size");
+  IRIS_REQUIRE(aligned16(dst) && aligned16(src) && block_bytes % 16 == 0 && dst_stride0 % 16 == 0 &&
+                   dst_stride1 % 16 == 0 && dst_stride2 % 16 == 0 && src_stride0 % 16 == 0 &&
+                   src_stride1 % 16 == 0 && src_stride2 % 16 == 0,
+               "block_copy: pointers, strides and block size must be multiples of 16 bytes");
+  const int64_t blocks = count0 * count1 * count2;
+  if (blocks == 0 || block_bytes == 0) return IRIS_OK;
+  const int64_t vecs = block_bytes / 16;
+  const int64_t chunks = (vecs + COPY_CHUNK - 1) / COPY_CHUNK;
+  const int64_t items = blocks * chunks;
+  const int64_t cap = static_cast<int64_t>(num_sms()) * 16;
+  const unsigned grid = static_cast<unsigned>(items < cap ? items : cap);
+  block_copy_kernel<<<grid, THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<uint8_t*>(dst), reinterpret_cast<const uint8_t*>(src), dst_stride0, dst_stride1, dst_stride2,
+      src_stride0, src_stride1, src_stride2, count1, count2, items, chunks, vecs);
   IRIS_CUDA(cudaGetLastError());
   return IRIS_OK;
 }

@@ -28,14 +28,15 @@ SIGNATURES: dict[str, list] = {
     ],
     "iris_rms_norm_add_rows": [P, P, P, I64, I64, I64, F, P],
     "iris_qk_norm_rope": [P, I32, I64, I64, I64, I64, I64, P, P, P, F, P, I32, I64, I64, P],
-    "iris_qkv_heads": [P, I64, I64, I64, I64, I64, P, P, P, P, F, P, P, P, I64, I64, P],
+    "iris_qkv_heads": [P, I64, I64, I64, I64, I64, P, P, P, P, F, P, P, P, I64, I64, I64, I32, P],
     "iris_gemm_bf16": [P, I64, P, I64, P, I32, I64, I64, I64, I64, I32, P, P, I64, I64, I64, I64, I64, I64, I64, P],
     "iris_flash_attn_fwd": [P, P, P, P, I64, I64, I64, I64, I64, F, I64, P],
     "iris_pixel_rms_norm": [P, I32, P, P, I64, F, P],
     "iris_pixel_mlp": [P, I32, P, P, P, P, P, P, P, P, P, I64, F, P],
-    "iris_pixel_mlp_head": [P, I32, P, P, P, P, P, P, P, P, P, P, P, I64, I64, I64, I64, F, P],
-    "iris_pixel_embed": [P, P, P, P, P, I32, P, P, F, I64, I64, I64, I64, P],
-    "iris_patchify": [P, P, I64, I64, I64, I64, I64, P],
+    "iris_pixel_mlp_head": [P, I32, P, P, P, P, P, P, P, P, P, P, P, I64, I64, I64, I64, I64, I64, F, P],
+    "iris_pixel_embed": [P, P, P, P, P, I32, P, P, F, I64, I64, I64, I64, I64, I64, P],
+    "iris_patchify": [P, P, I64, I64, I64, I64, I64, I64, I64, P],
+    "iris_block_copy": [P, I64, I64, I64, P, I64, I64, I64, I64, I64, I64, I64, P],
     "iris_unpatchify": [P, P, I64, I64, I64, I64, I64, P],
     "iris_timestep_embedding": [P, P, I64, I64, F, P],
     "iris_gemv": [P, I64, I64, P, I32, P, P, I64, I32, I32, P],
@@ -56,7 +57,7 @@ class GemmProblem(ctypes.Structure):
 
 
 SIGNATURES["iris_gemm_bf16_grouped"] = [ctypes.POINTER(GemmProblem), I32, P]
-SIGNATURES["iris_flash_attn_fwd_split"] = [P, P, P, I64, I64, I64, I64, I64, F, I64, P, P, P, P, I64, P]
+SIGNATURES["iris_flash_attn_fwd_split"] = [P, P, P, I64, I64, I64, I64, I64, I64, F, I64, P, P, P, P, I64, P]
 
 _lib: ctypes.CDLL | None = None
 

@@ -314,19 +314,25 @@ def profile_gemms(enable: bool):
 
 def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor, scale: float | None = None):
     """``softmax(q k^T * scale) v`` for ``q``: ``[B, H, N, 128]``, ``k``/``v``:
-    ``[B, H_kv, N, 128]`` (bf16, contiguous); ``out``: ``[B, N, >= H*128]`` bf16."""
-    _require(q.dim() == 4 and k.shape == v.shape and q.shape[0] == k.shape[0] and q.shape[2:] == k.shape[2:],
-             "flash_attention: q [B, H, N, D], k/v [B, H_kv, N, D]")  # fmt: skip
-    _require(all(t.dtype == torch.bfloat16 and t.is_contiguous() for t in (q, k, v)), "flash_attention: contiguous bf16")
+    ``[B, H_kv, N_kv, 128]`` (bf16, contiguous; ``N_kv`` may differ from ``N``);
+    ``out``: ``[B, N, >= H*128]`` bf16."""
+    _check_qkv(q, k, v)
     batch, heads, n, d = q.shape
     _require(out.dtype == torch.bfloat16 and out.stride(-1) == 1 and out.shape[-2] == n, "flash_attention: out layout")
     _require(out.dim() == 3 and out.stride(0) == n * out.stride(1), "flash_attention: out rows must be [B*N, stride]")
     _require_cuda(q, k, v, out)
     _lib.call(
-        "iris_flash_attn_fwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), batch, heads, k.shape[1], n, d,
-        float(scale if scale is not None else d**-0.5), out.stride(1), stream_of(q),
+        "iris_flash_attn_fwd_split", q.data_ptr(), k.data_ptr(), v.data_ptr(), batch, heads, k.shape[1], n,
+        k.shape[2], d, float(scale if scale is not None else d**-0.5), 0, None, out.data_ptr(), None, None,
+        out.stride(1), stream_of(q),
     )  # fmt: skip
     return out
+
+
+def _check_qkv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
+    _require(q.dim() == 4 and k.shape == v.shape and q.shape[0] == k.shape[0] and q.shape[3] == k.shape[3],
+             "flash_attention: q [B, H, N, D], k/v [B, H_kv, N_kv, D]")  # fmt: skip
+    _require(all(t.dtype == torch.bfloat16 and t.is_contiguous() for t in (q, k, v)), "flash_attention: contiguous bf16")
 
 
 def flash_attention_split(
@@ -343,9 +349,7 @@ def flash_attention_split(
     """Attention whose token ``i < split`` rows land densely in ``o_text`` (row
     ``b * split + i``) and the rest in ``o_image`` (row ``b * (N - split) + i - split``),
     each multiplied by ``sigmoid`` of the bf16 gate logits in the same rows."""
-    _require(q.dim() == 4 and k.shape == v.shape and q.shape[0] == k.shape[0] and q.shape[2:] == k.shape[2:],
-             "flash_attention: q [B, H, N, D], k/v [B, H_kv, N, D]")  # fmt: skip
-    _require(all(t.dtype == torch.bfloat16 and t.is_contiguous() for t in (q, k, v)), "flash_attention: contiguous bf16")
+    _check_qkv(q, k, v)
     batch, heads, n, d = q.shape
     outs = [t for t in (o_text, o_image, gate_text, gate_image) if t is not None]
     _require(all(t.dtype == torch.bfloat16 and t.stride(-1) == 1 for t in outs), "flash_attention: bf16 row-major outputs")
@@ -353,9 +357,32 @@ def flash_attention_split(
     _require(all(t.stride(-2) == stride for t in outs), "flash_attention: outputs and gates share one row stride")
     _require_cuda(q, k, v, *outs)
     _lib.call(
-        "iris_flash_attn_fwd_split", q.data_ptr(), k.data_ptr(), v.data_ptr(), batch, heads, k.shape[1], n, d,
-        float(scale if scale is not None else d**-0.5), split, _ptr(o_text), o_image.data_ptr(), _ptr(gate_text),
+        "iris_flash_attn_fwd_split", q.data_ptr(), k.data_ptr(), v.data_ptr(), batch, heads, k.shape[1], n,
+        k.shape[2], d, float(scale if scale is not None else d**-0.5), split, _ptr(o_text), o_image.data_ptr(), _ptr(gate_text),
         _ptr(gate_image), stride, stream_of(q),
+    )  # fmt: skip
+
+
+def block_copy(
+    dst: torch.Tensor,
+    dst_strides: tuple[int, int, int],
+    src: torch.Tensor,
+    src_strides: tuple[int, int, int],
+    counts: tuple[int, int, int],
+    block_bytes: int,
+    dst_offset: int = 0,
+    src_offset: int = 0,
+) -> None:
+    """``counts[0] x counts[1] x counts[2]`` blocks of ``block_bytes`` from
+    ``src`` to ``dst``; strides and offsets in bytes (multiples of 16)."""
+    _require_cuda(dst, src)
+    _require(dst.device == src.device, "block_copy: one device")
+    for name, t, off, strides in (("dst", dst, dst_offset, dst_strides), ("src", src, src_offset, src_strides)):
+        span = off + sum((c - 1) * st for c, st in zip(counts, strides) if c > 0) + block_bytes
+        _require(min(counts) == 0 or span <= t.numel() * t.element_size(), f"block_copy: {name} range out of bounds")
+    _lib.call(
+        "iris_block_copy", dst.data_ptr() + dst_offset, *dst_strides, src.data_ptr() + src_offset, *src_strides,
+        *counts, block_bytes, stream_of(dst),
     )  # fmt: skip
 
 

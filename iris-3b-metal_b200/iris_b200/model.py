@@ -27,6 +27,10 @@ Per step (``dit.py:283-375`` restructured):
 Precision plan: BF16 GEMM operands and attention, FP32 accumulation, FP32
 residual streams, norms, modulation and conditioning, FP32 pixel stream
 (the reference keeps BF16 there; FP32 is closer to the fp32 model).
+
+With a communicator (``comm``, see :mod:`iris_b200.ulysses`) one call is
+spread over its ranks by sequence parallelism: each rank runs the step on its
+slice of the joint sequence and every rank returns the whole velocity.
 """
 
 from __future__ import annotations
@@ -39,6 +43,7 @@ from iris_b200 import _lib
 from iris_b200 import kernels as K
 from iris_b200.config import ModelConfig, from_any
 from iris_b200.tables import cos_sin, rope_1d, rope_2d, sincos_pos_embed_2d
+from iris_b200.ulysses import SequenceShard, gather_image_tokens, gather_tokens, scatter_heads
 
 HEAD_DIM = 128
 SWIGLU_TILE = 128  # w1/w3 rows per SwiGLU GEMM tile half
@@ -116,7 +121,13 @@ class _Block:
 class CudaIris:
     """Velocity predictor ``(x, t, text) -> v`` for a loaded Iris model."""
 
-    def __init__(self, dit, attention_dtype: torch.dtype | None = None, pixel_dtype: torch.dtype = torch.float32):
+    def __init__(
+        self,
+        dit,
+        attention_dtype: torch.dtype | None = None,
+        pixel_dtype: torch.dtype = torch.float32,
+        comm=None,
+    ):
         cfg = from_any(dit.cfg)
         state = dit.state_dict()
         check_supported(cfg, state)
@@ -133,6 +144,12 @@ class CudaIris:
         self.attention_dtype = torch.bfloat16
         self.pixel_dtype = pixel_dtype
         self.text_dtype = torch.bfloat16
+        self.comm = comm if comm is not None and comm.world > 1 else None
+        if self.comm is not None:
+            world = self.comm.world
+            if cfg.num_heads % world or cfg.kv_heads % world:
+                raise ValueError(f"sequence parallelism over {world} ranks needs the trunk's query and key/value "
+                                 f"head counts ({cfg.num_heads}, {cfg.kv_heads}) divisible by {world}")  # fmt: skip
         self._pack(state)
         self._tables: dict = {}
         self._work: dict = {}
@@ -301,47 +318,49 @@ class CudaIris:
             self._tables[key] = (trunk, pixel, pos)
         return self._tables[key]
 
-    def _workspace(self, batch: int, grid: tuple[int, int], n_text: int) -> dict:
-        key = (batch, grid, n_text)
+    def _workspace(self, batch: int, grid: tuple[int, int], shard: SequenceShard) -> dict:
+        """Buffers of one geometry; token-row buffers hold this rank's rows only
+        (all of them without sequence parallelism)."""
+        key = (batch, grid, shard)
         if key in self._work:
             return self._work[key]
         self._work.clear()
         cfg, dev = self.cfg, self.device
-        d, p = cfg.hidden_size, cfg.patch_size
-        L = grid[0] * grid[1]
-        N = n_text + L
+        d = cfg.hidden_size
+        pp = cfg.patch_size**2
+        n, L_loc = shard.n, shard.image
         hq, hkv = cfg.num_heads, cfg.kv_heads
         pix = cfg.pixel
-        pp = p * p
         bf16 = torch.bfloat16
         wq = (hq + 2 * hkv) * HEAD_DIM
         e = lambda *shape, dtype=bf16: torch.empty(*shape, device=dev, dtype=dtype)  # noqa: E731
         ws = {
-            "tokens": e(batch * N, d, dtype=torch.float32),
-            "patches": e(batch * L, self.s_embed[0].shape[1]),
-            "h": e(batch * N, d),  # dual-stream branch inputs (text rows, then image rows)
-            "hj": e(batch * N, d),  # single-stream branch inputs ([text | image] per sample)
-            "h2": e(batch * N, d),
-            "qkv": e(batch * N, wq),
-            "q": e(batch, hq, N, HEAD_DIM),
-            "k": e(batch, hkv, N, HEAD_DIM),
-            "v": e(batch, hkv, N, HEAD_DIM),
-            "glog": e(batch * N, d),  # gate logits, dense per stream (text rows, then image rows)
-            "og": e(batch * N, d),  # gated attention output, same rows
-            "branch": e(batch * N, d),
-            "act": e(batch * N, self.ffn_pad),
-            "s_cond": e(batch * L, d),
-            "pixels": e(batch * L * pp, pix.hidden_size, dtype=self.pixel_dtype),
-            "ph": e(batch * L, pp * pix.hidden_size),
-            "pmods": e(batch * L, pp * 4 * pix.hidden_size),
-            "comp": e(batch * L, pix.attn_hidden_size),
-            "pqkv": e(batch * L, 3 * pix.attn_hidden_size),
-            "pq": e(batch, pix.num_heads, L, HEAD_DIM),
-            "pk": e(batch, pix.num_heads, L, HEAD_DIM),
-            "pv": e(batch, pix.num_heads, L, HEAD_DIM),
-            "po": e(batch * L, pix.attn_hidden_size),
-            "pproj": e(batch * L, pix.attn_hidden_size),
-            "pbranch": e(batch * L, pp * pix.hidden_size),
+            "tokens": e(batch * n, d, dtype=torch.float32),
+            "patches": e(batch * L_loc, self.s_embed[0].shape[1]),
+            "h": e(batch * n, d),  # dual-stream branch inputs (text rows, then image rows)
+            "hj": e(batch * n, d),  # single-stream branch inputs ([text | image] per sample)
+            "h2": e(batch * n, d),
+            "qkv": e(batch * n, wq),
+            # [B, H, n, 128]; head-major [H, B, n, 128] under sequence parallelism
+            "q": e(batch, hq, n, HEAD_DIM),
+            "k": e(batch, hkv, n, HEAD_DIM),
+            "v": e(batch, hkv, n, HEAD_DIM),
+            "glog": e(batch * n, d),  # gate logits, dense per stream (text rows, then image rows)
+            "og": e(batch * n, d),  # gated attention output, same rows
+            "branch": e(batch * n, d),
+            "act": e(batch * n, self.ffn_pad),
+            "s_cond": e(batch * L_loc, d),
+            "pixels": e(batch * L_loc * pp, pix.hidden_size, dtype=self.pixel_dtype),
+            "ph": e(batch * L_loc, pp * pix.hidden_size),
+            "pmods": e(batch * L_loc, pp * 4 * pix.hidden_size),
+            "comp": e(batch * L_loc, pix.attn_hidden_size),
+            "pqkv": e(batch * L_loc, 3 * pix.attn_hidden_size),
+            "pq": e(batch, pix.num_heads, L_loc, HEAD_DIM),
+            "pk": e(batch, pix.num_heads, shard.L, HEAD_DIM),
+            "pv": e(batch, pix.num_heads, shard.L, HEAD_DIM),
+            "po": e(batch * L_loc, pix.attn_hidden_size),
+            "pproj": e(batch * L_loc, pix.attn_hidden_size),
+            "pbranch": e(batch * L_loc, pp * pix.hidden_size),
             "t_freq": e(batch, 256, dtype=torch.float32),
             "t_h": e(batch, d, dtype=torch.float32),
             "t_emb": e(batch, d, dtype=torch.float32),
@@ -351,6 +370,27 @@ class CudaIris:
             "mods_txt": e(max(1, 0 if self.txt_bias is None else self.txt_bias.shape[0]), batch, 6 * d,
                           dtype=torch.float32),  # fmt: skip
         }
+        if shard.world > 1:
+            P, N = shard.world, shard.N
+            hql, hkvl = hq // P, hkv // P
+            ws.update({
+                # all-to-all receive buffers [P, H/P, B, n, 128] and the full-sequence heads
+                "q_r": e(P * hql * batch * n * HEAD_DIM),
+                "k_r": e(P * hkvl * batch * n * HEAD_DIM),
+                "v_r": e(P * hkvl * batch * n * HEAD_DIM),
+                "qf": e(batch, hql, N, HEAD_DIM),
+                "kf": e(batch, hkvl, N, HEAD_DIM),
+                "vf": e(batch, hkvl, N, HEAD_DIM),
+                "of": e(batch, N, hql * HEAD_DIM),  # attention output of this rank's heads
+                "o_s": e(batch * n * hq * HEAD_DIM),  # [P(dst), B, n, H/P 128]
+                "o_r": e(batch * n * hq * HEAD_DIM),  # [P(src), B, n, H/P 128]
+                "o_loc": e(batch * n, hq * HEAD_DIM),  # ungated attention output of the local rows
+                # pixel keys / values: local (padded), gathered
+                "pk_s": e(batch, pix.num_heads, shard.image_max, HEAD_DIM),
+                "pv_s": e(batch, pix.num_heads, shard.image_max, HEAD_DIM),
+                "pk_g": e(P * batch * pix.num_heads * shard.image_max * HEAD_DIM),
+                "pv_g": e(P * batch * pix.num_heads * shard.image_max * HEAD_DIM),
+            })  # fmt: skip
         self._work[key] = ws
         return ws
 
@@ -377,13 +417,18 @@ class CudaIris:
             raise ValueError("text must be [B, T, hidden_size] for the same batch as x")
         grid = (height // p, width // p)
         L, T = grid[0] * grid[1], text.shape[1]
-        N = T + L
+        comm = self.comm
+        shard = SequenceShard(comm.rank, comm.world, T, L) if comm is not None else SequenceShard(0, 1, T, L)
+        n, T_loc, L_loc = shard.n, shard.text, shard.image  # this rank's joint / text / image tokens
         d = cfg.hidden_size
         dev = self.device
         x = x.to(dev, torch.float32).contiguous()
         t = t.to(dev, torch.float32).reshape(batch).contiguous()
-        ws = self._workspace(batch, grid, T)
+        ws = self._workspace(batch, grid, shard)
         (cos, sin), (pcos, psin), pos = self._rope(grid, T)
+        # rotary tables are indexed by global position: start at this rank's first token
+        cos, sin = cos[shard.start :], sin[shard.start :]
+        pcos, psin = pcos[shard.image_start :], psin[shard.image_start :]
         st = torch.cuda.current_stream(dev).cuda_stream
         eps = float(cfg.norm_eps)
         tokens = ws["tokens"]
@@ -406,24 +451,32 @@ class CudaIris:
             _lib.call("iris_add_bias_rows", core.data_ptr(), bias_table.data_ptr(), ws[f"mods_{name}"].data_ptr(),
                       batch, bias_table.shape[0], 6 * d, st)  # fmt: skip
 
-        # residual stream: [text | image] rows per sample
-        tokens.view(batch, N, d)[:, :T].copy_(text.to(dev, torch.float32))
-        _lib.call("iris_patchify", x.data_ptr(), ws["patches"].data_ptr(), batch, channels, height, width, p, st)
-        K.gemm(ws["patches"], self.s_embed[0], tokens, bias=self.s_embed[1], out_rows=(L, N, T))
+        # residual stream: [text | image] rows per sample (this rank's slice)
+        if T_loc:
+            text_rows = text[:, shard.text_start : shard.text_start + T_loc]
+            tokens.view(batch, n, d)[:, :T_loc].copy_(text_rows.to(dev, torch.float32))
+        _lib.call("iris_patchify", x.data_ptr(), ws["patches"].data_ptr(), batch, channels, height, width, p,
+                  shard.image_start, L_loc, st)  # fmt: skip
+        K.gemm(ws["patches"], self.s_embed[0], tokens, bias=self.s_embed[1], out_rows=(L_loc, n, T_loc))
 
-        geom = _Geometry(batch=batch, T=T, L=L, N=N, d=d)
+        geom = _Geometry(batch=batch, T=T_loc, L=L_loc, N=n, d=d, shard=shard)
         self._first_norm(self.blocks[0], ws, geom, eps, st)
         for i, block in enumerate(self.blocks):
             nxt = self.blocks[i + 1] if i + 1 < len(self.blocks) else None
             self._block(block, nxt, ws, geom, cos, sin, eps, st)
             if capture is not None:
-                capture[f"block{i}"] = tokens.view(batch, N, d)[:, T:].clone()
+                capture[f"block{i}"] = tokens.view(batch, n, d)[:, T_loc:].clone()
         if capture is not None:
             capture["s_cond"] = ws["s_cond"].float().clone()
 
         # pixel stage
-        v = torch.empty(batch, channels, height, width, device=dev, dtype=torch.float32)
+        if comm is None:
+            v = torch.empty(batch, channels, height, width, device=dev, dtype=torch.float32)
+        else:  # every rank writes its own patches; the sum assembles the image
+            v = torch.zeros(batch, channels, height, width, device=dev, dtype=torch.float32)
         self._pixel_stage(x, ws, geom, grid, pcos, psin, pos, v, eps, st, capture)
+        if comm is not None:
+            comm.all_reduce_sum(v)
         return v
 
     # -- trunk --------------------------------------------------------------------------
@@ -440,7 +493,8 @@ class CudaIris:
     def _segments(self, block: _Block, g: "_Geometry"):
         """(stream, rows, rows per batch, token map, dense offset) for a block."""
         if block.dual:
-            return [("y", g.batch * g.T, g.T, (g.T, g.N, 0), 0), ("x", g.batch * g.L, g.L, (g.L, g.N, g.T), g.batch * g.T)]
+            segs = [("y", g.batch * g.T, g.T, (g.T, g.N, 0), 0), ("x", g.batch * g.L, g.L, (g.L, g.N, g.T), g.batch * g.T)]
+            return [seg for seg in segs if seg[1] > 0]  # a sequence-parallel rank may hold no text
         rows = g.batch * g.N
         return [("j", rows, g.N, (rows, 0, 0), 0)]
 
@@ -480,15 +534,18 @@ class CudaIris:
             _lib.call(
                 "iris_qkv_heads", ws["qkv"][off:].data_ptr(), g.batch, rpb, block.qkv[s].shape[0], cfg.num_heads,
                 cfg.kv_heads, qn.data_ptr(), kn.data_ptr(), cos.data_ptr(), sin.data_ptr(), eps, ws["q"].data_ptr(),
-                ws["k"].data_ptr(), ws["v"].data_ptr(), g.N, tmap[2], st,
+                ws["k"].data_ptr(), ws["v"].data_ptr(), g.N, g.N, tmap[2], int(self.comm is not None), st,
             )  # fmt: skip
-        grouped(None, block.gate, "glog")  # gate logits; sigmoid in the attention epilogue
-        split = g.T if block.dual else 0
-        bt = g.batch * split
-        K.flash_attention_split(
-            ws["q"], ws["k"], ws["v"], split, ws["og"][:bt] if bt else None, ws["og"][bt:],
-            ws["glog"][:bt] if bt else None, ws["glog"][bt:],
-        )  # fmt: skip
+        if self.comm is None:
+            grouped(None, block.gate, "glog")  # gate logits; sigmoid in the attention epilogue
+            split = g.T if block.dual else 0
+            bt = g.batch * split
+            K.flash_attention_split(
+                ws["q"], ws["k"], ws["v"], split, ws["og"][:bt] if bt else None, ws["og"][bt:],
+                ws["glog"][:bt] if bt else None, ws["glog"][bt:],
+            )  # fmt: skip
+        else:
+            self._attention_sequence_parallel(block, segs, ws, g, st)
         grouped("og", block.proj, "branch")
         for s, rows, rpb, tmap, off in segs:
             self._attn_residual(block, s, rows, rpb, tmap, off, ws, g, eps, st)
@@ -496,6 +553,25 @@ class CudaIris:
         grouped("act", block.w2, "branch")
         for s, rows, rpb, tmap, off in segs:
             self._mlp_residual(block, nxt, s, rows, rpb, tmap, off, ws, g, eps, st)
+
+    def _attention_sequence_parallel(self, block, segs, ws, g, st) -> None:
+        """Ulysses attention: Q/K/V (head-major, this rank's tokens) -> all-to-all
+        -> this rank's heads over the whole sequence -> attention -> all-to-all
+        back -> the gate GEMM applies sigmoid(h W_g^T) to the local token rows."""
+        comm, P = self.comm, self.comm.world
+        B, n = g.batch, g.N
+        hql, hkvl = self.cfg.num_heads // P, self.cfg.kv_heads // P
+        for name, heads in (("q", hql), ("k", hkvl), ("v", hkvl)):
+            scatter_heads(comm, K.block_copy, ws[name], ws[name + "_r"], ws[name + "f"], heads, B, n, HEAD_DIM)
+        K.flash_attention(ws["qf"], ws["kf"], ws["vf"], ws["of"])
+        gather_tokens(comm, K.block_copy, ws["of"], ws["o_s"], ws["o_r"], ws["o_loc"], B, n, hql * HEAD_DIM)
+        h = ws[_hkey(block)]
+        problems = [
+            K.gemm_problem(h[off : off + rows], block.gate[s], ws["og"][off : off + rows], epilogue=_lib.EPI_GATE,
+                           aux=ws["o_loc"], aux_rows=tmap)  # fmt: skip
+            for s, rows, _, tmap, off in segs[::-1]
+        ]
+        K.gemm_grouped(problems, st)
 
     def _attn_residual(self, block, stream, rows, rpb, tmap, off, ws, g, eps, st) -> None:
         """Post-norm + gate + residual of the attention branch, fused with the
@@ -552,12 +628,13 @@ class CudaIris:
         p = cfg.patch_size
         height, width = grid[0] * p, grid[1] * p
         pdt = _lib.F32 if self.pixel_dtype == torch.float32 else _lib.BF16
+        sp = self.comm is not None
         pw, pb = self.pixel_embed_w
         blocks = self.pixel_blocks
         _lib.call(
             "iris_pixel_embed", x.data_ptr(), pw.data_ptr(), pb.data_ptr(), None if pos is None else pos.data_ptr(),
             ws["pixels"].data_ptr(), pdt, ws["ph"].data_ptr(), blocks[0]["norm1"].data_ptr(), eps, g.batch, height,
-            width, p, st,
+            width, p, g.shard.image_start, g.L, st,
         )  # fmt: skip
         heads = pix.num_heads
         if capture is not None:
@@ -569,11 +646,16 @@ class CudaIris:
             K.gemm(ws["ph"], blk["compress"][0], ws["comp"], bias=blk["compress"][1])
             K.gemm(ws["comp"], blk["qkv"], ws["pqkv"])
             qn, kn = blk["qk_norm"]
+            kv = ("pk_s", "pv_s") if sp else ("pk", "pv")
             _lib.call(
                 "iris_qkv_heads", ws["pqkv"].data_ptr(), g.batch, g.L, 3 * pix.attn_hidden_size, heads, heads,
                 qn.data_ptr(), kn.data_ptr(), pcos.data_ptr(), psin.data_ptr(), eps, ws["pq"].data_ptr(),
-                ws["pk"].data_ptr(), ws["pv"].data_ptr(), g.L, 0, st,
+                ws[kv[0]].data_ptr(), ws[kv[1]].data_ptr(), g.L, ws[kv[0]].shape[2], 0, 0, st,
             )  # fmt: skip
+            if sp:  # local queries over the keys / values of every patch token
+                for name in ("pk", "pv"):
+                    gather_image_tokens(self.comm, K.block_copy, g.shard, ws[name + "_s"], ws[name + "_g"], ws[name],
+                                        g.batch, heads, HEAD_DIM)  # fmt: skip
             K.flash_attention(ws["pq"], ws["pk"], ws["pv"], ws["po"].view(g.batch, g.L, -1))
             K.gemm(ws["po"], blk["proj"][0], ws["pproj"], bias=blk["proj"][1])
             K.gemm(ws["pproj"], blk["expand"][0], ws["pbranch"], bias=blk["expand"][1])
@@ -590,7 +672,7 @@ class CudaIris:
                     "iris_pixel_mlp_head", ws["pixels"].data_ptr(), pdt, ws["pbranch"].data_ptr(),
                     ws["pmods"].data_ptr(), blk["norm2"].data_ptr(), w1.data_ptr(), b1.data_ptr(), w2.data_ptr(),
                     b2.data_ptr(), fn.data_ptr(), fw.data_ptr(), fb.data_ptr(), v.data_ptr(), g.batch, height, width,
-                    p, eps, st,
+                    p, g.shard.image_start, g.L, eps, st,
                 )  # fmt: skip
 
 
@@ -601,8 +683,11 @@ def _hkey(block: _Block) -> str:
 
 @dataclass
 class _Geometry:
+    """This rank's token counts per sample (all tokens without sequence parallelism)."""
+
     batch: int
     T: int
     L: int
     N: int
     d: int
+    shard: SequenceShard

@@ -338,7 +338,7 @@ def test_qkv_heads_matches_oracle(K):
     # device copies held in variables: the launch is asynchronous
     g, qw_d, kw_d, cos_d, sin_d = (t.cuda() for t in (qkv, qw, kw, cos, sin))
     _lib.call("iris_qkv_heads", g.data_ptr(), B, N, g.shape[-1], hq, hkv, qw_d.data_ptr(), kw_d.data_ptr(),
-              cos_d.data_ptr(), sin_d.data_ptr(), 1e-6, q.data_ptr(), k.data_ptr(), v.data_ptr(), T + N, T,
+              cos_d.data_ptr(), sin_d.data_ptr(), 1e-6, q.data_ptr(), k.data_ptr(), v.data_ptr(), T + N, T + N, T, 0,
               torch.cuda.current_stream().cuda_stream)  # fmt: skip
     torch.cuda.synchronize()
     c, s = cos[T:], sin[T:]
@@ -359,7 +359,7 @@ def test_patchify_and_unpatchify_are_bit_exact(K):
         x = (torch.arange(B * 3 * H * W, dtype=torch.float32) % 251).reshape(B, 3, H, W)
         out = torch.empty(B * (H // p) * (W // p), 3 * p * p, device="cuda", dtype=torch.bfloat16)
         xc = x.cuda()
-        _lib.call("iris_patchify", xc.data_ptr(), out.data_ptr(), B, 3, H, W, p, st)
+        _lib.call("iris_patchify", xc.data_ptr(), out.data_ptr(), B, 3, H, W, p, 0, (H // p) * (W // p), st)
         assert torch.equal(out.float().cpu(), ops.patchify(x, p).reshape(-1, 3 * p * p))
         pix = torch.randn(B * (H // p) * (W // p), p * p, 3)
         v = torch.empty(B, 3, H, W, device="cuda")

@@ -64,8 +64,12 @@ def test_invalid_calls_are_rejected_before_launch(lib):
     assert "width % 128" in msg
     msg = _einval(lib, "iris_flash_attn_fwd", 16, 16, 16, 16, 1, 3, 2, 10, 128, 0.1, 384, None)
     assert "multiple of heads_kv" in msg
-    msg = _einval(lib, "iris_patchify", 16, 16, 1, 3, 30, 32, 16, None)
+    msg = _einval(lib, "iris_patchify", 16, 16, 1, 3, 30, 32, 16, 0, 1, None)
     assert "divisible by patch_size" in msg
+    msg = _einval(lib, "iris_patchify", 16, 16, 1, 3, 32, 32, 16, 3, 2, None)
+    assert "token range" in msg
+    msg = _einval(lib, "iris_block_copy", 16, 16, 16, 16, 16, 16, 16, 16, 1, 1, 1, 24, None)
+    assert "multiples of 16" in msg
     msg = _einval(lib, "iris_timestep_embedding", 16, 16, 1, 255, 10.0, None)
     assert "even" in msg
 
