@@ -10,6 +10,11 @@ slowest rank's step time. The model is the BASELINE config-3 architecture
 random weights (std 0.02); inputs are seeded N(0, 1) noise and text states.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+    python bench.py --workload step2048 [--gpus N] ...
+
+``--workload step2048`` is BASELINE config 5 instead: one guided denoiser call
+(B = 2) at 2048^2 per step, spread over the N GPUs by Ulysses sequence
+parallelism (value = ms per step, the slowest rank's).
 
 For N > 1 run one process per GPU under torchrun. Rank 0 prints one JSON line.
 """
@@ -236,6 +241,122 @@ def profile_run(kind: str) -> None:
     print(json.dumps({"profile": kind, "finite": bool(torch.isfinite(v).all())}))
 
 
+def step2048(args, rank: int, world: int, local: int) -> None:
+    """one B = 2 (CFG pair) denoiser call at 2048^2 per step,
+    Ulysses sequence parallelism over the ranks (the call's tokens are split,
+    every rank returns the whole velocity)."""
+    import torch.distributed as dist
+
+    from iris_b200 import CudaIris, IrisWeights, _lib, baseline_step_config, synthetic_state
+    from iris_b200.parallel import init_process_group
+    from iris_b200.ulysses import TorchComm
+
+    res = 2048
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    comm = None
+    if world > 1:
+        init_process_group("nccl", timeout_s=600)
+        comm = TorchComm()
+    cfg = baseline_step_config()
+    engine = CudaIris(IrisWeights(cfg, synthetic_state(cfg, device, seed=0)), comm=comm)
+    gen = torch.Generator().manual_seed(1)
+    x_h = torch.randn(1, 3, res, res, generator=gen).repeat(2, 1, 1, 1).pin_memory()
+    tgen = torch.Generator().manual_seed(4)
+    states = torch.randn(2, TEXT_LEN, TEXT_DIM, generator=tgen).to(device)  # row 0 uncond, row 1 cond
+    text = engine.encode_text(states)
+    text_h = text.cpu().pin_memory()
+    t = torch.full((2,), 625.0, device=device)
+    x = x_h.to(device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def max_over_ranks(value: float) -> float:
+        if world == 1:
+            return value
+        m = torch.tensor([value], device=device, dtype=torch.float64)
+        dist.all_reduce(m, op=dist.ReduceOp.MAX)
+        return float(m.item())
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(args.steps):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        barrier()
+        return max_over_ranks(s.elapsed_time(e) / args.steps)
+
+    launches0 = _lib.launch_count()
+    with ClockSampler(local) as clocks:
+        ms = timed(lambda: engine(x, t, text))
+    launches = (_lib.launch_count() - launches0) // (args.steps + args.warmup)
+    v_h = torch.empty_like(x_h).pin_memory()
+
+    def e2e():
+        xd = x_h.to(device, non_blocking=True)
+        td = text_h.to(device, non_blocking=True)
+        v_h.copy_(engine(xd, t, td), non_blocking=True)
+
+    e_ms = timed(e2e)
+    if rank != 0:
+        dist.destroy_process_group()
+        return
+    flops = step_flops(2, L=(res // 16) ** 2)
+    pk = peaks()
+    per_gpu = flops / world / (ms / 1e3) / 1e12
+    line = {
+        "metric": "ms per denoise step at 2048² (B=2 CFG), Ulysses sequence parallel over N B200",
+        "value": ms,
+        "unit": "ms",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": False,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": {
+            "workload": "BASELINE config 5: one guided denoiser call (B=2: [uncond; cond]) at 2048^2, t = 625, "
+            "tokens split across N GPUs (Ulysses all-to-all around attention, all-gathered pixel K/V)",
+            "model": "iris-3b-shaped: d3072, 8 dual + 16 single-stream blocks, 24 MHA heads x 128, SwiGLU 8192, "
+            "4 post-modulated PiT blocks; random-init weights (std 0.02)",
+            "global_batch": 2,
+            "seq_len": 256 + (res // 16) ** 2,
+            "parallelism": f"ulysses{world}",
+            "step_tflop": flops / 1e12,
+            "l2": "no flush: every step streams 8.7 GB of weights, far above the 126 MB L2",
+        },
+        "roofline": {
+            "kernel": "whole step (GEMMs + attention), per GPU",
+            "bound": "tensor",
+            "achieved": per_gpu,
+            "peak": pk["bf16_sustained"],
+            "unit": "TFLOP/s",
+            "frac": per_gpu / pk["bf16_sustained"],
+            "traffic": None,
+            "peak_source": f"{pk['source']} bf16 sustained",
+        },
+        "e2e": {"value": e_ms, "unit": "ms", "h2d_bytes_per_step": x_h.numel() * 4 + text_h.numel() * 4,
+                "d2h_bytes_per_step": v_h.numel() * 4},  # fmt: skip
+        "gpu_launches": launches * args.steps,
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--gpus", type=int, default=1)
@@ -244,6 +365,7 @@ def main() -> None:
     parser.add_argument("--impl", default="ours", choices=["ours", "reference"])
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--profile", choices=["forward", "small"], help="one NVTX-marked B=2 call for ncu")
+    parser.add_argument("--workload", default="loop1024", choices=["loop1024", "step2048"])
     args = parser.parse_args()
     from iris_b200.parallel import env_world, gather_images, image_shard, init_process_group  # noqa: F401
 
@@ -255,6 +377,9 @@ def main() -> None:
         reference_arm(args, rank)
         return
     args.warmup = max(args.warmup, 3)
+    if args.workload == "step2048":
+        step2048(args, rank, world, local)
+        return
     import torch.distributed as dist
 
     from iris_b200 import CudaIris, IrisWeights, _lib, baseline_step_config, synthetic_state
