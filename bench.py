@@ -14,7 +14,9 @@ random weights (std 0.02); inputs are seeded N(0, 1) noise and text states.
 
 ``--workload step2048`` is BASELINE config 5 instead: one guided denoiser call
 (B = 2) at 2048^2 per step, spread over the N GPUs by Ulysses sequence
-parallelism (value = ms per step, the slowest rank's).
+parallelism (value = ms per step, the slowest rank's). ``--workload ops`` is
+config 2: the reference's two fused-op microbenchmarks (rms_norm_modulate and
+the qk_norm_rope pair) against the HBM roofline.
 
 For N > 1 run one process per GPU under torchrun. Rank 0 prints one JSON line.
 """
@@ -241,6 +243,82 @@ def profile_run(kind: str) -> None:
     print(json.dumps({"profile": kind, "finite": bool(torch.isfinite(v).all())}))
 
 
+def fused_ops(args) -> None:
+    """BASELINE config 2 through the reference's kernel API: rms_norm_modulate
+    on x bf16 [2, 4096, 3072] (bf16 out) and qk_norm_rope on the Q and K
+    projections bf16 [2, 4352, 3072] (24 heads, the 1024^2 RoPE table). Before
+    each timed call a 512 MB write evicts L2 (the operands fit in it) and a
+    256 MB read then replaces its dirty lines with clean ones, so the timed call
+    pays for no write-back of the flush. Each call is bracketed by CUDA events
+    on its stream; the median over the calls is reported."""
+    from iris_b200 import kernels as K
+    from iris_b200.tables import cos_sin, rope_1d, rope_2d
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    g = torch.Generator(device="cpu").manual_seed(2)
+    x = torch.randn(2, 4096, 3072, generator=g).to(device, torch.bfloat16)
+    w = (1 + 0.02 * torch.randn(3072, generator=g)).to(device)
+    shift, scale = (0.1 * torch.randn(2, 1, 3072, generator=g)).to(device), (0.1 * torch.randn(2, 1, 3072, generator=g)).to(device)
+    g3 = torch.Generator(device="cpu").manual_seed(3)
+    q, k = (torch.randn(2, 4352, 3072, generator=g3).to(device, torch.bfloat16) for _ in range(2))
+    qw, kw = (1 + 0.02 * torch.randn(128, generator=g3)).to(device), (1 + 0.02 * torch.randn(128, generator=g3)).to(device)
+    cos, sin = cos_sin(rope_1d(128, 256, 1e4), rope_2d(128, 64, 64, 1e4, 16.0, "isotropic"), device=device)
+    qo, ko = (torch.empty(2, 24, 4352, 128, device=device, dtype=torch.bfloat16) for _ in range(2))
+    flush = torch.empty(512 * 2**20, dtype=torch.uint8, device=device)
+    clean = torch.ones(64 * 2**20, dtype=torch.float32, device=device)
+
+    def timed(fn, reps):
+        for _ in range(3):
+            fn()
+        times = []
+        for _ in range(reps):
+            flush.fill_(1)  # evicts L2 and keeps the GPU busy while the events and the call are enqueued
+            clean.sum()  # clean lines replace the flush's dirty ones
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            times.append((s, e))
+        torch.cuda.synchronize()
+        return statistics.median(a.elapsed_time(b) for a, b in times)
+
+    norm_ms = timed(lambda: K.rms_norm_modulate(x, w, shift, scale, 1e-6, torch.bfloat16), max(args.steps, 20))
+
+    def qk():
+        K.qk_norm_rope(q, qw, cos, sin, 1e-6, 24, out=qo)
+        K.qk_norm_rope(k, kw, cos, sin, 1e-6, 24, out=ko)
+
+    qk_ms = timed(qk, max(args.steps, 20))
+    pk = peaks()
+    norm_bytes = 2 * (2 * 4096 * 3072 * 2) + 3072 * 4 + 2 * 2 * 3072 * 4
+    qk_bytes = 4 * (2 * 4352 * 24 * 128 * 2) + 2 * 4352 * 64 * 4 + 2 * 128 * 4
+    norm_gbs, qk_gbs = norm_bytes / norm_ms / 1e6, qk_bytes / qk_ms / 1e6
+    line = {
+        "metric": "GB/s of the fused norm ops (BASELINE config 2) vs the HBM roofline",
+        "value": min(norm_gbs, qk_gbs),
+        "unit": "GB/s",
+        "n_gpus": 1,
+        "steps": max(args.steps, 20),
+        "warmup": 3,
+        "higher_is_better": True,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": "BASELINE config 2 (i) rms_norm_modulate x bf16 [2,4096,3072] -> bf16, "
+                               "(ii) qk_norm_rope Q and K bf16 [2,4352,3072] -> [2,24,4352,128]",
+                   "l2": "flushed before every timed call (512 MB write, then a 256 MB read)"},  # fmt: skip
+        "ops": {
+            "rms_norm_modulate": {"us": norm_ms * 1e3, "bytes": norm_bytes, "gbs": norm_gbs,
+                                  "frac": norm_gbs / pk["hbm_gbs"]},  # fmt: skip
+            "qk_norm_rope_pair": {"us": qk_ms * 1e3, "bytes": qk_bytes, "gbs": qk_gbs, "frac": qk_gbs / pk["hbm_gbs"]},
+        },
+        "roofline": {"bound": "hbm", "achieved": min(norm_gbs, qk_gbs), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": min(norm_gbs, qk_gbs) / pk["hbm_gbs"], "traffic": None,
+                     "peak_source": f"{pk['source']} hbm copy"},  # fmt: skip
+    }
+    print(json.dumps(line), flush=True)
+
+
 def step2048(args, rank: int, world: int, local: int) -> None:
     """one B = 2 (CFG pair) denoiser call at 2048^2 per step,
     Ulysses sequence parallelism over the ranks (the call's tokens are split,
@@ -365,7 +443,7 @@ def main() -> None:
     parser.add_argument("--impl", default="ours", choices=["ours", "reference"])
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--profile", choices=["forward", "small"], help="one NVTX-marked B=2 call for ncu")
-    parser.add_argument("--workload", default="loop1024", choices=["loop1024", "step2048"])
+    parser.add_argument("--workload", default="loop1024", choices=["loop1024", "step2048", "ops"])
     args = parser.parse_args()
     from iris_b200.parallel import env_world, gather_images, image_shard, init_process_group  # noqa: F401
 
@@ -379,6 +457,10 @@ def main() -> None:
     args.warmup = max(args.warmup, 3)
     if args.workload == "step2048":
         step2048(args, rank, world, local)
+        return
+    if args.workload == "ops":
+        if rank == 0:
+            fused_ops(args)
         return
     import torch.distributed as dist
 

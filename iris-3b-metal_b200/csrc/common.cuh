@@ -140,6 +140,19 @@ IRIS_DEVICE void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst, i
       : "memory");
 }
 
+// Untiled bulk copy of `bytes` (multiple of 16; both addresses 16-byte
+// aligned) from global memory into this CTA's shared memory, completing on `bar`.
+IRIS_DEVICE void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// Orders this thread's earlier generic-proxy shared-memory accesses (made
+// visible to it by a barrier) before its later async-proxy (TMA) writes.
+IRIS_DEVICE void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 IRIS_DEVICE void tma_load_3d(const CUtensorMap* map, uint64_t* bar, void* dst, int32_t c0, int32_t c1,
                              int32_t c2) {
   asm volatile(

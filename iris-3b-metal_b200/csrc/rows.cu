@@ -3,11 +3,15 @@
 //   gated_residual_rms_norm(+)  src/iris_metal/kernels.py:148-175, 455-480
 //   rms_norm_add_rows           TextEmbedder norm + position table
 //
-// One warp per row; lane l owns the 4-element vectors l, l + 32, ... so every
+// Rows whose width is a multiple of 512 (3072 here) take one 128-thread CTA
+// each (see gated_residual_row_kernel); other widths one warp per row, where
+// lane l owns the 4-element vectors l, l + 32, ... so every
 // warp load is one coalesced 512-byte (fp32) or 256-byte (bf16) segment. The
 // whole row stays in registers (NV vectors per lane, width = 128 * NV), so
 // each row is read once and written once; the sum of squares is a warp
 // shuffle reduction.
+#include <algorithm>
+
 #include "common.cuh"
 #include "iris_abi_internal.h"
 
@@ -185,6 +189,147 @@ IRIS_DEVICE float block_sum(float v, float* red) {
   return red[0] + red[1] + red[2] + red[3];
 }
 
+// 16 bytes of a row as loaded (8 bf16 / f16 or 4 f32 elements), kept packed
+// until used so that a prefetched row costs few registers.
+template <typename T>
+struct Raw16 {
+  static constexpr int E = 8;
+  uint4 u;
+  IRIS_DEVICE void load(const T* p) { u = *reinterpret_cast<const uint4*>(p); }
+  IRIS_DEVICE float4 lo() const { return Vec4<T>::load(reinterpret_cast<const T*>(&u)); }
+  IRIS_DEVICE float4 hi() const { return Vec4<T>::load(reinterpret_cast<const T*>(&u) + 4); }
+};
+template <>
+struct Raw16<float> {
+  static constexpr int E = 4;
+  float4 u;
+  IRIS_DEVICE void load(const float* p) { u = *reinterpret_cast<const float4*>(p); }
+  IRIS_DEVICE float4 lo() const { return u; }
+  IRIS_DEVICE float4 hi() const { return u; }
+};
+
+// Stores E / 4 float4 as TO with the widest vector stores (16 bytes where the
+// E outputs of 2-byte types fill one).
+template <typename TO, int E>
+IRIS_DEVICE void store_vec(TO* p, const float4 (&y)[E / 4]) {
+  if constexpr (E == 8 && sizeof(TO) == 2) {
+    uint2 a, b;
+    Vec4<TO>::store(reinterpret_cast<TO*>(&a), y[0]);
+    Vec4<TO>::store(reinterpret_cast<TO*>(&b), y[1]);
+    *reinterpret_cast<uint4*>(p) = make_uint4(a.x, a.y, b.x, b.y);
+  } else {
+#pragma unroll
+    for (int h = 0; h < E / 4; ++h) Vec4<TO>::store(p + 4 * h, y[h]);
+  }
+}
+
+IRIS_DEVICE float4 norm_mod4(float4 x, float inv, const float* w, const float* sh, const float* sc, int e) {
+  const float4 g = ld4(w + e), s4 = ld4(sh + e), c4 = ld4(sc + e);
+  return make_float4(x.x * inv * g.x * (1.f + c4.x) + s4.x, x.y * inv * g.y * (1.f + c4.y) + s4.y,
+                     x.z * inv * g.z * (1.f + c4.z) + s4.z, x.w * inv * g.w * (1.f + c4.w) + s4.w);
+}
+
+// Persistent form with a TMA row ring: a resident grid of 128-thread CTAs
+// strides over the rows; thread 0 keeps up to `stages` whole input rows in
+// flight as bulk copies into shared memory (one mbarrier per slot), so each SM
+// has tens of KB of loads outstanding however long the math of a row takes.
+// A slot is refilled as soon as the block-wide sum of squares has passed its
+// barrier, i.e. once every thread holds its share of the row in registers.
+// The per-column factors w * (1 + scale[b]) and shift[b] of a thread's columns
+// stay in registers while b is unchanged: re-reading the three fp32 parameter
+// rows for every row would move six times the row's bytes through L1.
+constexpr int PIPE_MAX_STAGES = 8;
+constexpr int PIPE_SMEM_BYTES = 36 * 1024;  // row ring per CTA
+
+template <typename TX, typename TO, int VPT>
+__global__ void __launch_bounds__(ROW_THREADS) rms_norm_modulate_row_kernel(
+    const TX* __restrict__ x, RowMap xmap, TO* __restrict__ out, const float* __restrict__ weight,
+    const float* __restrict__ shift, const float* __restrict__ scale, int64_t mod_stride, int64_t rows,
+    int64_t rows_per_batch, int width, int stages, float eps) {
+  constexpr int E = Raw16<TX>::E;
+  extern __shared__ __align__(128) uint8_t ring[];
+  __shared__ uint64_t full[PIPE_MAX_STAGES];
+  __shared__ float red[2][4];
+  __shared__ int abort_flag;
+  const int t = threadIdx.x;
+  const uint32_t row_bytes = static_cast<uint32_t>(width) * sizeof(TX);
+  if (t == 0) {
+    for (int k = 0; k < stages; ++k) mbar_init(&full[k], 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (t == 0) {
+    for (int k = 0; k < stages; ++k) {
+      const int64_t r = blockIdx.x + static_cast<int64_t>(k) * gridDim.x;
+      if (r >= rows) break;
+      mbar_arrive_expect_tx(&full[k], row_bytes);
+      bulk_load(ring + k * row_bytes, x + xmap(r) * width, row_bytes, &full[k]);
+    }
+  }
+  volatile int* abort = &abort_flag;
+  float4 mul[VPT][E / 4], add[VPT][E / 4];
+  int64_t cur_b = -1;
+  int it = 0;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x, ++it) {
+    const int slot = it % stages;
+    mbar_wait(&full[slot], static_cast<uint32_t>((it / stages) & 1), abort);
+    const TX* row = reinterpret_cast<const TX*>(ring + slot * row_bytes);
+    Raw16<TX> v[VPT];
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) v[i].load(row + (i * ROW_THREADS + t) * E);
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) ss += E == 8 ? sumsq(v[i].lo()) + sumsq(v[i].hi()) : sumsq(v[i].lo());
+    const float inv = rsqrtf(block_sum(ss, red[it & 1]) / static_cast<float>(width) + eps);
+    if (*abort) break;  // read after the barrier: the same decision in every thread
+    if (t == 0) {
+      const int64_t rn = r + static_cast<int64_t>(stages) * gridDim.x;
+      if (rn < rows) {
+        fence_proxy_async_smem();  // the slot's reads (ordered by the barrier) before the copy's writes
+        mbar_arrive_expect_tx(&full[slot], row_bytes);
+        bulk_load(ring + slot * row_bytes, x + xmap(rn) * width, row_bytes, &full[slot]);
+      }
+    }
+    const int64_t b = r / rows_per_batch;
+    if (b != cur_b) {  // this thread's columns of w * (1 + scale[b]) and shift[b], kept in registers
+      cur_b = b;
+      const float* sh = shift + b * mod_stride;
+      const float* sc = scale + b * mod_stride;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+#pragma unroll
+        for (int h = 0; h < E / 4; ++h) {
+          const int e = (i * ROW_THREADS + t) * E + 4 * h;
+          const float4 g = ld4(weight + e), c4 = ld4(sc + e);
+          mul[i][h] = make_float4(g.x * (1.f + c4.x), g.y * (1.f + c4.y), g.z * (1.f + c4.z), g.w * (1.f + c4.w));
+          add[i][h] = ld4(sh + e);
+        }
+      }
+    }
+    TO* o = out + r * width;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int e = (i * ROW_THREADS + t) * E;
+      float4 y[E / 4];
+#pragma unroll
+      for (int h = 0; h < E / 4; ++h) {
+        const float4 xv = h == 0 ? v[i].lo() : v[i].hi();
+        const float4 m = mul[i][h], a = add[i][h];
+        y[h] = make_float4(xv.x * inv * m.x + a.x, xv.y * inv * m.y + a.y, xv.z * inv * m.z + a.z,
+                           xv.w * inv * m.w + a.w);
+      }
+      store_vec<TO, E>(o + e, y);
+    }
+  }
+  if (*abort && t == 0) {
+    // copies may still be landing in the ring: give them time before the CTA exits
+    const uint64_t t0 = global_timer_ns();
+    while (global_timer_ns() - t0 < 1000000ull) {
+    }
+  }
+}
+
 template <typename TB, typename TO, int VPT>
 __global__ void __launch_bounds__(ROW_THREADS) gated_residual_row_kernel(
     float* __restrict__ residual, RowMap rmap, const TB* __restrict__ branch, RowMap bmap,
@@ -307,9 +452,47 @@ __global__ void __launch_bounds__(WARPS * 32) rms_norm_add_kernel(float* __restr
     MACRO(32);                      \
   }
 
+// CTAs of a persistent row launch: as many as are resident at once, at most one per row.
+template <typename Kernel>
+unsigned resident_grid(Kernel kernel, int64_t rows, int smem = 0) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, ROW_THREADS, smem) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  const int64_t cap = static_cast<int64_t>(num_sms()) * per_sm;
+  return static_cast<unsigned>(rows < cap ? (rows > 0 ? rows : 1) : cap);
+}
+
 template <typename TX, typename TO>
 int launch_norm_modulate(const void* x, RowMap xm, void* out, const float* w, const float* sh, const float* sc,
                          int64_t mod_stride, int64_t rows, int64_t rpb, int width, float eps, cudaStream_t st) {
+  constexpr int E = Raw16<TX>::E;
+  const int64_t row_bytes = static_cast<int64_t>(width) * sizeof(TX);
+  const int stages = static_cast<int>(std::min<int64_t>(PIPE_MAX_STAGES, PIPE_SMEM_BYTES / row_bytes));
+  if (width % (E * ROW_THREADS) == 0 && width / (E * ROW_THREADS) <= 8 && stages >= 2 && aligned16(x) &&
+      (xm.seg_stride * row_bytes) % 16 == 0 && (xm.seg_offset * row_bytes) % 16 == 0) {
+    const int vpt = width / (E * ROW_THREADS);
+    const int smem = static_cast<int>(stages * row_bytes);
+#define IRIS_ROW(VPT)                                                                                              \
+  {                                                                                                                \
+    auto kernel = rms_norm_modulate_row_kernel<TX, TO, VPT>;                                                       \
+    const unsigned grid = resident_grid(kernel, rows, smem);                                                       \
+    kernel<<<grid, ROW_THREADS, smem, st>>>(reinterpret_cast<const TX*>(x), xm, reinterpret_cast<TO*>(out), w, sh, \
+                                            sc, mod_stride, rows, rpb, width, stages, eps);                       \
+  }
+    switch (vpt) {
+      case 1: IRIS_ROW(1); break;
+      case 2: IRIS_ROW(2); break;
+      case 3: IRIS_ROW(3); break;
+      case 4: IRIS_ROW(4); break;
+      case 5: IRIS_ROW(5); break;
+      case 6: IRIS_ROW(6); break;
+      case 7: IRIS_ROW(7); break;
+      default: IRIS_ROW(8); break;
+    }
+#undef IRIS_ROW
+    IRIS_CUDA(cudaGetLastError());
+    return IRIS_OK;
+  }
   const int nv = width / 128;
   const unsigned grid = static_cast<unsigned>((rows + WARPS - 1) / WARPS);
 #define IRIS_LAUNCH(NV)                                                                                           \
