@@ -52,6 +52,13 @@ WORKLOAD = (
 )
 
 
+# DRAM bytes (read + write) per GEMM launch of the N = 1 workload, mean over the
+# 564 launches of one step, from
+#   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum --clock-control none \
+#       -k regex:gemm_bf16 -c 564 --csv --log-file gemm_traffic.csv python bench.py --steps 1 --warmup 3 --no-cpu-baseline
+GEMM_TRAFFIC_PER_LAUNCH = 2655.8e6
+
+
 def peaks() -> dict:
     path = REPO / "MEASURED_PEAKS.json"
     if path.exists():
@@ -514,7 +521,7 @@ def main() -> None:
     barrier()
     torch.cuda.synchronize()
     launches = (_lib.launch_count() - launches0) // args.steps
-    gemm_flops, gemm_ms, gemm_n = K.profile_gemms(False)
+    gemm_flops, gemm_ms, gemm_n, gemm_bytes = K.profile_gemms(False)
     ms = max_over_ranks(start.elapsed_time(end) / args.steps)
     value = IMAGES / (ms / 1e3)
 
@@ -603,13 +610,16 @@ def main() -> None:
             "l2": "no flush: every step streams 8.7 GB of weights, far above the 126 MB L2",
         },
         "roofline": {
-            "kernel": "gemm_bf16_kernel (tcgen05, all GEMM launches of the timed region)",
+            "kernel": "gemm_bf16_pair_kernel (tcgen05 cta_group::2, all GEMM launches of the timed region)",
             "bound": "tensor",
             "achieved": achieved,
             "peak": pk["bf16_sustained"],
             "unit": "TFLOP/s",
             "frac": (achieved / pk["bf16_sustained"]) if achieved else None,
-            "traffic": None,
+            "traffic": GEMM_TRAFFIC_PER_LAUNCH if world == 1 else None,
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, mean over the 564 GEMM launches of "
+            "one N=1 step (4 guided calls of 16 rows); units: bytes per launch",
+            "algorithmic_bytes_per_launch": gemm_bytes / gemm_n if gemm_n else None,
             "launches": gemm_n,
             "peak_source": f"{pk['source']} bf16 sustained",
         },

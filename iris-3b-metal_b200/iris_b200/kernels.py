@@ -285,7 +285,17 @@ def gemm_grouped(problems: list, stream: int) -> None:
     _lib.call("iris_gemm_bf16_grouped", array, len(problems), stream)
     if timing:
         end.record()
-        _gemm_profile.append((start, end, sum(2.0 * q.M * q.N * q.K for q in problems)))
+        _gemm_profile.append((start, end, sum(2.0 * q.M * q.N * q.K for q in problems),
+                              sum(_gemm_bytes(q) for q in problems)))  # fmt: skip
+
+
+def _gemm_bytes(q) -> float:
+    """Algorithmic HBM bytes of one problem: A and W read once, the output
+    (and a gate's aux rows) once."""
+    cols = q.N // 2 if q.epilogue == _lib.EPI_SWIGLU else q.N
+    out = q.M * cols * (4 if q.out_dtype == _lib.F32 else 2)
+    aux = q.M * q.N * 2 if q.epilogue == _lib.EPI_GATE else 0
+    return 2.0 * (q.M + q.N) * q.K + out + aux + (4 * q.N if q.bias else 0)
 
 
 def gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor, **kwargs) -> torch.Tensor:
@@ -300,7 +310,8 @@ _gemm_profile: list | None = None
 def profile_gemms(enable: bool):
     """Start (``True``) or stop (``False``) timing every GEMM launch with CUDA
     events on its stream. Stopping synchronises and returns
-    ``(algorithmic FLOPs, milliseconds, launches)`` summed over the launches."""
+    ``(algorithmic FLOPs, milliseconds, launches, algorithmic bytes)`` summed
+    over the launches."""
     global _gemm_profile
     if enable:
         _gemm_profile = []
@@ -309,7 +320,7 @@ def profile_gemms(enable: bool):
     torch.cuda.synchronize()
     flops = sum(r[2] for r in records)
     ms = sum(r[0].elapsed_time(r[1]) for r in records)
-    return flops, ms, len(records)
+    return flops, ms, len(records), sum(r[3] for r in records)
 
 
 def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor, scale: float | None = None):
