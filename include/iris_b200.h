@@ -42,6 +42,7 @@ extern "C" {
 #define IRIS_EPI_STORE 0  /* out = acc (+ bias)                        */
 #define IRIS_EPI_SWIGLU 1 /* out = silu(acc[w1 block]) * acc[w3 block] */
 #define IRIS_EPI_GATE 2   /* out = aux * sigmoid(acc)                  */
+#define IRIS_EPI_HEADS 3  /* [q | k | v] heads -> normed, rotated head layouts (see iris_heads_epilogue) */
 
 /* Residual-kernel follow-ups (iris_gated_residual_rms_norm next_mode) */
 #define IRIS_NEXT_NONE 0
@@ -116,7 +117,32 @@ int iris_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw, void*
                    int64_t out_seg_rows, int64_t out_seg_stride, int64_t out_seg_offset, int64_t aux_seg_rows,
                    int64_t aux_seg_stride, int64_t aux_seg_offset, void* stream);
 
-/* One problem of a grouped launch: the arguments of iris_gemm_bf16 as plain data. */
+/* IRIS_EPI_HEADS: the GEMM's columns are heads_q + 2 heads_kv slots of 128
+ * (q | k | v, the layout iris_qkv_heads reads); row m is token position
+ * t = out_map(m) % tokens of sample b = out_map(m) / tokens. q and k slots are
+ * RMS-normed over their 128 fp32 accumulators times q_weight / k_weight and
+ * rotated by cos / sin[t] (pairs (2i, 2i+1)), v is copied; each lands in
+ * q_out / k_out / v_out (bf16) at [b, h, t, 128] with n_out (q) or n_out_kv
+ * (k, v) positions per (b, h), or at [h, b, t, 128] with head_major = 1.
+ * src/iris_metal/model.py:243-250,277-279,304-306 (projection + qk_norm_rope
+ * twice + the V copy) in one pass; cos / sin must cover `tokens` rows. */
+typedef struct iris_heads_epilogue {
+  void* q_out;
+  void* k_out;
+  void* v_out;
+  const float* q_weight;
+  const float* k_weight;
+  const float* cos;
+  const float* sin;
+  float eps;
+  int head_major;
+  int64_t heads_q, heads_kv;
+  int64_t tokens, batch;
+  int64_t n_out, n_out_kv;
+} iris_heads_epilogue;
+
+/* One problem of a grouped launch: the arguments of iris_gemm_bf16 as plain
+ * data, plus `heads` for IRIS_EPI_HEADS (null otherwise; `out` is unused then). */
 typedef struct iris_gemm_problem {
   const void* a;
   int64_t lda;
@@ -132,6 +158,7 @@ typedef struct iris_gemm_problem {
   int64_t ldaux;
   int64_t out_seg_rows, out_seg_stride, out_seg_offset;
   int64_t aux_seg_rows, aux_seg_stride, aux_seg_offset;
+  const iris_heads_epilogue* heads;
 } iris_gemm_problem;
 
 /* 1 to 4 independent GEMMs in one persistent launch (the text- and

@@ -22,8 +22,12 @@
 // Epilogues: STORE (optional bias, fp32 or bf16 out), SWIGLU (each 256-wide
 // W tile holds 128 rows of w1 then the matching 128 rows of w3; writes
 // silu(a) * b as bf16, 128 columns per tile), GATE (out = aux * sigmoid(acc),
-// bf16). Output and aux rows go through a segmented row map so a stream's
-// rows can live inside a joint [text | image] token buffer.
+// bf16), HEADS (two 128-wide [q | k | v] head slots per tile: q and k
+// RMS-normed and rotated, all three written to their [b, h, token, 128] or
+// head-major layouts). Output and aux rows go through a segmented row map so
+// a stream's rows can live inside a joint [text | image] token buffer.
+#include <algorithm>
+
 #include "common.cuh"
 #include "iris_abi_internal.h"
 
@@ -48,7 +52,24 @@ constexpr int GROUP_M = 16;           // tile rasterisation: 16 M-blocks per gro
 constexpr int MAX_PROBLEMS = 4;
 constexpr size_t SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + 256 /*barriers*/;
 
-enum Epilogue : int { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_GATE = 2 };
+enum Epilogue : int { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_GATE = 2, EPI_HEADS = 3 };
+
+// EPI_HEADS: the tile's 256 columns are two 128-wide head slots of a [q | k |
+// v] projection; q and k slots are RMS-normed and rotated, v copied, each to
+// its head layout (what iris_qkv_heads does from a stored projection).
+struct HeadsOut {
+  __nv_bfloat16* q;
+  __nv_bfloat16* k;
+  __nv_bfloat16* v;
+  const float* qw;
+  const float* kw;
+  const float* cos;
+  const float* sin;
+  float eps;
+  int head_major;
+  int hq, hkv;
+  int64_t tokens, batch, n_out, n_out_kv;
+};
 
 struct Problem {
   int M, N, K;
@@ -62,6 +83,7 @@ struct Problem {
   const __nv_bfloat16* aux;     // GATE: [*, ldaux]
   int64_t ldaux;
   RowMap aux_map;
+  HeadsOut heads;               // HEADS only
 };
 
 struct Batch {
@@ -119,6 +141,141 @@ IRIS_DEVICE void store_row32(const Problem& p, int64_t prow, int col0, const flo
     float4* d4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + prow * p.ldc + col0);
 #pragma unroll
     for (int j = 0; j < 8; ++j) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  }
+}
+
+// One 128-wide head slot of row m (TMEM columns [col, col + 128) of this
+// thread's lane) -> its q / k / v row: RMSNorm over the 128 fp32 accumulators
+// times the gain, rotary pairs (2i, 2i+1) by the token's cos / sin, bf16.
+// Every lane of the warp runs the TMEM loads (warp-collective); only lanes
+// with a real row (`row_ok`) store.
+IRIS_DEVICE void store_head_slot(const HeadsOut& hd, uint32_t t_col, int slot, int64_t bn, bool row_ok) {
+  const int64_t b = bn / hd.tokens, t = bn % hd.tokens;
+  const bool is_q = slot < hd.hq, is_k = !is_q && slot < hd.hq + hd.hkv;
+  const int h = is_q ? slot : is_k ? slot - hd.hq : slot - hd.hq - hd.hkv;
+  const int heads = is_q ? hd.hq : hd.hkv;
+  const int64_t len = is_q ? hd.n_out : hd.n_out_kv;
+  __nv_bfloat16* base = is_q ? hd.q : is_k ? hd.k : hd.v;
+  __nv_bfloat16* dst = base + ((hd.head_major ? h * hd.batch + b : b * heads + h) * len + t) * 128;
+  float inv = 1.f;
+  const float* gain = is_q ? hd.qw : hd.kw;
+  if (is_q || is_k) {
+    float ss = 0.f;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      uint32_t r[32];
+      tmem_ld32(t_col + c * 32, r);
+      tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) ss = fmaf(__uint_as_float(r[j]), __uint_as_float(r[j]), ss);
+    }
+    inv = rsqrtf(ss * (1.f / 128.f) + hd.eps);
+  }
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    uint32_t r[32];
+    tmem_ld32(t_col + c * 32, r);
+    tmem_wait_ld();
+    uint32_t packed[16];
+    if (is_q || is_k) {
+      const float4* g4 = reinterpret_cast<const float4*>(gain + c * 32);
+      const float4* c4 = reinterpret_cast<const float4*>(hd.cos + t * 64 + c * 16);
+      const float4* s4 = reinterpret_cast<const float4*>(hd.sin + t * 64 + c * 16);
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {  // 8 columns = 4 rotary pairs at a time
+        const float4 ga = __ldg(g4 + 2 * q4), gb = __ldg(g4 + 2 * q4 + 1);
+        const float4 cs = __ldg(c4 + q4), sn = __ldg(s4 + q4);
+        const float g[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+        const float cc[4] = {cs.x, cs.y, cs.z, cs.w}, sc[4] = {sn.x, sn.y, sn.z, sn.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int j = q4 * 8 + 2 * e;
+          const float a = __uint_as_float(r[j]) * inv * g[2 * e];
+          const float bb = __uint_as_float(r[j + 1]) * inv * g[2 * e + 1];
+          packed[q4 * 4 + e] = pack_bf16x2(a * cc[e] - bb * sc[e], a * sc[e] + bb * cc[e]);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) packed[j] = pack_bf16x2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+    }
+    if (row_ok) {
+      uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        d4[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+    }
+  }
+}
+
+// The epilogue of one accumulator tile for this thread's row m (TMEM lane
+// base `t_base`, column 0 of the accumulator); `nb` is the tile's N block.
+IRIS_DEVICE void epilogue_row(const Problem& p, uint32_t t_base, int64_t m, int nb) {
+  const bool row_ok = m < p.M;
+  if (p.epilogue == EPI_HEADS) {
+    const int64_t bn = row_ok ? p.out_map(m) : 0;
+    const int slots = p.heads.hq + 2 * p.heads.hkv;
+#pragma unroll 1
+    for (int k = 0; k < 2; ++k) {
+      const int slot = nb * 2 + k;  // uniform across the warp, as the TMEM loads require
+      if (slot < slots) store_head_slot(p.heads, t_base + k * 128, slot, bn, row_ok);
+    }
+    return;
+  }
+  if (p.epilogue == EPI_SWIGLU) {
+    const int64_t prow = row_ok ? p.out_map(m) : 0;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      uint32_t ra[32], rb[32];
+      tmem_ld32(t_base + c * 32, ra);
+      tmem_ld32(t_base + 128 + c * 32, rb);
+      tmem_wait_ld();
+      const int col0 = nb * (BN / 2) + c * 32;
+      if (row_ok && col0 < p.N / 2) {
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float a = __uint_as_float(ra[j]);
+          v[j] = a * sigmoidf_fast(a) * __uint_as_float(rb[j]);
+        }
+        store_row32(p, prow, col0, v);
+      }
+    }
+    return;
+  }
+  const int64_t prow = row_ok ? p.out_map(m) : 0;
+  const int64_t arow = (row_ok && p.epilogue == EPI_GATE) ? p.aux_map(m) : 0;
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; ++c) {
+    uint32_t r[32];
+    tmem_ld32(t_base + c * 32, r);
+    tmem_wait_ld();
+    const int col0 = nb * BN + c * 32;
+    if (row_ok && col0 < p.N) {
+      float v[32];
+      if (p.epilogue == EPI_GATE) {
+        const uint4* a4 = reinterpret_cast<const uint4*>(p.aux + arow * p.ldaux + col0);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint4 w = a4[j];
+          const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            const float2 f = unpack_bf16x2(ws[h]);
+            const int e = j * 8 + h * 2;
+            v[e] = f.x * sigmoidf_fast(__uint_as_float(r[e]));
+            v[e + 1] = f.y * sigmoidf_fast(__uint_as_float(r[e + 1]));
+          }
+        }
+      } else if (p.bias != nullptr) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) + __ldg(p.bias + col0 + j);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+      }
+      store_row32(p, prow, col0, v);
+    }
   }
 }
 
@@ -254,63 +411,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!__all_sync(0xffffffffu, mbar_wait(&s->tmem_full[acc], acc_phase, abort))) break;
       tc_fence_after();
       const uint32_t t_base = tmem + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(quarter * 32) << 16);
-      const int64_t m = static_cast<int64_t>(tl.mb) * BM + row_in_tile;
-      const bool row_ok = m < p.M;
-      if (p.epilogue == EPI_SWIGLU) {
-        const int64_t prow = row_ok ? p.out_map(m) : 0;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t ra[32], rb[32];
-          tmem_ld32(t_base + c * 32, ra);
-          tmem_ld32(t_base + 128 + c * 32, rb);
-          tmem_wait_ld();
-          const int col0 = tl.nb * (BN / 2) + c * 32;
-          if (row_ok && col0 < p.N / 2) {
-            float v[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float a = __uint_as_float(ra[j]);
-              v[j] = a * sigmoidf_fast(a) * __uint_as_float(rb[j]);
-            }
-            store_row32(p, prow, col0, v);
-          }
-        }
-      } else {
-        const int64_t prow = row_ok ? p.out_map(m) : 0;
-        const int64_t arow = (row_ok && p.epilogue == EPI_GATE) ? p.aux_map(m) : 0;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(t_base + c * 32, r);
-          tmem_wait_ld();
-          const int col0 = tl.nb * BN + c * 32;
-          if (row_ok && col0 < p.N) {
-            float v[32];
-            if (p.epilogue == EPI_GATE) {
-              const uint4* a4 = reinterpret_cast<const uint4*>(p.aux + arow * p.ldaux + col0);
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const uint4 w = a4[j];
-                const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-                for (int h = 0; h < 4; ++h) {
-                  const float2 f = unpack_bf16x2(ws[h]);
-                  const int e = j * 8 + h * 2;
-                  v[e] = f.x * sigmoidf_fast(__uint_as_float(r[e]));
-                  v[e + 1] = f.y * sigmoidf_fast(__uint_as_float(r[e + 1]));
-                }
-              }
-            } else if (p.bias != nullptr) {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) + __ldg(p.bias + col0 + j);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-            }
-            store_row32(p, prow, col0, v);
-          }
-        }
-      }
+      epilogue_row(p, t_base, static_cast<int64_t>(tl.mb) * BM + row_in_tile, tl.nb);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s->tmem_empty[acc]);
@@ -494,62 +595,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       if (!__all_sync(0xffffffffu, mbar_wait_cluster(&s->tmem_full[acc], acc_phase, abort))) break;
       tc_fence_after();
       const uint32_t t_base = tmem + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(quarter * 32) << 16);
-      const int64_t m = static_cast<int64_t>(tl.mb) * pair::BM + static_cast<int64_t>(rank) * 128 + row_in_tile;
-      const bool row_ok = m < p.M;
-      const int64_t prow = row_ok ? p.out_map(m) : 0;
-      if (p.epilogue == EPI_SWIGLU) {
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t ra[32], rb[32];
-          tmem_ld32(t_base + c * 32, ra);
-          tmem_ld32(t_base + 128 + c * 32, rb);
-          tmem_wait_ld();
-          const int col0 = tl.nb * (BN / 2) + c * 32;
-          if (row_ok && col0 < p.N / 2) {
-            float v[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float a = __uint_as_float(ra[j]);
-              v[j] = a * sigmoidf_fast(a) * __uint_as_float(rb[j]);
-            }
-            store_row32(p, prow, col0, v);
-          }
-        }
-      } else {
-        const int64_t arow = (row_ok && p.epilogue == EPI_GATE) ? p.aux_map(m) : 0;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(t_base + c * 32, r);
-          tmem_wait_ld();
-          const int col0 = tl.nb * BN + c * 32;
-          if (row_ok && col0 < p.N) {
-            float v[32];
-            if (p.epilogue == EPI_GATE) {
-              const uint4* a4 = reinterpret_cast<const uint4*>(p.aux + arow * p.ldaux + col0);
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const uint4 w = a4[j];
-                const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-                for (int h = 0; h < 4; ++h) {
-                  const float2 f = unpack_bf16x2(ws[h]);
-                  const int e = j * 8 + h * 2;
-                  v[e] = f.x * sigmoidf_fast(__uint_as_float(r[e]));
-                  v[e + 1] = f.y * sigmoidf_fast(__uint_as_float(r[e + 1]));
-                }
-              }
-            } else if (p.bias != nullptr) {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) + __ldg(p.bias + col0 + j);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-            }
-            store_row32(p, prow, col0, v);
-          }
-        }
-      }
+      epilogue_row(p, t_base, static_cast<int64_t>(tl.mb) * pair::BM + static_cast<int64_t>(rank) * 128 + row_in_tile,
+                   tl.nb);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(empty_leader + static_cast<uint32_t>(acc) * 8u);
@@ -562,16 +609,45 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   if (warp == 1) tmem_dealloc_pair(tmem, TMEM_COLS);
 }
 
+int check_heads(const iris_gemm_problem& q) {
+  const iris_heads_epilogue* hd = q.heads;
+  IRIS_REQUIRE(hd != nullptr, "iris_gemm_bf16: the heads epilogue needs its parameters");
+  IRIS_REQUIRE(hd->heads_q > 0 && hd->heads_kv >= 0 && q.N == (hd->heads_q + 2 * hd->heads_kv) * 128,
+               "iris_gemm_bf16: heads epilogue needs N = (heads_q + 2 heads_kv) * 128");
+  IRIS_REQUIRE(hd->q_out && hd->q_weight && hd->cos && hd->sin &&
+                   (hd->heads_kv == 0 || (hd->k_out && hd->v_out && hd->k_weight)),
+               "iris_gemm_bf16: heads epilogue null pointer");
+  IRIS_REQUIRE(aligned16(hd->q_out) && aligned16(hd->q_weight) && aligned16(hd->cos) && aligned16(hd->sin) &&
+                   (hd->heads_kv == 0 || (aligned16(hd->k_out) && aligned16(hd->v_out) && aligned16(hd->k_weight))),
+               "iris_gemm_bf16: heads epilogue pointers must be 16-byte aligned");
+  IRIS_REQUIRE(hd->tokens > 0 && hd->batch > 0 && hd->tokens <= hd->n_out &&
+                   (hd->heads_kv == 0 || hd->tokens <= hd->n_out_kv),
+               "iris_gemm_bf16: heads epilogue needs tokens <= n_out, n_out_kv");
+  // the largest row the map produces must stay inside batch * tokens positions
+  const int64_t last = (q.M - 1) / q.out_seg_rows * q.out_seg_stride + q.out_seg_offset +
+                       std::min<int64_t>(q.out_seg_rows, q.M) - 1;
+  IRIS_REQUIRE(q.out_seg_stride >= 0 && q.out_seg_offset >= 0 && last < hd->batch * hd->tokens,
+               "iris_gemm_bf16: heads epilogue row map leaves the batch * tokens positions");
+  return IRIS_OK;
+}
+
 int check_problem(const iris_gemm_problem& q) {
-  IRIS_REQUIRE(q.a && q.w && q.out, "iris_gemm_bf16: null pointer");
+  if (q.epilogue == EPI_HEADS) {
+    IRIS_REQUIRE(q.a && q.w, "iris_gemm_bf16: null pointer");
+  } else {
+    IRIS_REQUIRE(q.a && q.w && q.out, "iris_gemm_bf16: null pointer");
+  }
   IRIS_REQUIRE(q.M > 0 && q.N > 0 && q.K > 0, "iris_gemm_bf16: empty problem");
   IRIS_REQUIRE(q.M < (1ll << 31) && q.N < (1ll << 31) && q.K < (1ll << 31), "iris_gemm_bf16: dimension too large");
   IRIS_REQUIRE(q.K % 8 == 0 && q.lda % 8 == 0 && q.ldw % 8 == 0 && q.lda >= q.K && q.ldw >= q.K,
                "iris_gemm_bf16: K and leading dimensions must be multiples of 8 (16-byte TMA rows)");
   IRIS_REQUIRE(q.N % 32 == 0, "iris_gemm_bf16: N must be a multiple of 32");
-  IRIS_REQUIRE(q.epilogue >= EPI_STORE && q.epilogue <= EPI_GATE, "iris_gemm_bf16: unknown epilogue");
+  IRIS_REQUIRE(q.epilogue >= EPI_STORE && q.epilogue <= EPI_HEADS, "iris_gemm_bf16: unknown epilogue");
+  IRIS_REQUIRE(q.out_seg_rows > 0 && q.aux_seg_rows > 0, "iris_gemm_bf16: row maps need seg_rows > 0");
+  IRIS_REQUIRE(aligned16(q.a) && aligned16(q.w), "iris_gemm_bf16: pointers must be 16-byte aligned");
+  if (q.epilogue == EPI_HEADS) return check_heads(q);
   IRIS_REQUIRE(q.out_dtype == 0 || q.out_dtype == 1, "iris_gemm_bf16: out dtype must be f32 or bf16");
-  IRIS_REQUIRE(aligned16(q.a) && aligned16(q.w) && aligned16(q.out), "iris_gemm_bf16: pointers must be 16-byte aligned");
+  IRIS_REQUIRE(aligned16(q.out), "iris_gemm_bf16: pointers must be 16-byte aligned");
   IRIS_REQUIRE(q.ldc % 8 == 0, "iris_gemm_bf16: ldc must be a multiple of 8");
   if (q.epilogue == EPI_SWIGLU) {
     IRIS_REQUIRE(q.N % BN == 0 && q.out_dtype == 1 && q.ldc >= q.N / 2,
@@ -584,7 +660,6 @@ int check_problem(const iris_gemm_problem& q) {
                  "iris_gemm_bf16: gate epilogue needs an aligned bf16 aux with ldaux % 8 == 0");
     IRIS_REQUIRE(q.bias == nullptr, "iris_gemm_bf16: gate epilogue takes no bias");
   }
-  IRIS_REQUIRE(q.out_seg_rows > 0 && q.aux_seg_rows > 0, "iris_gemm_bf16: row maps need seg_rows > 0");
   return IRIS_OK;
 }
 
@@ -629,6 +704,14 @@ extern "C" int iris_gemm_bf16_grouped(const iris_gemm_problem* problems, int cou
     p.aux = reinterpret_cast<const __nv_bfloat16*>(q.aux);
     p.ldaux = q.ldaux;
     p.aux_map = RowMap{q.aux_seg_rows, q.aux_seg_stride, q.aux_seg_offset};
+    p.heads = HeadsOut{};
+    if (q.epilogue == EPI_HEADS) {
+      const iris_heads_epilogue& hd = *q.heads;
+      p.heads = HeadsOut{static_cast<__nv_bfloat16*>(hd.q_out), static_cast<__nv_bfloat16*>(hd.k_out),
+                         static_cast<__nv_bfloat16*>(hd.v_out), hd.q_weight, hd.k_weight, hd.cos, hd.sin, hd.eps,
+                         hd.head_major, static_cast<int>(hd.heads_q), static_cast<int>(hd.heads_kv), hd.tokens,
+                         hd.batch, hd.n_out, hd.n_out_kv};
+    }
     total += static_cast<int64_t>(p.num_m) * p.num_n;
     IRIS_REQUIRE(total < (1ll << 30), "iris_gemm_bf16_grouped: too many tiles");
     bt.tile_start[i + 1] = static_cast<int>(total);
@@ -695,5 +778,7 @@ extern "C" int iris_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t
   q.aux_seg_rows = aux_seg_rows;
   q.aux_seg_stride = aux_seg_stride;
   q.aux_seg_offset = aux_seg_offset;
+  q.heads = nullptr;
+  IRIS_REQUIRE(epilogue != iris::gemm::EPI_HEADS, "iris_gemm_bf16: the heads epilogue runs through iris_gemm_bf16_grouped");
   return iris_gemm_bf16_grouped(&q, 1, stream);
 }

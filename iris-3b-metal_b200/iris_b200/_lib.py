@@ -14,7 +14,7 @@ LIBRARY = Path(__file__).resolve().parent / "libiris_b200.so"
 
 IRIS_OK, IRIS_EINVAL, IRIS_ECUDA = 0, 1, 2
 F32, BF16, F16 = 0, 1, 2
-EPI_STORE, EPI_SWIGLU, EPI_GATE = 0, 1, 2
+EPI_STORE, EPI_SWIGLU, EPI_GATE, EPI_HEADS = 0, 1, 2, 3
 NEXT_NONE, NEXT_NORM_MODULATE, NEXT_SILU_ADD = 0, 1, 2
 
 P, I64, I32, F = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float
@@ -45,6 +45,16 @@ SIGNATURES: dict[str, list] = {
     "iris_all_finite": [P, I64, P, P],
 }
 
+class HeadsEpilogue(ctypes.Structure):
+    """``iris_heads_epilogue`` of include/iris_b200.h."""
+
+    _fields_ = [
+        ("q_out", P), ("k_out", P), ("v_out", P), ("q_weight", P), ("k_weight", P), ("cos", P), ("sin", P),
+        ("eps", F), ("head_major", I32), ("heads_q", I64), ("heads_kv", I64), ("tokens", I64), ("batch", I64),
+        ("n_out", I64), ("n_out_kv", I64),
+    ]  # fmt: skip
+
+
 class GemmProblem(ctypes.Structure):
     """``iris_gemm_problem`` of include/iris_b200.h."""
 
@@ -53,6 +63,7 @@ class GemmProblem(ctypes.Structure):
         ("M", I64), ("N", I64), ("K", I64), ("epilogue", I32), ("bias", P), ("aux", P), ("ldaux", I64),
         ("out_seg_rows", I64), ("out_seg_stride", I64), ("out_seg_offset", I64),
         ("aux_seg_rows", I64), ("aux_seg_stride", I64), ("aux_seg_offset", I64),
+        ("heads", ctypes.POINTER(HeadsEpilogue)),
     ]  # fmt: skip
 
 

@@ -19,6 +19,8 @@ engine (``gemm``, ``flash_attention``, ...) follow the same rules.
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from iris_b200 import _lib
@@ -245,33 +247,72 @@ def pixel_mlp_(
 def gemm_problem(
     a: torch.Tensor,
     w: torch.Tensor,
-    out: torch.Tensor,
+    out: torch.Tensor | None,
     *,
     bias: torch.Tensor | None = None,
     epilogue: int = _lib.EPI_STORE,
     aux: torch.Tensor | None = None,
     out_rows: tuple[int, int, int] | None = None,
     aux_rows: tuple[int, int, int] | None = None,
+    heads: "HeadsOut | None" = None,
 ) -> "_lib.GemmProblem":
     """Validate one ``out = epilogue(a @ w.T)`` and describe it for the library:
     ``a``: bf16 ``[M, K]`` (row stride may exceed K), ``w``: bf16 ``[N, K]``;
-    ``out`` rows through the row map ``(seg_rows, seg_stride, seg_offset)``."""
+    ``out`` rows through the row map ``(seg_rows, seg_stride, seg_offset)``.
+    With ``heads`` (:class:`HeadsOut`) the epilogue is ``EPI_HEADS`` and ``out``
+    is unused: the ``[q | k | v]`` columns go normed and rotated to the head
+    tensors, row ``m`` being token position ``map(m) % tokens``."""
     _require(a.dim() == 2 and w.dim() == 2 and a.dtype == w.dtype == torch.bfloat16, "gemm needs bf16 [M, K] x [N, K]")
-    _require(a.stride(1) == 1 and w.stride(1) == 1 and out.stride(-1) == 1, "gemm operands must be row-major")
+    _require(a.stride(1) == 1 and w.stride(1) == 1, "gemm operands must be row-major")
     M, K = a.shape
     N = w.shape[0]
     _require(w.shape[1] == K, "gemm: inner dimensions differ")
     if bias is not None:
         _require_fp32(bias=bias)
         _require(bias.numel() == N, "gemm: bias width")
-    _require_cuda(a, w, out)
     out_rows = out_rows or (M, 0, 0)
     aux_rows = aux_rows or (M, 0, 0)
+    if heads is not None:
+        _require_cuda(a, w)
+        problem = _lib.GemmProblem(
+            a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), None, _lib.BF16, 0, M, N, K, _lib.EPI_HEADS, None,
+            None, 0, *out_rows, *aux_rows, ctypes.pointer(heads.struct),
+        )  # fmt: skip
+        problem._keep = heads  # the struct must outlive the launch call
+        return problem
+    _require(out.stride(-1) == 1, "gemm operands must be row-major")
+    _require_cuda(a, w, out)
     return _lib.GemmProblem(
         a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), out.data_ptr(), _dtype(out),
         out.stride(-2) if out.dim() >= 2 else N, M, N, K, epilogue, _ptr(bias), _ptr(aux),
-        aux.stride(-2) if aux is not None else 0, *out_rows, *aux_rows,
+        aux.stride(-2) if aux is not None else 0, *out_rows, *aux_rows, None,
     )  # fmt: skip
+
+
+class HeadsOut:
+    """Targets of the ``EPI_HEADS`` GEMM epilogue (``iris_heads_epilogue``):
+    ``q`` / ``k`` / ``v`` bf16 head tensors holding ``[B, H, n, 128]`` (or
+    ``[H, B, n, 128]`` with ``head_major``) of ``hq`` / ``hkv`` heads, the q / k
+    gains (FP32 ``[128]``), rotary tables (FP32 ``[tokens, 64]``, row = token
+    position), ``tokens`` positions per sample."""
+
+    def __init__(self, q, k, v, q_weight, k_weight, cos, sin, eps, hq, hkv, tokens, batch, n_out, n_out_kv,
+                 head_major=False):  # fmt: skip
+        _require_fp32(q_weight=q_weight, cos=cos, sin=sin)
+        _require(q_weight.numel() == HEAD_DIM and (k_weight is None or k_weight.numel() == HEAD_DIM),
+                 "heads epilogue gains must have 128 entries")  # fmt: skip
+        _require(cos.shape == sin.shape and cos.shape[-1] == HEAD_DIM // 2 and cos.shape[0] >= tokens,
+                 "heads epilogue rotary tables must cover the token positions")  # fmt: skip
+        _require(all(t is None or t.dtype == torch.bfloat16 for t in (q, k, v)), "heads epilogue writes bf16")
+        _require(q.numel() >= batch * hq * n_out * HEAD_DIM
+                 and (hkv == 0 or min(k.numel(), v.numel()) >= batch * hkv * n_out_kv * HEAD_DIM),
+                 "heads epilogue outputs are too small")  # fmt: skip
+        _require_cuda(*(t for t in (q, k, v, q_weight, k_weight, cos, sin) if t is not None))
+        self._tensors = (q, k, v, q_weight, k_weight, cos, sin)
+        self.struct = _lib.HeadsEpilogue(
+            q.data_ptr(), _ptr(k), _ptr(v), q_weight.data_ptr(), _ptr(k_weight), cos.data_ptr(), sin.data_ptr(),
+            float(eps), int(bool(head_major)), hq, hkv, tokens, batch, n_out, n_out_kv,
+        )  # fmt: skip
 
 
 def gemm_grouped(problems: list, stream: int) -> None:

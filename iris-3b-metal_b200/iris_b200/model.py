@@ -18,8 +18,8 @@ Per step (``dit.py:283-375`` restructured):
 * every branch input is written by the kernel that finishes the previous
   residual update (gated post-norm + residual + next RMSNorm-modulate fused);
 * GEMMs on the tensor cores with fused epilogues (bias, SwiGLU, sigmoid gate),
-  attention by the tcgen05 flash kernel; Q/K/V written by one fused
-  norm + RoPE + head-transpose kernel;
+  attention by the tcgen05 flash kernel; the Q/K/V GEMM's epilogue applies
+  the QK-norm and RoPE and writes the head layout directly;
 * pixel stage: per-pixel adaLN GEMM, compress / attention / expand on the
   tensor cores, the post-modulated per-pixel MLP fused, and the last block
   fused with the FinalLayer and the fold into the velocity image.
@@ -332,7 +332,6 @@ class CudaIris:
         hq, hkv = cfg.num_heads, cfg.kv_heads
         pix = cfg.pixel
         bf16 = torch.bfloat16
-        wq = (hq + 2 * hkv) * HEAD_DIM
         e = lambda *shape, dtype=bf16: torch.empty(*shape, device=dev, dtype=dtype)  # noqa: E731
         ws = {
             "tokens": e(batch * n, d, dtype=torch.float32),
@@ -340,7 +339,6 @@ class CudaIris:
             "h": e(batch * n, d),  # dual-stream branch inputs (text rows, then image rows)
             "hj": e(batch * n, d),  # single-stream branch inputs ([text | image] per sample)
             "h2": e(batch * n, d),
-            "qkv": e(batch * n, wq),
             # [B, H, n, 128]; head-major [H, B, n, 128] under sequence parallelism
             "q": e(batch, hq, n, HEAD_DIM),
             "k": e(batch, hkv, n, HEAD_DIM),
@@ -354,7 +352,6 @@ class CudaIris:
             "ph": e(batch * L_loc, pp * pix.hidden_size),
             "pmods": e(batch * L_loc, pp * 4 * pix.hidden_size),
             "comp": e(batch * L_loc, pix.attn_hidden_size),
-            "pqkv": e(batch * L_loc, 3 * pix.attn_hidden_size),
             "pq": e(batch, pix.num_heads, L_loc, HEAD_DIM),
             "pk": e(batch, pix.num_heads, shard.L, HEAD_DIM),
             "pv": e(batch, pix.num_heads, shard.L, HEAD_DIM),
@@ -528,14 +525,16 @@ class CudaIris:
                 problems.append(K.gemm_problem(a[off : off + rows], w, ws[out_key][off : off + rows], **extra))
             K.gemm_grouped(problems, st)
 
-        grouped(None, block.qkv, "qkv")
-        for s, rows, rpb, tmap, off in segs:
+        # Q/K/V projection with QK-norm + RoPE + the head layout in its epilogue
+        problems = []
+        for s, rows, _, tmap, off in order:
             qn, kn = block.qk_norm[s]
-            _lib.call(
-                "iris_qkv_heads", ws["qkv"][off:].data_ptr(), g.batch, rpb, block.qkv[s].shape[0], cfg.num_heads,
-                cfg.kv_heads, qn.data_ptr(), kn.data_ptr(), cos.data_ptr(), sin.data_ptr(), eps, ws["q"].data_ptr(),
-                ws["k"].data_ptr(), ws["v"].data_ptr(), g.N, g.N, tmap[2], int(self.comm is not None), st,
+            heads = K.HeadsOut(
+                ws["q"], ws["k"], ws["v"], qn, kn, cos, sin, eps, cfg.num_heads, cfg.kv_heads, g.N, g.batch, g.N, g.N,
+                head_major=self.comm is not None,
             )  # fmt: skip
+            problems.append(K.gemm_problem(h[off : off + rows], block.qkv[s], None, out_rows=tmap, heads=heads))
+        K.gemm_grouped(problems, st)
         if self.comm is None:
             grouped(None, block.gate, "glog")  # gate logits; sigmoid in the attention epilogue
             split = g.T if block.dual else 0
@@ -644,14 +643,13 @@ class CudaIris:
                 capture[f"pixel_block{i - 1}"] = ws["pixels"].float().view(g.batch * g.L, -1, pix.hidden_size).clone()
             K.gemm(ws["s_cond"], blk["adaln"][0], ws["pmods"], bias=blk["adaln"][1])
             K.gemm(ws["ph"], blk["compress"][0], ws["comp"], bias=blk["compress"][1])
-            K.gemm(ws["comp"], blk["qkv"], ws["pqkv"])
             qn, kn = blk["qk_norm"]
             kv = ("pk_s", "pv_s") if sp else ("pk", "pv")
-            _lib.call(
-                "iris_qkv_heads", ws["pqkv"].data_ptr(), g.batch, g.L, 3 * pix.attn_hidden_size, heads, heads,
-                qn.data_ptr(), kn.data_ptr(), pcos.data_ptr(), psin.data_ptr(), eps, ws["pq"].data_ptr(),
-                ws[kv[0]].data_ptr(), ws[kv[1]].data_ptr(), g.L, ws[kv[0]].shape[2], 0, 0, st,
+            targets = K.HeadsOut(
+                ws["pq"], ws[kv[0]], ws[kv[1]], qn, kn, pcos, psin, eps, heads, heads, g.L, g.batch, g.L,
+                ws[kv[0]].shape[2],
             )  # fmt: skip
+            K.gemm_grouped([K.gemm_problem(ws["comp"], blk["qkv"], None, heads=targets)], st)
             if sp:  # local queries over the keys / values of every patch token
                 for name in ("pk", "pv"):
                     gather_image_tokens(self.comm, K.block_copy, g.shard, ws[name + "_s"], ws[name + "_g"], ws[name],

@@ -277,6 +277,42 @@ def test_gemm_pair_kernel_epilogues_and_row_maps(K):
     assert torch.all(act[:, F_:] == 0)
 
 
+@pytest.mark.parametrize("M,hq,hkv,head_major", [(90, 2, 1, False), (300, 3, 1, False), (600, 4, 2, True)])
+def test_gemm_heads_epilogue_matches_projection_then_qk_norm_rope(K, M, hq, hkv, head_major):
+    """EPI_HEADS (one-SM and CTA-pair kernels; odd slot counts; a row map that
+    puts the rows after T text positions) against the fp32 projection followed
+    by the oracle's qk_norm_rope and the V copy."""
+    T, B = 5, 2
+    L = M // B
+    tokens = T + L
+    Kd = 256
+    gen = torch.Generator(device="cuda").manual_seed(M + hq)
+    a = torch.randn(M, Kd, device="cuda", generator=gen).to(torch.bfloat16)
+    w = (torch.randn((hq + 2 * hkv) * 128, Kd, device="cuda", generator=gen) * 0.1).to(torch.bfloat16)
+    qw, kw = (torch.rand(128, device="cuda", generator=gen) + 0.5 for _ in range(2))
+    cos, sin = (torch.randn(tokens, 64, device="cuda", generator=gen) for _ in range(2))
+    shape_q = (hq, B, tokens, 128) if head_major else (B, hq, tokens, 128)
+    shape_kv = (hkv, B, tokens, 128) if head_major else (B, hkv, tokens, 128)
+    q = torch.zeros(*shape_q, device="cuda", dtype=torch.bfloat16)
+    k, v = (torch.zeros(*shape_kv, device="cuda", dtype=torch.bfloat16) for _ in range(2))
+    heads = K.HeadsOut(q, k, v, qw, kw, cos, sin, 1e-6, hq, hkv, tokens, B, tokens, tokens, head_major=head_major)
+    K.gemm_grouped([K.gemm_problem(a, w, None, out_rows=(L, tokens, T), heads=heads)],
+                   torch.cuda.current_stream().cuda_stream)  # fmt: skip
+    proj = (a.float() @ w.float().T).view(B, L, hq + 2 * hkv, 128).cpu()
+    c, s_ = cos[T:].cpu(), sin[T:].cpu()
+    if head_major:
+        q, k, v = (t.transpose(0, 1) for t in (q, k, v))
+    got_q, got_k, got_v = (t[:, :, T:].float().cpu() for t in (q, k, v))
+    for h in range(hq):
+        ref = ops.qk_norm_rope_reference(proj[:, :, h].reshape(B, L, 128), qw.cpu(), c, s_, 1e-6)[:, 0]
+        assert rel_err(got_q[:, h], ref) < 1e-2
+    for h in range(hkv):
+        ref = ops.qk_norm_rope_reference(proj[:, :, hq + h].reshape(B, L, 128), kw.cpu(), c, s_, 1e-6)[:, 0]
+        assert rel_err(got_k[:, h], ref) < 1e-2
+        assert rel_err(got_v[:, h], proj[:, :, hq + hkv + h]) < 1e-2
+    assert torch.all(q[:, :, :T] == 0) and torch.all(k[:, :, :T] == 0)
+
+
 # -------------------------------------------------------------------- attention
 def test_flash_attention_split_gate_writes_each_stream_densely(K):
     B, H, T, N = 2, 2, 16, 52
