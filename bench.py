@@ -256,8 +256,10 @@ def fused_ops(args) -> None:
     projections bf16 [2, 4352, 3072] (24 heads, the 1024^2 RoPE table). Before
     each timed call a 512 MB write evicts L2 (the operands fit in it) and a
     256 MB read then replaces its dirty lines with clean ones, so the timed call
-    pays for no write-back of the flush. Each call is bracketed by CUDA events
-    on its stream; the median over the calls is reported."""
+    pays for no write-back of the flush; a ~100 us device sleep then keeps the
+    GPU busy while the host enqueues the call. Each call is bracketed by CUDA events
+    on its stream; the mean over the calls is reported (the event clock ticks in
+    2.048 us steps, so a median would snap to a tick)."""
     from iris_b200 import kernels as K
     from iris_b200.tables import cos_sin, rope_1d, rope_2d
 
@@ -276,27 +278,34 @@ def fused_ops(args) -> None:
     clean = torch.ones(64 * 2**20, dtype=torch.float32, device=device)
 
     def timed(fn, reps):
-        for _ in range(3):
+        # warm until the clocks have ramped: about 0.3 s of flushes and calls
+        t_end = time.perf_counter() + 0.3
+        while time.perf_counter() < t_end:
+            flush.fill_(1)
             fn()
+            torch.cuda.synchronize()
         times = []
         for _ in range(reps):
             flush.fill_(1)  # evicts L2 and keeps the GPU busy while the events and the call are enqueued
             clean.sum()  # clean lines replace the flush's dirty ones
+            torch.cuda._sleep(200_000)  # ~100 us of queued device time: the host's launch latency stays outside the events
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record()
             fn()
             e.record()
             times.append((s, e))
         torch.cuda.synchronize()
-        return statistics.median(a.elapsed_time(b) for a, b in times)
+        # CUDA events tick in 2.048 us steps on these boxes: the median snaps to
+        # a tick, the mean over many calls (random start phase) does not.
+        return statistics.mean(a.elapsed_time(b) for a, b in times)
 
-    norm_ms = timed(lambda: K.rms_norm_modulate(x, w, shift, scale, 1e-6, torch.bfloat16), max(args.steps, 20))
+    norm_ms = timed(lambda: K.rms_norm_modulate(x, w, shift, scale, 1e-6, torch.bfloat16), max(args.steps, 100))
 
     def qk():
         K.qk_norm_rope(q, qw, cos, sin, 1e-6, 24, out=qo)
         K.qk_norm_rope(k, kw, cos, sin, 1e-6, 24, out=ko)
 
-    qk_ms = timed(qk, max(args.steps, 20))
+    qk_ms = timed(qk, max(args.steps, 100))
     pk = peaks()
     norm_bytes = 2 * (2 * 4096 * 3072 * 2) + 3072 * 4 + 2 * 2 * 3072 * 4
     qk_bytes = 4 * (2 * 4352 * 24 * 128 * 2) + 2 * 4352 * 64 * 4 + 2 * 128 * 4
@@ -306,8 +315,8 @@ def fused_ops(args) -> None:
         "value": min(norm_gbs, qk_gbs),
         "unit": "GB/s",
         "n_gpus": 1,
-        "steps": max(args.steps, 20),
-        "warmup": 3,
+        "steps": max(args.steps, 100),
+        "warmup": "0.3 s of flush + call per op, until the clocks ramp",
         "higher_is_better": True,
         "dtype": "bf16",
         "data": "synthetic",
