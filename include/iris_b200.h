@@ -273,6 +273,17 @@ int iris_add_bias_rows(const float* core, const float* bias, float* out, int64_t
 int iris_cfg_euler(const float* v, const float* x, float* x_out, int64_t images, int64_t per_image, float cfg_scale,
                    float sigma, float sigma_next, int guided, void* stream);
 
+/* One multistep DPM-Solver++ step of FlowDPMSolver (src/iris3b/flow/solver.py:58-109,
+ * _model_out + _pred_x0 + _first_order / _second_order): with guided != 0, v holds
+ * [uncond; cond] (2 * images rows) and out = v_u + cfg_scale (v_c - v_u), else out = v;
+ * x0 = out (predict_x != 0) or x - sigma out; x_out = a x + b x0 + c (x0 - x0_prev),
+ * x0 also written to x0_out. First order: a = t / s, b = -(1 - t) expm1(-h), c = 0
+ * (x0_prev may be null); second order: a = t / s0, b = -(1 - t) expm1(-h),
+ * c = -(1 - t) expm1(-h) / (2 r0). All fp32, [images, per_image] contiguous. */
+int iris_dpm_update(const float* v, const float* x, const float* x0_prev, float* x0_out, float* x_out, int64_t images,
+                    int64_t per_image, float cfg_scale, int guided, float sigma, int predict_x, float a, float b,
+                    float c, void* stream);
+
 /* require_finite, src/iris_metal/model.py:102-110: *flag (device int) = 1 if
  * every x[i] is finite, else 0. */
 int iris_all_finite(const float* x, int64_t n, int* flag, void* stream);

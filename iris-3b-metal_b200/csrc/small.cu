@@ -6,6 +6,8 @@
 //   gemv                     small-M linear (conditioning MLP, shared adaLN cores)
 //   add_bias_rows            SharedCoreBias, src/iris3b/nn/modulation.py:284-285
 //   cfg_euler                CFG combine + flow-Euler step, solver.py:72-74, sampling.py:129-135
+//   dpm_update               CFG combine + x0 prediction + DPM-Solver++ (1st/2nd order) step,
+//                            src/iris3b/flow/solver.py:58-109
 //   all_finite               require_finite, src/iris_metal/model.py:102-110
 #include "common.cuh"
 #include "iris_abi_internal.h"
@@ -164,6 +166,33 @@ __global__ void cfg_euler_kernel(const float* __restrict__ v, const float* __res
   }
 }
 
+// One multistep DPM-Solver++ step on the rectified-flow schedule
+// (src/iris3b/flow/solver.py:58-109): out = v_u + g (v_c - v_u) (guided) or v;
+// x0 = out (x-prediction) or x - s out (v-prediction);
+// x_out = a x + b x0 + c (x0 - x0_prev) (c = 0: first order, x0_prev unused).
+// x0 is written to x0_out for the next step's history.
+__global__ void dpm_update_kernel(const float* __restrict__ v, const float* __restrict__ x,
+                                  const float* __restrict__ x0_prev, float* __restrict__ x0_out,
+                                  float* __restrict__ x_out, int64_t total, float cfg_scale, int guided,
+                                  float sigma, int predict_x, float a, float b, float c) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float out;
+    if (guided) {
+      const float u = v[i], w = v[total + i];
+      out = u + cfg_scale * (w - u);
+    } else {
+      out = v[i];
+    }
+    const float xi = x[i];
+    const float x0 = predict_x ? out : xi - sigma * out;
+    float xn = a * xi + b * x0;
+    if (x0_prev != nullptr) xn += c * (x0 - x0_prev[i]);
+    x0_out[i] = x0;
+    x_out[i] = xn;
+  }
+}
+
 __global__ void all_finite_kernel(const float* __restrict__ x, int64_t n, int* flag) {
   int bad = 0;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
@@ -299,6 +328,21 @@ extern "C" int iris_cfg_euler(const float* v, const float* x, float* x_out, int6
   if (total <= 0) return IRIS_OK;
   cfg_euler_kernel<<<grid_for(total, 4), THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
       v, x, x_out, images, per_image, cfg_scale, sigma, sigma_next, guided);
+  IRIS_CUDA(cudaGetLastError());
+  return IRIS_OK;
+}
+
+extern "C" int iris_dpm_update(const float* v, const float* x, const float* x0_prev, float* x0_out, float* x_out,
+                               int64_t images, int64_t per_image, float cfg_scale, int guided, float sigma,
+                               int predict_x, float a, float b, float c, void* stream) {
+  using namespace iris::small;
+  IRIS_REQUIRE(v && x && x0_out && x_out, "dpm_update: null pointer");
+  IRIS_REQUIRE(images >= 0 && per_image >= 0, "dpm_update: negative size");
+  IRIS_REQUIRE(c == 0.f || x0_prev != nullptr, "dpm_update: a second-order step needs the previous x0");
+  const int64_t total = images * per_image;
+  if (total == 0) return IRIS_OK;
+  dpm_update_kernel<<<grid_for(total, 4), THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
+      v, x, c == 0.f ? nullptr : x0_prev, x0_out, x_out, total, cfg_scale, guided, sigma, predict_x, a, b, c);
   IRIS_CUDA(cudaGetLastError());
   return IRIS_OK;
 }

@@ -42,6 +42,7 @@ SIGNATURES: dict[str, list] = {
     "iris_gemv": [P, I64, I64, P, I32, P, P, I64, I32, I32, P],
     "iris_add_bias_rows": [P, P, P, I64, I64, I64, P],
     "iris_cfg_euler": [P, P, P, I64, I64, F, F, F, I32, P],
+    "iris_dpm_update": [P, P, P, P, P, I64, I64, F, I32, F, I32, F, F, F, P],
     "iris_all_finite": [P, I64, P, P],
 }
 

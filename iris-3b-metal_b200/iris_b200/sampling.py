@@ -6,7 +6,10 @@
   on the doubled batch ``[uncond; cond]``. The combine and the Euler update are
   one fused kernel per step (``iris_cfg_euler``).
 * :class:`FlowDPMSolver`: ``src/iris3b/flow/solver.py:36-141`` with the same
-  API; it drives any ``model_fn`` (e.g. :class:`iris_b200.model.CudaIris`).
+  API; it drives any ``model_fn`` (e.g. :class:`iris_b200.model.CudaIris`) on
+  CUDA tensors. The CFG combine, the x0 prediction and the first- or
+  second-order update of each step are one fused kernel (``iris_dpm_update``),
+  whose coefficients come from the host in double precision.
 """
 
 from __future__ import annotations
@@ -100,25 +103,21 @@ class FlowDPMSolver:
         self.reuse_cfg_text = reuse_cfg_text
         self._cfg_text: torch.Tensor | None = None
 
-    def _model_out(self, x, t: float, cond, uncond):
+    def _model_call(self, x, t: float, cond, uncond) -> tuple[torch.Tensor, bool]:
+        """The model output for ``x`` at ``t``: ``[uncond; cond]`` rows (and True)
+        when CFG applies at ``t`` (``solver.py:58-74``), else the plain rows."""
         lo, hi = self.cfg_interval
         use_cfg = uncond is not None and self.cfg_scale != 1.0 and lo < t < hi
         rows = 2 * x.shape[0] if use_cfg else x.shape[0]
         t_model = torch.full((rows,), t * self.num_timesteps, device=x.device, dtype=torch.float32)
         if not use_cfg:
-            return self.model_fn(x, t_model, cond)
+            return self.model_fn(x, t_model, cond), False
         text = self._cfg_text
         if text is None:
             text = torch.cat([uncond, cond], dim=0)
             if self.reuse_cfg_text:
                 self._cfg_text = text
-        out = self.model_fn(torch.cat([x, x], dim=0), t_model, text)
-        out_uncond, out_cond = out.chunk(2, dim=0)
-        return out_uncond + self.cfg_scale * (out_cond - out_uncond)
-
-    def _pred_x0(self, x, t: float, cond, uncond):
-        out = self._model_out(x, t, cond, uncond)
-        return out if self.prediction == "x" else x - t * out
+        return self.model_fn(torch.cat([x, x], dim=0), t_model, text), True
 
     @staticmethod
     def time_grid(steps: int, shift: float) -> list[float]:
@@ -126,32 +125,43 @@ class FlowDPMSolver:
         return shift_sigma(sigma, shift).flip(0).tolist()
 
     @staticmethod
-    def _first_order(x, s: float, t: float, x0):
-        phi1 = math.expm1(-(_lambda(t) - _lambda(s)))
-        return (t / s) * x - (1.0 - t) * phi1 * x0
-
-    @staticmethod
-    def _second_order(x, prev1, prev0, t: float):
-        (s1, x0_1), (s0, x0_0) = prev1, prev0
-        lam_t, lam_0, lam_1 = _lambda(t), _lambda(s0), _lambda(s1)
+    def coefficients(s: float, t: float, prev_s: float | None) -> tuple[float, float, float]:
+        """``(a, b, c)`` of ``x_next = a x + b x0 + c (x0 - x0_prev)``: the first-order
+        update (``prev_s`` None, ``solver.py:84-88``) or the second-order one with
+        the previous step at ``prev_s`` (``solver.py:90-109``), in double precision."""
+        if prev_s is None:
+            phi1 = math.expm1(-(_lambda(t) - _lambda(s)))
+            return t / s, -(1.0 - t) * phi1, 0.0
+        lam_t, lam_0, lam_1 = _lambda(t), _lambda(s), _lambda(prev_s)
         h, h0 = lam_t - lam_0, lam_0 - lam_1
-        d = (x0_0 - x0_1) / (h0 / h)
         phi1 = math.expm1(-h)
-        return (t / s0) * x - (1.0 - t) * phi1 * x0_0 - 0.5 * (1.0 - t) * phi1 * d
+        return t / s, -(1.0 - t) * phi1, -0.5 * (1.0 - t) * phi1 / (h0 / h)
 
     @torch.no_grad()
     def sample(self, z, cond, uncond=None, steps: int = 50, order: int = 2, shift: float = 1.0):
+        """Integrate from noise ``z`` (CUDA, fp32 ``[k, ...]``) to a sample; the
+        order ramps up over the first steps and back down at the end, so the
+        last (t = 0) update is the first-order x <- x0 projection."""
+        if not z.is_cuda:
+            raise ValueError("FlowDPMSolver.sample runs on CUDA tensors")
         grid = self.time_grid(steps, shift)
-        x = z
+        x = z.to(torch.float32).contiguous()
         self._cfg_text = None
-        history: list = []
+        images, per_image = x.shape[0], x[0].numel()
+        x0_prev, s_prev = None, None
         for i in range(1, steps + 1):
             s, t = grid[i - 1], grid[i]
-            x0 = self._pred_x0(x, s, cond, uncond)
-            history.append((s, x0))
+            out, guided = self._model_call(x, s, cond, uncond)
             step_order = min(i, order, steps + 1 - i)
-            x = self._first_order(x, s, t, x0) if step_order == 1 else self._second_order(x, history[-2], history[-1], t)
-            if len(history) > 2:
-                history.pop(0)
+            a, b, c = self.coefficients(s, t, s_prev if step_order == 2 else None)
+            x0 = torch.empty_like(x)
+            x_next = torch.empty_like(x)
+            _lib.call(
+                "iris_dpm_update", out.contiguous().data_ptr(), x.data_ptr(),
+                x0_prev.data_ptr() if (c != 0.0 and x0_prev is not None) else None, x0.data_ptr(),
+                x_next.data_ptr(), images, per_image, float(self.cfg_scale), int(guided), float(s),
+                int(self.prediction == "x"), float(a), float(b), float(c), stream_of(x),
+            )  # fmt: skip
+            x, x0_prev, s_prev = x_next, x0, s
         self._cfg_text = None
         return x

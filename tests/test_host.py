@@ -79,21 +79,33 @@ def test_pack_swiglu_layout():
     assert torch.all(w13[2 * 256 + 44 : 2 * 256 + 128] == 0) and torch.all(w2p[:, ffn:] == 0)
 
 
-def test_flow_dpm_solver_matches_reference():
+def test_dpm_coefficients_match_oracle_updates():
+    """The fused DPM-Solver++ step computes x_next = a x + b x0 + c (x0 - x0_prev);
+    its host-side (a, b, c) reproduce the oracle's first- and second-order
+    updates (solver.py:84-109) on every step of the golden grids."""
     from iris_b200.sampling import FlowDPMSolver
 
+    from oracle.sampler import FlowDPMSolverOracle
+
     fx = golden("samplers")
-    z, cond, uncond = fx["inputs"]["z"], fx["inputs"]["cond"], fx["inputs"]["uncond"]
-
-    def model_fn(x, t, text):
-        return 0.3 * x + 0.05 * text + 1e-4 * t[:, None, None, None]
-
+    g = torch.Generator().manual_seed(0)
+    x, x0, x0p = (torch.randn(64, generator=g, dtype=torch.float64) for _ in range(3))
     for key, case in fx.items():
-        if key.startswith("dpm_"):
-            solver = FlowDPMSolver(model_fn, cfg_scale=case["cfg_scale"])
-            assert solver.time_grid(case["steps"], case["shift"]) == case["grid"]
-            out = solver.sample(z, cond, uncond, steps=case["steps"], order=case["order"], shift=case["shift"])
-            torch.testing.assert_close(out, case["sample"], rtol=1e-6, atol=1e-6)
+        if not key.startswith("dpm_"):
+            continue
+        grid = FlowDPMSolver.time_grid(case["steps"], case["shift"])
+        assert grid == case["grid"]
+        steps, order = case["steps"], case["order"]
+        for i in range(1, steps + 1):
+            s, t = grid[i - 1], grid[i]
+            second = min(i, order, steps + 1 - i) == 2
+            a, b, c = FlowDPMSolver.coefficients(s, t, grid[i - 2] if second else None)
+            fused = a * x + b * x0 + c * (x0 - x0p)
+            if second:
+                expect = FlowDPMSolverOracle.second_order(x, (grid[i - 2], x0p), (s, x0), t)
+            else:
+                expect = FlowDPMSolverOracle.first_order(x, s, t, x0)
+            torch.testing.assert_close(fused, expect, rtol=1e-12, atol=1e-12)
 
 
 def test_dp_shards_cover_every_image_once():
