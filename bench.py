@@ -278,23 +278,20 @@ def fused_ops(args) -> None:
     clean = torch.ones(64 * 2**20, dtype=torch.float32, device=device)
 
     def timed(fn, reps):
-        # warm until the clocks have ramped: about 0.3 s of flushes and calls
-        t_end = time.perf_counter() + 0.3
-        while time.perf_counter() < t_end:
-            flush.fill_(1)
-            fn()
+        # the first pass (same calls, discarded) warms the clocks under the same
+        # back-to-back load as the measured one
+        for _pass in range(2):
+            times = []
+            for _ in range(reps):
+                flush.fill_(1)  # evicts L2 and keeps the GPU busy while the events and the call are enqueued
+                clean.sum()  # clean lines replace the flush's dirty ones
+                torch.cuda._sleep(200_000)  # ~100 us of queued device time: host launch latency stays outside the events
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record()
+                fn()
+                e.record()
+                times.append((s, e))
             torch.cuda.synchronize()
-        times = []
-        for _ in range(reps):
-            flush.fill_(1)  # evicts L2 and keeps the GPU busy while the events and the call are enqueued
-            clean.sum()  # clean lines replace the flush's dirty ones
-            torch.cuda._sleep(200_000)  # ~100 us of queued device time: the host's launch latency stays outside the events
-            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s.record()
-            fn()
-            e.record()
-            times.append((s, e))
-        torch.cuda.synchronize()
         # CUDA events tick in 2.048 us steps on these boxes: the median snaps to
         # a tick, the mean over many calls (random start phase) does not.
         return statistics.mean(a.elapsed_time(b) for a, b in times)
@@ -316,7 +313,7 @@ def fused_ops(args) -> None:
         "unit": "GB/s",
         "n_gpus": 1,
         "steps": max(args.steps, 100),
-        "warmup": "0.3 s of flush + call per op, until the clocks ramp",
+        "warmup": "one discarded pass of the same calls per op",
         "higher_is_better": True,
         "dtype": "bf16",
         "data": "synthetic",

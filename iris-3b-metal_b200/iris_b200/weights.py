@@ -9,11 +9,12 @@ or synthesises random weights for benchmarking.
 
 from __future__ import annotations
 
+from dataclasses import fields, replace
 from pathlib import Path
 
 import torch
 
-from iris_b200.config import ModelConfig, from_any
+from iris_b200.config import ModelConfig, PixelStageConfig, from_any
 
 
 class IrisWeights:
@@ -26,6 +27,9 @@ class IrisWeights:
 
     @classmethod
     def from_safetensors(cls, path: str | Path, cfg, device: torch.device | str = "cuda") -> "IrisWeights":
+        """Every tensor of a ``model.safetensors`` file, moved to ``device`` one at a
+        time (the engine repacks the matrices to BF16 once; gains, biases and
+        tables stay as stored)."""
         from safetensors import safe_open
 
         state = {}
@@ -33,6 +37,30 @@ class IrisWeights:
             for key in reader.keys():
                 state[key] = reader.get_tensor(key).to(device)
         return cls(cfg, state)
+
+    @classmethod
+    def from_checkpoint(cls, checkpoint: str | Path, device: torch.device | str = "cuda") -> "IrisWeights":
+        """A released checkpoint directory: ``config.yaml`` (its ``model`` section)
+        and ``model.safetensors``, the layout ``load_config`` + ``load_dit`` read
+        (``src/iris_metal/loading.py:15-17,67-77``)."""
+        root = Path(checkpoint)
+        return cls.from_safetensors(root / "model.safetensors", load_model_config(root / "config.yaml"), device)
+
+
+def load_model_config(path: str | Path) -> ModelConfig:
+    """The ``model`` section of a checkpoint's ``config.yaml`` over the defaults;
+    keys the schema does not define are dropped, as ``inference_config`` does
+    (``src/iris3b/config.py:539-568``)."""
+    import yaml
+
+    with open(path) as f:
+        raw = yaml.safe_load(f) or {}
+    model = dict(raw.get("model") or {})
+    known = {f.name for f in fields(ModelConfig)}
+    pixel_known = {f.name for f in fields(PixelStageConfig)}
+    pixel = {k: v for k, v in dict(model.pop("pixel", None) or {}).items() if k in pixel_known}
+    values = {k: v for k, v in model.items() if k in known}
+    return replace(ModelConfig(), **values, pixel=replace(PixelStageConfig(), **pixel))
 
 
 def synthetic_state(cfg: ModelConfig, device, seed: int = 0, std: float = 0.02, dtype=torch.bfloat16) -> dict:

@@ -70,6 +70,18 @@ def test_forward_matches_reference(iris, name):
     assert psnr(v, fx["v"]) > PSNR_MIN
 
 
+def test_checkpoint_directory_forward_matches_reference(iris, tmp_path):
+    """config.yaml + model.safetensors loaded by IrisWeights.from_checkpoint
+    (the directory layout of load_config / load_dit) give the reference output."""
+    from test_host import _write_checkpoint
+
+    fx = golden("released_mha")
+    _write_checkpoint(tmp_path, fx)
+    engine = iris.CudaIris(iris.IrisWeights.from_checkpoint(tmp_path, device="cuda"))
+    v = engine(fx["x"].cuda(), fx["t"].cuda(), fx["prepared_text"].cuda())
+    assert rel_err(v, fx["v"]) < REL_TOL
+
+
 def test_encode_text_matches_reference(iris):
     fx = golden("released_mha")
     cfg = _config(fx["config"])

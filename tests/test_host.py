@@ -118,3 +118,38 @@ def test_dp_shards_cover_every_image_once():
                 lo, hi = image_shard(images, rank, world)
                 seen.extend(range(lo, hi))
             assert seen == list(range(images))
+
+
+def _write_checkpoint(root, fx):
+    """A released-style checkpoint directory: config.yaml (a training config with
+    sections and keys the loader must drop) and model.safetensors (fp32)."""
+    import yaml
+    from safetensors.torch import save_file
+
+    from oracle.config import OracleConfig, PixelConfig
+    from oracle.params import seeded_init
+
+    d = dict(fx["config"])
+    cfg = OracleConfig(**{**d, "pixel": PixelConfig(**d["pixel"])})
+    params = seeded_init(cfg, seed=0)
+    model = {**d, "pixel": {**d["pixel"], "legacy_field": 1}, "unknown_model_key": "x"}
+    (root / "config.yaml").write_text(yaml.safe_dump({"model": model, "train": {"lr": 1e-4}, "flow": {}}))
+    save_file({k: v.contiguous() for k, v in params.items()}, str(root / "model.safetensors"))
+    return d, params
+
+
+def test_checkpoint_directory_loads_config_and_weights(tmp_path):
+    from iris_b200 import IrisWeights
+
+    fx = golden("released_mha")
+    d, params = _write_checkpoint(tmp_path, fx)
+    w = IrisWeights.from_checkpoint(tmp_path, device="cpu")
+    for key, value in d.items():
+        if key != "pixel":
+            assert getattr(w.cfg, key) == value, key
+    for key, value in d["pixel"].items():
+        assert getattr(w.cfg.pixel, key) == value, key
+    state = w.state_dict()
+    assert set(state) == set(params)
+    for key, value in params.items():
+        assert torch.equal(state[key], value), key
