@@ -44,6 +44,15 @@ extern "C" {
 #define IRIS_EPI_GATE 2   /* out = aux * sigmoid(acc)                  */
 #define IRIS_EPI_HEADS 3  /* [q | k | v] heads -> normed, rotated head layouts (see iris_heads_epilogue) */
 
+/* Sequence parallelism over processes (peer memory) */
+#define IRIS_MAX_PEERS 8        /* ranks one call may span */
+#define IRIS_IPC_HANDLE_BYTES 64 /* bytes of an exported buffer handle */
+
+/* IRIS_EPI_HEADS destinations (iris_heads_epilogue.peer_mode) */
+#define IRIS_HEADS_LOCAL 0          /* q_out / k_out / v_out of this process */
+#define IRIS_HEADS_PEER_SCATTER 1   /* head h -> rank h / (heads / world): its [b, h % (heads / world), token_offset + t] */
+#define IRIS_HEADS_PEER_BROADCAST_KV 2 /* q local as with IRIS_HEADS_LOCAL; k and v -> every rank's [b, h, token_offset + t] */
+
 /* Residual-kernel follow-ups (iris_gated_residual_rms_norm next_mode) */
 #define IRIS_NEXT_NONE 0
 #define IRIS_NEXT_NORM_MODULATE 1 /* next_out = rms_norm(res) * w * (1 + scale[b]) + shift[b] */
@@ -139,6 +148,16 @@ typedef struct iris_heads_epilogue {
   int64_t heads_q, heads_kv;
   int64_t tokens, batch;
   int64_t n_out, n_out_kv;
+  /* Sequence parallelism (IRIS_HEADS_PEER_*; IRIS_HEADS_LOCAL ignores the rest):
+   * the rows are this rank's tokens, written to the ranks' buffers through
+   * q_peer / k_peer / v_peer[j] (pointers valid in this process, e.g. from
+   * iris_ipc_import) at position token_offset + t of n_dest per (b, h). */
+  int peer_mode;
+  int world;
+  int64_t token_offset, n_dest;
+  void* q_peer[IRIS_MAX_PEERS];
+  void* k_peer[IRIS_MAX_PEERS];
+  void* v_peer[IRIS_MAX_PEERS];
 } iris_heads_epilogue;
 
 /* One problem of a grouped launch: the arguments of iris_gemm_bf16 as plain
@@ -186,6 +205,36 @@ int iris_flash_attn_fwd_split(const void* q, const void* k, const void* v, int64
                               int64_t heads_kv, int64_t n, int64_t n_kv, int64_t head_dim, float scale, int64_t split,
                               void* o_text, void* o_image, const void* gate_text, const void* gate_image,
                               int64_t row_stride, void* stream);
+
+/* Sequence-parallel attention (no reference counterpart: the reference runs
+ * on one device): this rank's heads_q heads over all n = world *
+ * tokens_per_rank query positions; each output row goes straight to the rank
+ * that owns its token, o_peers[j] (pointers valid in this process), row
+ * b * tokens_per_rank + i % tokens_per_rank, columns col0 + h * 128 ... of
+ * row_stride bf16. The all-to-all of the attention output, done by the
+ * epilogue's stores. */
+int iris_flash_attn_fwd_peers(const void* q, const void* k, const void* v, int64_t batch, int64_t heads_q,
+                              int64_t heads_kv, int64_t n, int64_t n_kv, int64_t head_dim, float scale,
+                              void* const* o_peers, int world, int64_t tokens_per_rank, int64_t col0,
+                              int64_t row_stride, void* stream);
+
+/* ---- peer memory (sequence parallelism across processes) ---------------- */
+/* No reference counterpart. iris_ipc_export: the IPC handle (IRIS_IPC_HANDLE_BYTES)
+ * of the allocation holding device pointer ptr and ptr's offset in it;
+ * iris_ipc_import maps another process's handle (base of the allocation; add
+ * the offset), iris_ipc_close unmaps it. */
+int iris_ipc_export(const void* ptr, void* handle, int64_t* offset);
+int iris_ipc_import(const void* handle, void** base);
+int iris_ipc_close(void* base);
+
+/* Barrier of the ranks of one sequence-parallel call: writes epoch into slot
+ * `rank` of every peer's flags (peer_flags[j], mapped into this process), then
+ * waits until every peer j has written at least epoch into flags[j]. Work
+ * enqueued on `stream` before the barrier (e.g. epilogue stores into peer
+ * buffers) is visible to the peers after theirs returns. A wait longer than
+ * timeout_ns gives up and sets bit 0 of the device error word. */
+int iris_peer_barrier(unsigned int* flags, void* const* peer_flags, int rank, int world, unsigned int epoch,
+                      int64_t timeout_ns, void* stream);
 
 /* ---- pixel stage -------------------------------------------------------- */
 /* pixel_rms_norm, src/iris_metal/kernels.py:486-498 (MSL :217-232): bf16 out. */

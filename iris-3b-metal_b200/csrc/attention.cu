@@ -60,6 +60,10 @@ struct Params {
   __nv_bfloat16* o_image;  // rows b * (n - split) + i - split
   const __nv_bfloat16* gate_text;  // bf16 gate logits in the same rows, or null
   const __nv_bfloat16* gate_image;
+  // sequence parallelism (peers > 0): query i's row goes to rank i / peer_tokens,
+  // row b * peer_tokens + i % peer_tokens, columns peer_col0 + h * 128 ...
+  int64_t peers, peer_tokens, peer_col0, peer_row_stride;
+  __nv_bfloat16* o_peer[IRIS_MAX_PEERS];
 };
 
 IRIS_DEVICE float ex2(float x) {
@@ -404,6 +408,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (ok && __all_sync(0xffffffffu, mbar_wait(&s->o_final[tile], 0, abort))) {
       tc_fence_after();
       __nv_bfloat16* dst = (text ? p.o_text : p.o_image) + off;
+      if (p.peers > 0) {  // the row of the rank that owns token q, over NVLink
+        const int64_t owner = min(static_cast<int64_t>(q) / p.peer_tokens, p.peers - 1);
+        const int64_t lrow = static_cast<int64_t>(b) * p.peer_tokens + (q - owner * p.peer_tokens);
+        dst = p.o_peer[owner] + lrow * p.peer_row_stride + p.peer_col0 + static_cast<int64_t>(h) * D + half * 64;
+      }
       const float inv = 1.f / l_total;
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
@@ -448,6 +457,28 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 using namespace iris;
 
+static int launch_attention(const void* q, const void* k, const void* v, iris::attn::Params& p, void* stream) {
+  using namespace iris::attn;
+  CUtensorMap tq, tk, tv;
+  IRIS_CHECK_STATUS(make_tmap_2d_bf16(&tq, q, D, p.batch * p.heads_q * p.n, D, 64, BQ));
+  IRIS_CHECK_STATUS(make_tmap_2d_bf16(&tk, k, D, p.batch * p.heads_kv * p.n_kv, D, 64, BKV));
+  IRIS_CHECK_STATUS(make_tmap_2d_bf16(&tv, v, D, p.batch * p.heads_kv * p.n_kv, D, 64, BKV));
+  static bool configured[64] = {false};
+  int dev = 0;
+  IRIS_CUDA(cudaGetDevice(&dev));
+  if (dev < 64 && !configured[dev]) {
+    IRIS_CUDA(cudaFuncSetAttribute(flash_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(SMEM_BYTES)));
+    configured[dev] = true;
+  }
+  const int per_cta = TILES * BQ;
+  dim3 grid(static_cast<unsigned>((p.n + per_cta - 1) / per_cta), static_cast<unsigned>(p.heads_q),
+            static_cast<unsigned>(p.batch));
+  flash_attn_kernel<<<grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
+  IRIS_CUDA(cudaGetLastError());
+  return IRIS_OK;
+}
+
 extern "C" int iris_flash_attn_fwd_split(const void* q, const void* k, const void* v, int64_t batch,
                                          int64_t heads_q, int64_t heads_kv, int64_t n, int64_t n_kv,
                                          int64_t head_dim, float scale,
@@ -470,11 +501,7 @@ extern "C" int iris_flash_attn_fwd_split(const void* q, const void* k, const voi
   IRIS_REQUIRE((gate_image == nullptr || aligned16(gate_image)) && (gate_text == nullptr || aligned16(gate_text)),
                "flash_attn_fwd: gate alignment");
   IRIS_REQUIRE(batch <= 65535 && heads_q <= 65535, "flash_attn_fwd: grid too large");
-  CUtensorMap tq, tk, tv;
-  IRIS_CHECK_STATUS(make_tmap_2d_bf16(&tq, q, D, batch * heads_q * n, D, 64, BQ));
-  IRIS_CHECK_STATUS(make_tmap_2d_bf16(&tk, k, D, batch * heads_kv * n_kv, D, 64, BKV));
-  IRIS_CHECK_STATUS(make_tmap_2d_bf16(&tv, v, D, batch * heads_kv * n_kv, D, 64, BKV));
-  Params p;
+  Params p = {};
   p.batch = batch;
   p.heads_q = heads_q;
   p.heads_kv = heads_kv;
@@ -487,20 +514,45 @@ extern "C" int iris_flash_attn_fwd_split(const void* q, const void* k, const voi
   p.o_image = reinterpret_cast<__nv_bfloat16*>(o_image);
   p.gate_text = reinterpret_cast<const __nv_bfloat16*>(gate_text);
   p.gate_image = reinterpret_cast<const __nv_bfloat16*>(gate_image);
-  static bool configured[64] = {false};
-  int dev = 0;
-  IRIS_CUDA(cudaGetDevice(&dev));
-  if (dev < 64 && !configured[dev]) {
-    IRIS_CUDA(cudaFuncSetAttribute(flash_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   static_cast<int>(SMEM_BYTES)));
-    configured[dev] = true;
+  return launch_attention(q, k, v, p, stream);
+}
+
+extern "C" int iris_flash_attn_fwd_peers(const void* q, const void* k, const void* v, int64_t batch, int64_t heads_q,
+                                         int64_t heads_kv, int64_t n, int64_t n_kv, int64_t head_dim, float scale,
+                                         void* const* o_peers, int world, int64_t tokens_per_rank, int64_t col0,
+                                         int64_t row_stride, void* stream) {
+  using namespace iris::attn;
+  IRIS_REQUIRE(q && k && v && o_peers, "flash_attn_fwd_peers: null pointer");
+  IRIS_REQUIRE(head_dim == D, "flash_attn_fwd_peers: head_dim must be 128");
+  IRIS_REQUIRE(batch > 0 && heads_q > 0 && heads_kv > 0 && heads_q % heads_kv == 0,
+               "flash_attn_fwd_peers: heads_q must be a positive multiple of heads_kv");
+  IRIS_REQUIRE(world >= 1 && world <= IRIS_MAX_PEERS && tokens_per_rank > 0 && n == world * tokens_per_rank,
+               "flash_attn_fwd_peers: n must be world * tokens_per_rank");
+  IRIS_REQUIRE(batch * heads_q * n < (1ll << 31) && n_kv > 0 && batch * heads_kv * n_kv < (1ll << 31),
+               "flash_attn_fwd_peers: sequence too long");
+  IRIS_REQUIRE(col0 >= 0 && col0 % 8 == 0 && row_stride % 8 == 0 && col0 + heads_q * D <= row_stride,
+               "flash_attn_fwd_peers: columns col0 + heads_q * 128 must fit a row (multiples of 8)");
+  IRIS_REQUIRE(aligned16(q) && aligned16(k) && aligned16(v), "flash_attn_fwd_peers: alignment");
+  IRIS_REQUIRE(batch <= 65535 && heads_q <= 65535, "flash_attn_fwd_peers: grid too large");
+  Params p = {};
+  p.batch = batch;
+  p.heads_q = heads_q;
+  p.heads_kv = heads_kv;
+  p.n = n;
+  p.n_kv = n_kv;
+  p.row_stride = row_stride;
+  p.split = 0;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.peers = world;
+  p.peer_tokens = tokens_per_rank;
+  p.peer_col0 = col0;
+  p.peer_row_stride = row_stride;
+  for (int j = 0; j < world; ++j) {
+    IRIS_REQUIRE(o_peers[j] != nullptr && aligned16(o_peers[j]), "flash_attn_fwd_peers: output rows must be aligned");
+    p.o_peer[j] = static_cast<__nv_bfloat16*>(o_peers[j]);
   }
-  const int per_cta = TILES * BQ;
-  dim3 grid(static_cast<unsigned>((n + per_cta - 1) / per_cta), static_cast<unsigned>(heads_q),
-            static_cast<unsigned>(batch));
-  flash_attn_kernel<<<grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
-  IRIS_CUDA(cudaGetLastError());
-  return IRIS_OK;
+  p.o_image = p.o_peer[0];
+  return launch_attention(q, k, v, p, stream);
 }
 
 extern "C" int iris_flash_attn_fwd(const void* q, const void* k, const void* v, void* o, int64_t batch,

@@ -50,13 +50,23 @@ constexpr int TMEM_COLS = 512;        // two 256-column fp32 accumulators
 constexpr int THREADS = 192;
 constexpr int GROUP_M = 16;           // tile rasterisation: 16 M-blocks per group
 constexpr int MAX_PROBLEMS = 4;
-constexpr size_t SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + 256 /*barriers*/;
+// Per epilogue warp, an 8 KB staging tile (32 rows x 256 B) for the peer forms
+// of EPI_HEADS: a warp's head rows leave as whole 256-byte rows, two per
+// store instruction, instead of 16-byte pieces of 32 different rows, which
+// over NVLink would travel as many partial writes.
+constexpr int EPI_STAGE_BYTES = 32 * 256;
+constexpr int EPI_WARPS = 4;
+constexpr size_t SMEM_BYTES =
+    1024 /*align slack*/ + STAGES * STAGE_BYTES + 256 /*barriers*/ + EPI_WARPS * EPI_STAGE_BYTES;
 
 enum Epilogue : int { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_GATE = 2, EPI_HEADS = 3 };
 
 // EPI_HEADS: the tile's 256 columns are two 128-wide head slots of a [q | k |
 // v] projection; q and k slots are RMS-normed and rotated, v copied, each to
 // its head layout (what iris_qkv_heads does from a stored projection).
+// With a peer mode the rows are one sequence-parallel rank's tokens and each
+// head row is stored into the buffer of the rank that consumes it (mapped
+// into this process), so the projection and the exchange are one kernel.
 struct HeadsOut {
   __nv_bfloat16* q;
   __nv_bfloat16* k;
@@ -69,6 +79,11 @@ struct HeadsOut {
   int head_major;
   int hq, hkv;
   int64_t tokens, batch, n_out, n_out_kv;
+  int peer_mode, world;
+  int64_t token_offset, n_dest;
+  __nv_bfloat16* q_peer[IRIS_MAX_PEERS];
+  __nv_bfloat16* k_peer[IRIS_MAX_PEERS];
+  __nv_bfloat16* v_peer[IRIS_MAX_PEERS];
 };
 
 struct Problem {
@@ -106,6 +121,9 @@ struct Smem {
   uint32_t tmem_base;
   int abort;
 };
+
+static_assert(sizeof(Smem) <= 256, "one-SM barriers must fit their 256-byte slot");
+static_assert(SMEM_BYTES <= 232448, "one-SM kernel shared memory");
 
 struct Tile {
   int p, mb, nb;
@@ -149,14 +167,28 @@ IRIS_DEVICE void store_row32(const Problem& p, int64_t prow, int col0, const flo
 // times the gain, rotary pairs (2i, 2i+1) by the token's cos / sin, bf16.
 // Every lane of the warp runs the TMEM loads (warp-collective); only lanes
 // with a real row (`row_ok`) store.
-IRIS_DEVICE void store_head_slot(const HeadsOut& hd, uint32_t t_col, int slot, int64_t bn, bool row_ok) {
+IRIS_DEVICE void store_head_slot(const HeadsOut& hd, uint32_t t_col, int slot, int64_t bn, bool row_ok,
+                                 uint8_t* stage) {
   const int64_t b = bn / hd.tokens, t = bn % hd.tokens;
   const bool is_q = slot < hd.hq, is_k = !is_q && slot < hd.hq + hd.hkv;
   const int h = is_q ? slot : is_k ? slot - hd.hq : slot - hd.hq - hd.hkv;
   const int heads = is_q ? hd.hq : hd.hkv;
   const int64_t len = is_q ? hd.n_out : hd.n_out_kv;
-  __nv_bfloat16* base = is_q ? hd.q : is_k ? hd.k : hd.v;
-  __nv_bfloat16* dst = base + ((hd.head_major ? h * hd.batch + b : b * heads + h) * len + t) * 128;
+  // destinations: one, or (k / v broadcast) one per rank
+  const bool scatter = hd.peer_mode == IRIS_HEADS_PEER_SCATTER;
+  const bool broadcast = hd.peer_mode == IRIS_HEADS_PEER_BROADCAST_KV && !is_q;
+  const int n_dst = broadcast ? hd.world : 1;
+  auto dst_of = [&](int j) -> __nv_bfloat16* {
+    if (scatter) {
+      const int per = heads / hd.world;
+      const int owner = h / per;
+      __nv_bfloat16* pb = is_q ? hd.q_peer[owner] : is_k ? hd.k_peer[owner] : hd.v_peer[owner];
+      return pb + ((b * per + (h - owner * per)) * hd.n_dest + hd.token_offset + t) * 128;
+    }
+    if (broadcast) return (is_k ? hd.k_peer[j] : hd.v_peer[j]) + ((b * heads + h) * hd.n_dest + hd.token_offset + t) * 128;
+    __nv_bfloat16* base = is_q ? hd.q : is_k ? hd.k : hd.v;
+    return base + ((hd.head_major ? h * hd.batch + b : b * heads + h) * len + t) * 128;
+  };
   float inv = 1.f;
   const float* gain = is_q ? hd.qw : hd.kw;
   if (is_q || is_k) {
@@ -199,18 +231,44 @@ IRIS_DEVICE void store_head_slot(const HeadsOut& hd, uint32_t t_col, int slot, i
 #pragma unroll
       for (int j = 0; j < 16; ++j) packed[j] = pack_bf16x2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
     }
-    if (row_ok) {
-      uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+    if (hd.peer_mode != IRIS_HEADS_LOCAL) {
+      // 16-byte chunk q of row r at (q ^ (r & 15)) * 16: the 32 rows' same chunk spread over the banks
+      const int r = threadIdx.x & 31;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        *reinterpret_cast<uint4*>(stage + r * 256 + (((c * 4 + j) ^ (r & 15)) * 16)) =
+            make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+    } else if (row_ok) {
+      uint4* d4 = reinterpret_cast<uint4*>(dst_of(0) + c * 32);
 #pragma unroll
       for (int j = 0; j < 4; ++j)
         d4[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
     }
   }
+  if (hd.peer_mode == IRIS_HEADS_LOCAL) return;
+  // write-out: lane L stores 16-byte chunk L % 16 of row 2k + L / 16, so each
+  // instruction writes two whole 256-byte rows (each row's destination and
+  // validity come from the thread that owns it)
+  __syncwarp();
+  const int lane = threadIdx.x & 31;
+#pragma unroll 1
+  for (int r_dst = 0; r_dst < n_dst; ++r_dst) {
+    const unsigned long long mine = row_ok ? reinterpret_cast<unsigned long long>(dst_of(r_dst)) : 0ull;
+#pragma unroll 4
+    for (int k = 0; k < 16; ++k) {
+      const int row = 2 * k + (lane >> 4), q = lane & 15;
+      const unsigned long long dst = __shfl_sync(0xffffffffu, mine, row);
+      if (dst != 0ull)
+        *reinterpret_cast<uint4*>(dst + q * 16) =
+            *reinterpret_cast<const uint4*>(stage + row * 256 + ((q ^ (row & 15)) * 16));
+    }
+  }
+  __syncwarp();  // the tile is reused by this warp's next head slot
 }
 
 // The epilogue of one accumulator tile for this thread's row m (TMEM lane
 // base `t_base`, column 0 of the accumulator); `nb` is the tile's N block.
-IRIS_DEVICE void epilogue_row(const Problem& p, uint32_t t_base, int64_t m, int nb) {
+IRIS_DEVICE void epilogue_row(const Problem& p, uint32_t t_base, int64_t m, int nb, uint8_t* stage) {
   const bool row_ok = m < p.M;
   if (p.epilogue == EPI_HEADS) {
     const int64_t bn = row_ok ? p.out_map(m) : 0;
@@ -218,7 +276,7 @@ IRIS_DEVICE void epilogue_row(const Problem& p, uint32_t t_base, int64_t m, int 
 #pragma unroll 1
     for (int k = 0; k < 2; ++k) {
       const int slot = nb * 2 + k;  // uniform across the warp, as the TMEM loads require
-      if (slot < slots) store_head_slot(p.heads, t_base + k * 128, slot, bn, row_ok);
+      if (slot < slots) store_head_slot(p.heads, t_base + k * 128, slot, bn, row_ok, stage);
     }
     return;
   }
@@ -401,6 +459,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32)
     const int row_in_tile = quarter * 32 + lane;
+    uint8_t* stage = base + STAGES * STAGE_BYTES + 256 + (warp - 2) * EPI_STAGE_BYTES;
     int it = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
       const Tile tl = locate(bt, t);
@@ -411,7 +470,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!__all_sync(0xffffffffu, mbar_wait(&s->tmem_full[acc], acc_phase, abort))) break;
       tc_fence_after();
       const uint32_t t_base = tmem + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(quarter * 32) << 16);
-      epilogue_row(p, t_base, static_cast<int64_t>(tl.mb) * BM + row_in_tile, tl.nb);
+      epilogue_row(p, t_base, static_cast<int64_t>(tl.mb) * BM + row_in_tile, tl.nb, stage);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s->tmem_empty[acc]);
@@ -443,7 +502,7 @@ constexpr int STAGES = 6;
 constexpr int A_BYTES = 128 * BK * 2;  // 16 KB: this CTA's rows
 constexpr int B_BYTES = 128 * BK * 2;  // 16 KB: this CTA's half of the W tile
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr size_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
+constexpr size_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256 + EPI_WARPS * EPI_STAGE_BYTES;
 
 struct Smem {
   uint64_t full[STAGES];  // used in the leader only: both CTAs' copies complete here
@@ -454,6 +513,8 @@ struct Smem {
   uint32_t tmem_base;
   int abort;
 };
+static_assert(sizeof(Smem) <= 256, "pair barriers must fit their 256-byte slot");
+static_assert(SMEM_BYTES <= 232448, "pair kernel shared memory");
 }  // namespace pair
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
@@ -585,6 +646,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int quarter = warp & 3;
     const int row_in_tile = quarter * 32 + lane;
+    uint8_t* stage = base + pair::STAGES * pair::STAGE_BYTES + 256 + (warp - 2) * EPI_STAGE_BYTES;
     const uint32_t empty_leader = map_to_cta(&s->tmem_empty[0], 0);
     int it = 0;
     for (int t = pair_id; t < num_tiles; t += pairs, ++it) {
@@ -596,7 +658,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       tc_fence_after();
       const uint32_t t_base = tmem + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(quarter * 32) << 16);
       epilogue_row(p, t_base, static_cast<int64_t>(tl.mb) * pair::BM + static_cast<int64_t>(rank) * 128 + row_in_tile,
-                   tl.nb);
+                   tl.nb, stage);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(empty_leader + static_cast<uint32_t>(acc) * 8u);
@@ -614,14 +676,34 @@ int check_heads(const iris_gemm_problem& q) {
   IRIS_REQUIRE(hd != nullptr, "iris_gemm_bf16: the heads epilogue needs its parameters");
   IRIS_REQUIRE(hd->heads_q > 0 && hd->heads_kv >= 0 && q.N == (hd->heads_q + 2 * hd->heads_kv) * 128,
                "iris_gemm_bf16: heads epilogue needs N = (heads_q + 2 heads_kv) * 128");
-  IRIS_REQUIRE(hd->q_out && hd->q_weight && hd->cos && hd->sin &&
-                   (hd->heads_kv == 0 || (hd->k_out && hd->v_out && hd->k_weight)),
+  const int mode = hd->peer_mode;
+  IRIS_REQUIRE(mode == IRIS_HEADS_LOCAL || mode == IRIS_HEADS_PEER_SCATTER || mode == IRIS_HEADS_PEER_BROADCAST_KV,
+               "iris_gemm_bf16: unknown heads peer_mode");
+  IRIS_REQUIRE(hd->q_weight && hd->cos && hd->sin && (hd->heads_kv == 0 || hd->k_weight),
                "iris_gemm_bf16: heads epilogue null pointer");
-  IRIS_REQUIRE(aligned16(hd->q_out) && aligned16(hd->q_weight) && aligned16(hd->cos) && aligned16(hd->sin) &&
-                   (hd->heads_kv == 0 || (aligned16(hd->k_out) && aligned16(hd->v_out) && aligned16(hd->k_weight))),
+  IRIS_REQUIRE(aligned16(hd->q_weight) && aligned16(hd->cos) && aligned16(hd->sin) &&
+                   (hd->heads_kv == 0 || aligned16(hd->k_weight)),
                "iris_gemm_bf16: heads epilogue pointers must be 16-byte aligned");
-  IRIS_REQUIRE(hd->tokens > 0 && hd->batch > 0 && hd->tokens <= hd->n_out &&
-                   (hd->heads_kv == 0 || hd->tokens <= hd->n_out_kv),
+  const bool local_q = mode != IRIS_HEADS_PEER_SCATTER, local_kv = mode == IRIS_HEADS_LOCAL;
+  IRIS_REQUIRE(!local_q || (hd->q_out && aligned16(hd->q_out)), "iris_gemm_bf16: heads epilogue q_out");
+  IRIS_REQUIRE(!local_kv || hd->heads_kv == 0 || (hd->k_out && hd->v_out && aligned16(hd->k_out) && aligned16(hd->v_out)),
+               "iris_gemm_bf16: heads epilogue k_out / v_out");
+  if (mode != IRIS_HEADS_LOCAL) {
+    IRIS_REQUIRE(hd->world >= 1 && hd->world <= IRIS_MAX_PEERS, "iris_gemm_bf16: heads epilogue world out of range");
+    IRIS_REQUIRE(hd->token_offset >= 0 && hd->token_offset + hd->tokens <= hd->n_dest,
+                 "iris_gemm_bf16: heads epilogue token_offset + tokens > n_dest");
+    if (mode == IRIS_HEADS_PEER_SCATTER)
+      IRIS_REQUIRE(hd->heads_q % hd->world == 0 && hd->heads_kv % hd->world == 0,
+                   "iris_gemm_bf16: scattered heads must divide over the ranks");
+    for (int j = 0; j < hd->world; ++j) {
+      const bool q_ok = mode != IRIS_HEADS_PEER_SCATTER || (hd->q_peer[j] && aligned16(hd->q_peer[j]));
+      const bool kv_ok = hd->heads_kv == 0 || (hd->k_peer[j] && hd->v_peer[j] && aligned16(hd->k_peer[j]) &&
+                                               aligned16(hd->v_peer[j]));
+      IRIS_REQUIRE(q_ok && kv_ok, "iris_gemm_bf16: heads epilogue peer buffers must be non-null and 16-byte aligned");
+    }
+  }
+  IRIS_REQUIRE(hd->tokens > 0 && hd->batch > 0 && (!local_q || hd->tokens <= hd->n_out) &&
+                   (!local_kv || hd->heads_kv == 0 || hd->tokens <= hd->n_out_kv),
                "iris_gemm_bf16: heads epilogue needs tokens <= n_out, n_out_kv");
   // the largest row the map produces must stay inside batch * tokens positions
   const int64_t last = (q.M - 1) / q.out_seg_rows * q.out_seg_stride + q.out_seg_offset +
@@ -707,10 +789,32 @@ extern "C" int iris_gemm_bf16_grouped(const iris_gemm_problem* problems, int cou
     p.heads = HeadsOut{};
     if (q.epilogue == EPI_HEADS) {
       const iris_heads_epilogue& hd = *q.heads;
-      p.heads = HeadsOut{static_cast<__nv_bfloat16*>(hd.q_out), static_cast<__nv_bfloat16*>(hd.k_out),
-                         static_cast<__nv_bfloat16*>(hd.v_out), hd.q_weight, hd.k_weight, hd.cos, hd.sin, hd.eps,
-                         hd.head_major, static_cast<int>(hd.heads_q), static_cast<int>(hd.heads_kv), hd.tokens,
-                         hd.batch, hd.n_out, hd.n_out_kv};
+      HeadsOut& ho = p.heads;
+      ho.q = static_cast<__nv_bfloat16*>(hd.q_out);
+      ho.k = static_cast<__nv_bfloat16*>(hd.k_out);
+      ho.v = static_cast<__nv_bfloat16*>(hd.v_out);
+      ho.qw = hd.q_weight;
+      ho.kw = hd.k_weight;
+      ho.cos = hd.cos;
+      ho.sin = hd.sin;
+      ho.eps = hd.eps;
+      ho.head_major = hd.head_major;
+      ho.hq = static_cast<int>(hd.heads_q);
+      ho.hkv = static_cast<int>(hd.heads_kv);
+      ho.tokens = hd.tokens;
+      ho.batch = hd.batch;
+      ho.n_out = hd.n_out;
+      ho.n_out_kv = hd.n_out_kv;
+      ho.peer_mode = hd.peer_mode;
+      ho.world = hd.world;
+      ho.token_offset = hd.token_offset;
+      ho.n_dest = hd.n_dest;
+      for (int j = 0; j < IRIS_MAX_PEERS; ++j) {
+        const bool used = j < hd.world;
+        ho.q_peer[j] = used ? static_cast<__nv_bfloat16*>(hd.q_peer[j]) : nullptr;
+        ho.k_peer[j] = used ? static_cast<__nv_bfloat16*>(hd.k_peer[j]) : nullptr;
+        ho.v_peer[j] = used ? static_cast<__nv_bfloat16*>(hd.v_peer[j]) : nullptr;
+      }
     }
     total += static_cast<int64_t>(p.num_m) * p.num_n;
     IRIS_REQUIRE(total < (1ll << 30), "iris_gemm_bf16_grouped: too many tiles");

@@ -4,6 +4,7 @@
 #include "attention.cu"
 #include "gemm.cu"
 #include "heads.cu"
+#include "peer.cu"
 #include "pixel.cu"
 #include "rows.cu"
 #include "small.cu"

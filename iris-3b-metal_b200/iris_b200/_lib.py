@@ -15,6 +15,9 @@ LIBRARY = Path(__file__).resolve().parent / "libiris_b200.so"
 IRIS_OK, IRIS_EINVAL, IRIS_ECUDA = 0, 1, 2
 F32, BF16, F16 = 0, 1, 2
 EPI_STORE, EPI_SWIGLU, EPI_GATE, EPI_HEADS = 0, 1, 2, 3
+HEADS_LOCAL, HEADS_PEER_SCATTER, HEADS_PEER_BROADCAST_KV = 0, 1, 2
+MAX_PEERS = 8  # IRIS_MAX_PEERS
+IPC_HANDLE_BYTES = 64
 NEXT_NONE, NEXT_NORM_MODULATE, NEXT_SILU_ADD = 0, 1, 2
 
 P, I64, I32, F = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float
@@ -52,7 +55,8 @@ class HeadsEpilogue(ctypes.Structure):
     _fields_ = [
         ("q_out", P), ("k_out", P), ("v_out", P), ("q_weight", P), ("k_weight", P), ("cos", P), ("sin", P),
         ("eps", F), ("head_major", I32), ("heads_q", I64), ("heads_kv", I64), ("tokens", I64), ("batch", I64),
-        ("n_out", I64), ("n_out_kv", I64),
+        ("n_out", I64), ("n_out_kv", I64), ("peer_mode", I32), ("world", I32), ("token_offset", I64),
+        ("n_dest", I64), ("q_peer", P * MAX_PEERS), ("k_peer", P * MAX_PEERS), ("v_peer", P * MAX_PEERS),
     ]  # fmt: skip
 
 
@@ -69,6 +73,11 @@ class GemmProblem(ctypes.Structure):
 
 
 SIGNATURES["iris_gemm_bf16_grouped"] = [ctypes.POINTER(GemmProblem), I32, P]
+SIGNATURES["iris_flash_attn_fwd_peers"] = [P, P, P, I64, I64, I64, I64, I64, I64, F, P, I32, I64, I64, I64, P]
+SIGNATURES["iris_ipc_export"] = [P, P, ctypes.POINTER(I64)]
+SIGNATURES["iris_ipc_import"] = [P, ctypes.POINTER(P)]
+SIGNATURES["iris_ipc_close"] = [P]
+SIGNATURES["iris_peer_barrier"] = [P, P, I32, I32, ctypes.c_uint, I64, P]
 SIGNATURES["iris_flash_attn_fwd_split"] = [P, P, P, I64, I64, I64, I64, I64, I64, F, I64, P, P, P, P, I64, P]
 
 _lib: ctypes.CDLL | None = None
@@ -97,7 +106,8 @@ def load() -> ctypes.CDLL:
 
 _launches = 0
 # kernels each entry point enqueues (1 unless listed)
-_KERNELS_PER_CALL = {"iris_device_error": 0, "iris_all_finite": 2}
+_KERNELS_PER_CALL = {"iris_device_error": 0, "iris_all_finite": 2, "iris_ipc_export": 0, "iris_ipc_import": 0,
+                     "iris_ipc_close": 0}
 
 
 def launch_count() -> int:

@@ -297,22 +297,48 @@ class HeadsOut:
     position), ``tokens`` positions per sample."""
 
     def __init__(self, q, k, v, q_weight, k_weight, cos, sin, eps, hq, hkv, tokens, batch, n_out, n_out_kv,
-                 head_major=False):  # fmt: skip
+                 head_major=False, peers=None):  # fmt: skip
         _require_fp32(q_weight=q_weight, cos=cos, sin=sin)
         _require(q_weight.numel() == HEAD_DIM and (k_weight is None or k_weight.numel() == HEAD_DIM),
                  "heads epilogue gains must have 128 entries")  # fmt: skip
         _require(cos.shape == sin.shape and cos.shape[-1] == HEAD_DIM // 2 and cos.shape[0] >= tokens,
                  "heads epilogue rotary tables must cover the token positions")  # fmt: skip
         _require(all(t is None or t.dtype == torch.bfloat16 for t in (q, k, v)), "heads epilogue writes bf16")
-        _require(q.numel() >= batch * hq * n_out * HEAD_DIM
-                 and (hkv == 0 or min(k.numel(), v.numel()) >= batch * hkv * n_out_kv * HEAD_DIM),
-                 "heads epilogue outputs are too small")  # fmt: skip
+        mode = _lib.HEADS_LOCAL if peers is None else peers.mode
+        local_q, local_kv = mode != _lib.HEADS_PEER_SCATTER, mode == _lib.HEADS_LOCAL
+        _require(not local_q or q.numel() >= batch * hq * n_out * HEAD_DIM, "heads epilogue q output is too small")
+        _require(not local_kv or hkv == 0 or min(k.numel(), v.numel()) >= batch * hkv * n_out_kv * HEAD_DIM,
+                 "heads epilogue k / v outputs are too small")  # fmt: skip
         _require_cuda(*(t for t in (q, k, v, q_weight, k_weight, cos, sin) if t is not None))
         self._tensors = (q, k, v, q_weight, k_weight, cos, sin)
         self.struct = _lib.HeadsEpilogue(
-            q.data_ptr(), _ptr(k), _ptr(v), q_weight.data_ptr(), _ptr(k_weight), cos.data_ptr(), sin.data_ptr(),
+            _ptr(q), _ptr(k), _ptr(v), q_weight.data_ptr(), _ptr(k_weight), cos.data_ptr(), sin.data_ptr(),
             float(eps), int(bool(head_major)), hq, hkv, tokens, batch, n_out, n_out_kv,
         )  # fmt: skip
+        if peers is not None:
+            peers.fill(self.struct)
+
+
+class PeerHeads:
+    """Sequence-parallel destinations of the ``EPI_HEADS`` epilogue: ``mode``
+    ``_lib.HEADS_PEER_SCATTER`` (head ``h`` of q / k / v to rank
+    ``h // (heads / world)``) or ``_lib.HEADS_PEER_BROADCAST_KV`` (k and v to
+    every rank, q local); per rank ``j`` the device pointers (valid in this
+    process) of its ``[B, heads', n_dest, 128]`` q / k / v buffers; this rank's
+    tokens land at positions ``token_offset + t``."""
+
+    def __init__(self, mode: int, q_ptrs, k_ptrs, v_ptrs, token_offset: int, n_dest: int):
+        world = len(k_ptrs)
+        _require(1 <= world <= _lib.MAX_PEERS and len(v_ptrs) == world, "peer heads: 1 to 8 ranks")
+        _require(mode != _lib.HEADS_PEER_SCATTER or len(q_ptrs) == world, "peer heads: q pointers per rank")
+        self.mode, self.world = mode, world
+        self.q, self.k, self.v = list(q_ptrs or [0] * world), list(k_ptrs), list(v_ptrs)
+        self.token_offset, self.n_dest = token_offset, n_dest
+
+    def fill(self, st) -> None:
+        st.peer_mode, st.world, st.token_offset, st.n_dest = self.mode, self.world, self.token_offset, self.n_dest
+        for j in range(self.world):
+            st.q_peer[j], st.k_peer[j], st.v_peer[j] = self.q[j] or None, self.k[j], self.v[j]
 
 
 def gemm_grouped(problems: list, stream: int) -> None:
@@ -379,6 +405,57 @@ def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torc
         out.stride(1), stream_of(q),
     )  # fmt: skip
     return out
+
+
+def flash_attention_peers(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out_ptrs, tokens_per_rank: int,
+                          col0: int, row_stride: int, scale: float | None = None) -> None:  # fmt: skip
+    """Sequence-parallel attention of this rank's heads over every token: the
+    output row of query ``i`` (bf16, ``q.shape[1] * 128`` columns from ``col0``)
+    goes to rank ``i // tokens_per_rank``'s token rows ``out_ptrs[j]`` (device
+    pointers valid in this process), row ``b * tokens_per_rank + i %
+    tokens_per_rank`` of ``row_stride`` elements."""
+    _check_qkv(q, k, v)
+    batch, heads, n, d = q.shape
+    world = len(out_ptrs)
+    _require(1 <= world <= _lib.MAX_PEERS and n == world * tokens_per_rank, "flash_attention_peers: n = world * tokens")
+    _require_cuda(q, k, v)
+    ptrs = (ctypes.c_void_p * world)(*out_ptrs)
+    _lib.call(
+        "iris_flash_attn_fwd_peers", q.data_ptr(), k.data_ptr(), v.data_ptr(), batch, heads, k.shape[1], n,
+        k.shape[2], d, float(scale if scale is not None else d**-0.5), ptrs, world, tokens_per_rank, col0, row_stride,
+        stream_of(q),
+    )  # fmt: skip
+
+
+def ipc_export(t: torch.Tensor) -> tuple[bytes, int]:
+    """(IPC handle, byte offset) of the allocation holding ``t``'s storage."""
+    _require_cuda(t)
+    handle = ctypes.create_string_buffer(_lib.IPC_HANDLE_BYTES)
+    offset = ctypes.c_int64(0)
+    _lib.call("iris_ipc_export", t.data_ptr(), handle, ctypes.byref(offset))
+    return handle.raw, int(offset.value)
+
+
+def ipc_import(handle: bytes) -> int:
+    """Map another process's allocation; returns its base device pointer."""
+    _require(len(handle) == _lib.IPC_HANDLE_BYTES, "ipc_import: bad handle")
+    base = ctypes.c_void_p(0)
+    _lib.call("iris_ipc_import", ctypes.create_string_buffer(handle, len(handle)), ctypes.byref(base))
+    return int(base.value)
+
+
+def ipc_close(base: int) -> None:
+    _lib.call("iris_ipc_close", base)
+
+
+def peer_barrier(flags: torch.Tensor, peer_flag_ptrs, rank: int, epoch: int, timeout_s: float = 2.0) -> None:
+    """Signal the ranks (slot ``rank`` of each peer's flags) and wait for theirs in
+    ``flags`` (int32 ``[world]`` of this rank), on the current stream."""
+    world = len(peer_flag_ptrs)
+    _require(flags.dtype == torch.int32 and flags.numel() >= world, "peer_barrier: flags must be int32 [world]")
+    ptrs = (ctypes.c_void_p * world)(*[p or None for p in peer_flag_ptrs])
+    _lib.call("iris_peer_barrier", flags.data_ptr(), ptrs, rank, world, epoch & 0xFFFFFFFF, int(timeout_s * 1e9),
+              stream_of(flags))  # fmt: skip
 
 
 def _check_qkv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:

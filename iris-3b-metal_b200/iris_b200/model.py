@@ -43,7 +43,7 @@ from iris_b200 import _lib
 from iris_b200 import kernels as K
 from iris_b200.config import ModelConfig, from_any
 from iris_b200.tables import cos_sin, rope_1d, rope_2d, sincos_pos_embed_2d
-from iris_b200.ulysses import SequenceShard, gather_image_tokens, gather_tokens, scatter_heads
+from iris_b200.ulysses import PeerBuffers, SequenceShard, gather_image_tokens, gather_tokens, scatter_heads
 
 HEAD_DIM = 128
 SWIGLU_TILE = 128  # w1/w3 rows per SwiGLU GEMM tile half
@@ -150,6 +150,12 @@ class CudaIris:
             if cfg.num_heads % world or cfg.kv_heads % world:
                 raise ValueError(f"sequence parallelism over {world} ranks needs the trunk's query and key/value "
                                  f"head counts ({cfg.num_heads}, {cfg.kv_heads}) divisible by {world}")  # fmt: skip
+            if world > _lib.MAX_PEERS:
+                raise ValueError(f"sequence parallelism spans at most {_lib.MAX_PEERS} ranks")
+        # one process per GPU: the exchanges are the producing kernels' stores into peer memory
+        self.peer = self.comm is not None and bool(getattr(self.comm, "peer_capable", False))
+        self.peer_timeout_s = 2.0
+        self._epoch = 0
         self._pack(state)
         self._tables: dict = {}
         self._work: dict = {}
@@ -324,6 +330,9 @@ class CudaIris:
         key = (batch, grid, shard)
         if key in self._work:
             return self._work[key]
+        for old in self._work.values():
+            if "_peers" in old:
+                old["_peers"].close()
         self._work.clear()
         cfg, dev = self.cfg, self.device
         d = cfg.hidden_size
@@ -367,7 +376,24 @@ class CudaIris:
             "mods_txt": e(max(1, 0 if self.txt_bias is None else self.txt_bias.shape[0]), batch, 6 * d,
                           dtype=torch.float32),  # fmt: skip
         }
-        if shard.world > 1:
+        if shard.world > 1 and self.peer:
+            P, N = shard.world, shard.N
+            hql, hkvl = hq // P, hkv // P
+            ws.update({
+                # written by every rank's kernels: this rank's heads over the whole sequence,
+                # its token rows of every head's attention output, the pixel keys / values of
+                # every patch token (two buffers, alternating by pixel block), barrier flags
+                "qf": e(batch, hql, N, HEAD_DIM),
+                "kf": e(batch, hkvl, N, HEAD_DIM),
+                "vf": e(batch, hkvl, N, HEAD_DIM),
+                "o_loc": e(batch * n, hq * HEAD_DIM),
+                "pk1": e(batch, pix.num_heads, shard.L, HEAD_DIM),
+                "pv1": e(batch, pix.num_heads, shard.L, HEAD_DIM),
+                "flags": torch.zeros(P, device=dev, dtype=torch.int32),
+            })  # fmt: skip
+            shared = ("qf", "kf", "vf", "o_loc", "pk", "pv", "pk1", "pv1", "flags")
+            ws["_peers"] = PeerBuffers(self.comm, {name: ws[name] for name in shared})
+        elif shard.world > 1:
             P, N = shard.world, shard.N
             hql, hkvl = hq // P, hkv // P
             ws.update({
@@ -527,11 +553,16 @@ class CudaIris:
 
         # Q/K/V projection with QK-norm + RoPE + the head layout in its epilogue
         problems = []
+        peers = None
+        if self.peer:  # each head row straight into the full-sequence buffer of the rank that owns the head
+            pb = ws["_peers"]
+            peers = K.PeerHeads(_lib.HEADS_PEER_SCATTER, pb.ptrs["qf"], pb.ptrs["kf"], pb.ptrs["vf"], g.shard.start,
+                                g.shard.N)  # fmt: skip
         for s, rows, _, tmap, off in order:
             qn, kn = block.qk_norm[s]
             heads = K.HeadsOut(
                 ws["q"], ws["k"], ws["v"], qn, kn, cos, sin, eps, cfg.num_heads, cfg.kv_heads, g.N, g.batch, g.N, g.N,
-                head_major=self.comm is not None,
+                head_major=self.comm is not None, peers=peers,
             )  # fmt: skip
             problems.append(K.gemm_problem(h[off : off + rows], block.qkv[s], None, out_rows=tmap, heads=heads))
         K.gemm_grouped(problems, st)
@@ -560,10 +591,18 @@ class CudaIris:
         comm, P = self.comm, self.comm.world
         B, n = g.batch, g.N
         hql, hkvl = self.cfg.num_heads // P, self.cfg.kv_heads // P
-        for name, heads in (("q", hql), ("k", hkvl), ("v", hkvl)):
-            scatter_heads(comm, K.block_copy, ws[name], ws[name + "_r"], ws[name + "f"], heads, B, n, HEAD_DIM)
-        K.flash_attention(ws["qf"], ws["kf"], ws["vf"], ws["of"])
-        gather_tokens(comm, K.block_copy, ws["of"], ws["o_s"], ws["o_r"], ws["o_loc"], B, n, hql * HEAD_DIM)
+        if self.peer:
+            # the Q/K/V epilogue has stored into every rank's qf / kf / vf; attention
+            # stores each output row into the token rows of the rank that owns it
+            self._barrier(ws)
+            K.flash_attention_peers(ws["qf"], ws["kf"], ws["vf"], ws["_peers"].ptrs["o_loc"], n,
+                                    comm.rank * hql * HEAD_DIM, self.cfg.num_heads * HEAD_DIM)  # fmt: skip
+            self._barrier(ws)
+        else:
+            for name, heads in (("q", hql), ("k", hkvl), ("v", hkvl)):
+                scatter_heads(comm, K.block_copy, ws[name], ws[name + "_r"], ws[name + "f"], heads, B, n, HEAD_DIM)
+            K.flash_attention(ws["qf"], ws["kf"], ws["vf"], ws["of"])
+            gather_tokens(comm, K.block_copy, ws["of"], ws["o_s"], ws["o_r"], ws["o_loc"], B, n, hql * HEAD_DIM)
         h = ws[_hkey(block)]
         problems = [
             K.gemm_problem(h[off : off + rows], block.gate[s], ws["og"][off : off + rows], epilogue=_lib.EPI_GATE,
@@ -571,6 +610,12 @@ class CudaIris:
             for s, rows, _, tmap, off in segs[::-1]
         ]
         K.gemm_grouped(problems, st)
+
+    def _barrier(self, ws) -> None:
+        """All ranks' work enqueued so far (their stores into this rank's buffers
+        included) completes before this rank's next kernel; bounded wait."""
+        self._epoch += 1
+        K.peer_barrier(ws["flags"], ws["_peers"].ptrs["flags"], self.comm.rank, self._epoch, self.peer_timeout_s)
 
     def _attn_residual(self, block, stream, rows, rpb, tmap, off, ws, g, eps, st) -> None:
         """Post-norm + gate + residual of the attention branch, fused with the
@@ -644,17 +689,26 @@ class CudaIris:
             K.gemm(ws["s_cond"], blk["adaln"][0], ws["pmods"], bias=blk["adaln"][1])
             K.gemm(ws["ph"], blk["compress"][0], ws["comp"], bias=blk["compress"][1])
             qn, kn = blk["qk_norm"]
-            kv = ("pk_s", "pv_s") if sp else ("pk", "pv")
+            kv = ("pk_s", "pv_s") if sp and not self.peer else ("pk", "pv")
+            peers = None
+            if self.peer:  # every rank's keys / values of all patch tokens; two buffers, alternating by block
+                kv = ("pk", "pv") if i % 2 == 0 else ("pk1", "pv1")
+                pb = ws["_peers"]
+                peers = K.PeerHeads(_lib.HEADS_PEER_BROADCAST_KV, None, pb.ptrs[kv[0]], pb.ptrs[kv[1]],
+                                    g.shard.image_start, g.shard.L)  # fmt: skip
             targets = K.HeadsOut(
                 ws["pq"], ws[kv[0]], ws[kv[1]], qn, kn, pcos, psin, eps, heads, heads, g.L, g.batch, g.L,
-                ws[kv[0]].shape[2],
+                ws[kv[0]].shape[2], peers=peers,
             )  # fmt: skip
             K.gemm_grouped([K.gemm_problem(ws["comp"], blk["qkv"], None, heads=targets)], st)
-            if sp:  # local queries over the keys / values of every patch token
+            if self.peer:
+                self._barrier(ws)
+            elif sp:  # local queries over the keys / values of every patch token
                 for name in ("pk", "pv"):
                     gather_image_tokens(self.comm, K.block_copy, g.shard, ws[name + "_s"], ws[name + "_g"], ws[name],
                                         g.batch, heads, HEAD_DIM)  # fmt: skip
-            K.flash_attention(ws["pq"], ws["pk"], ws["pv"], ws["po"].view(g.batch, g.L, -1))
+            full = kv if self.peer else ("pk", "pv")
+            K.flash_attention(ws["pq"], ws[full[0]], ws[full[1]], ws["po"].view(g.batch, g.L, -1))
             K.gemm(ws["po"], blk["proj"][0], ws["pproj"], bias=blk["proj"][1])
             K.gemm(ws["pproj"], blk["expand"][0], ws["pbranch"], bias=blk["expand"][1])
             (w1, b1), (w2, b2) = blk["fc1"], blk["fc2"]

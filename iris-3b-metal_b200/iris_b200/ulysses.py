@@ -23,6 +23,16 @@ the exchanges are:
 RoPE tables are indexed by global token position, the collectives go through
 a small communicator (:class:`TorchComm` over ``torch.distributed`` / NCCL in
 production), and every rank returns the full velocity.
+
+With one process per GPU (a communicator with ``peer_capable``), the exchanges
+are not collectives at all: the ranks map each other's exchange buffers with
+CUDA IPC (:class:`PeerBuffers`) and the producing kernels store into the
+consumer's buffer over NVLink -- the Q/K/V projection's epilogue writes every
+head row to the full-sequence buffer of the rank that owns that head, the
+attention epilogue writes every output row to the token rows of the rank that
+owns that token, and the pixel-stage K/V projection writes its rows to every
+rank. A bounded barrier kernel on flags in peer memory orders each producer
+before its consumers.
 """
 
 from __future__ import annotations
@@ -67,6 +77,45 @@ class TorchComm:
 
     def all_reduce_sum(self, t: torch.Tensor) -> None:
         self._dist.all_reduce(t, group=self.group)
+
+    # one process per GPU on one node: the ranks can map each other's buffers
+    peer_capable = True
+
+    def all_gather_object(self, obj) -> list:
+        out = [None] * self.world
+        self._dist.all_gather_object(out, obj, group=self.group)
+        return out
+
+
+class PeerBuffers:
+    """This rank's exchange buffers and, for each, the device pointer of every
+    rank's copy as mapped into this process (CUDA IPC; the rank's own entry is
+    its local pointer). Buffers that share an allocation are mapped once."""
+
+    def __init__(self, comm, tensors: dict[str, torch.Tensor]):
+        from iris_b200 import kernels as K
+
+        self._K = K
+        self.tensors = tensors
+        handles = {name: K.ipc_export(t) for name, t in tensors.items()}
+        everyone = comm.all_gather_object(handles)
+        self._bases: dict[bytes, int] = {}
+        self.ptrs: dict[str, list[int]] = {name: [] for name in tensors}
+        for j, theirs in enumerate(everyone):
+            for name in tensors:
+                handle, offset = theirs[name]
+                if j == comm.rank:
+                    self.ptrs[name].append(tensors[name].data_ptr())
+                    continue
+                base = self._bases.get(handle)
+                if base is None:
+                    base = self._bases[handle] = K.ipc_import(handle)
+                self.ptrs[name].append(base + offset)
+
+    def close(self) -> None:
+        for base in self._bases.values():
+            self._K.ipc_close(base)
+        self._bases.clear()
 
 
 @dataclass(frozen=True)

@@ -4,9 +4,15 @@
   keys, head-major Q/K/V with separate query / key lengths, and the
   token-range forms of patchify, pixel embed and the pixel head (bit-exact
   against slices of the whole-image calls);
-* the engine: P ranks as threads on one GPU (tests/thread_comm.py) against
-  the same model run without sequence parallelism, and P = 2 processes over
-  NCCL when the box has two GPUs.
+* the peer-memory exchange: the Q/K/V epilogue's scatter / broadcast and the
+  attention epilogue's scatter into other ranks' buffers, emulated on one GPU
+  by giving the kernels local buffers as the "peers" (each rank's launch runs
+  in turn); the barrier's bounded wait running out on a flag nothing sets; a
+  CUDA IPC round trip through a second process;
+* the engine: P ranks as threads on one GPU (tests/thread_comm.py, the
+  collective exchange) against the same model run without sequence
+  parallelism, and P = 2 processes (the peer-memory exchange) when the box has
+  two GPUs.
 """
 
 import os
@@ -102,6 +108,168 @@ def test_qkv_heads_head_major_and_key_length(iris):
     q2, k2, v2 = run(0, pad)
     assert torch.equal(q2, q0) and torch.equal(k2[:, :, :N], k0) and torch.equal(v2[:, :, :N], v0)
     assert torch.all(k2[:, :, N:] == 0)
+
+
+def _heads_problem_inputs(B, N, hq, hkv, K_dim, seed):
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    a = (0.5 * torch.randn(B * N, K_dim, device="cuda", generator=gen)).to(torch.bfloat16)
+    w = (0.05 * torch.randn((hq + 2 * hkv) * 128, K_dim, device="cuda", generator=gen)).to(torch.bfloat16)
+    qw, kw = (torch.rand(128, device="cuda", generator=gen) + 0.5 for _ in range(2))
+    cos, sin = (torch.randn(N, 64, device="cuda", generator=gen) for _ in range(2))
+    return a, w, qw, kw, cos, sin
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_heads_epilogue_scatters_to_owner_ranks(iris, world):
+    """Rank r's tokens, projected with the peer-scatter epilogue into every rank's
+    full-sequence buffers, equal the one-rank projection of all tokens sliced
+    by head group (the ranks' launches run in turn on one GPU)."""
+    from iris_b200 import _lib
+    from iris_b200 import kernels as K
+
+    B, n, hq, hkv, K_dim = 2, 136, 8, 4, 256
+    N = world * n
+    a, w, qw, kw, cos, sin = _heads_problem_inputs(B, N, hq, hkv, K_dim, world)
+    q_ref = torch.zeros(B, hq, N, 128, device="cuda", dtype=torch.bfloat16)
+    k_ref, v_ref = (torch.zeros(B, hkv, N, 128, device="cuda", dtype=torch.bfloat16) for _ in range(2))
+    ref = K.HeadsOut(q_ref, k_ref, v_ref, qw, kw, cos, sin, 1e-6, hq, hkv, N, B, N, N)
+    K.gemm_grouped([K.gemm_problem(a, w, None, heads=ref)], torch.cuda.current_stream().cuda_stream)
+    qf = [torch.zeros(B, hq // world, N, 128, device="cuda", dtype=torch.bfloat16) for _ in range(world)]
+    kf = [torch.zeros(B, hkv // world, N, 128, device="cuda", dtype=torch.bfloat16) for _ in range(world)]
+    vf = [torch.zeros_like(t) for t in kf]
+    for r in range(world):
+        rows = a.view(B, N, K_dim)[:, r * n : (r + 1) * n].reshape(B * n, K_dim).contiguous()
+        peers = K.PeerHeads(_lib.HEADS_PEER_SCATTER, [t.data_ptr() for t in qf], [t.data_ptr() for t in kf],
+                            [t.data_ptr() for t in vf], r * n, N)  # fmt: skip
+        heads = K.HeadsOut(None, None, None, qw, kw, cos[r * n :], sin[r * n :], 1e-6, hq, hkv, n, B, n, n,
+                           peers=peers)  # fmt: skip
+        K.gemm_grouped([K.gemm_problem(rows, w, None, heads=heads)], torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    for j in range(world):
+        hq_l, hkv_l = hq // world, hkv // world
+        assert rel_err(qf[j], q_ref[:, j * hq_l : (j + 1) * hq_l]) < 1e-3
+        assert rel_err(kf[j], k_ref[:, j * hkv_l : (j + 1) * hkv_l]) < 1e-3
+        assert rel_err(vf[j], v_ref[:, j * hkv_l : (j + 1) * hkv_l]) < 1e-3
+
+
+def test_heads_epilogue_broadcasts_keys_values(iris):
+    """Pixel-stage form: q stays local, k and v of this rank's tokens go to every
+    rank's full buffers at the rank's token offset."""
+    from iris_b200 import _lib
+    from iris_b200 import kernels as K
+
+    world, B, n, h, K_dim = 3, 2, 72, 2, 128
+    N = world * n
+    a, w, qw, kw, cos, sin = _heads_problem_inputs(B, N, h, h, K_dim, 11)
+    q_ref = torch.zeros(B, h, N, 128, device="cuda", dtype=torch.bfloat16)
+    k_ref, v_ref = (torch.zeros(B, h, N, 128, device="cuda", dtype=torch.bfloat16) for _ in range(2))
+    ref = K.HeadsOut(q_ref, k_ref, v_ref, qw, kw, cos, sin, 1e-6, h, h, N, B, N, N)
+    st = torch.cuda.current_stream().cuda_stream
+    K.gemm_grouped([K.gemm_problem(a, w, None, heads=ref)], st)
+    kf = [torch.zeros(B, h, N, 128, device="cuda", dtype=torch.bfloat16) for _ in range(world)]
+    vf = [torch.zeros_like(t) for t in kf]
+    qs = []
+    for r in range(world):
+        rows = a.view(B, N, K_dim)[:, r * n : (r + 1) * n].reshape(B * n, K_dim).contiguous()
+        q_loc = torch.zeros(B, h, n, 128, device="cuda", dtype=torch.bfloat16)
+        peers = K.PeerHeads(_lib.HEADS_PEER_BROADCAST_KV, None, [t.data_ptr() for t in kf],
+                            [t.data_ptr() for t in vf], r * n, N)  # fmt: skip
+        heads = K.HeadsOut(q_loc, None, None, qw, kw, cos[r * n :], sin[r * n :], 1e-6, h, h, n, B, n, N,
+                           peers=peers)  # fmt: skip
+        K.gemm_grouped([K.gemm_problem(rows, w, None, heads=heads)], st)
+        qs.append(q_loc)
+    torch.cuda.synchronize()
+    for j in range(world):
+        assert rel_err(kf[j], k_ref) < 1e-3 and rel_err(vf[j], v_ref) < 1e-3
+        assert rel_err(qs[j], q_ref[:, :, j * n : (j + 1) * n]) < 1e-3
+
+
+def test_attention_epilogue_scatters_rows_to_token_owners(iris):
+    """Attention of one rank's heads over every token, each output row stored into
+    the token rows of the rank that owns the token (at this rank's columns),
+    equals the plain output re-laid out."""
+    from iris_b200 import kernels as K
+
+    world, rank, B, hl, n = 2, 1, 2, 3, 160
+    H, N = world * hl, world * n
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    q, k, v = (torch.randn(B, hl, N, 128, device="cuda", generator=gen).to(torch.bfloat16) for _ in range(3))
+    ref = torch.empty(B, N, hl * 128, device="cuda", dtype=torch.bfloat16)
+    K.flash_attention(q, k, v, ref)
+    rows = [torch.zeros(B * n, H * 128, device="cuda", dtype=torch.bfloat16) for _ in range(world)]
+    K.flash_attention_peers(q, k, v, [t.data_ptr() for t in rows], n, rank * hl * 128, H * 128)
+    torch.cuda.synchronize()
+    for j in range(world):
+        got = rows[j].view(B, n, H * 128)[:, :, rank * hl * 128 : (rank + 1) * hl * 128]
+        assert torch.equal(got, ref[:, j * n : (j + 1) * n])
+        others = rows[j].view(B, n, H * 128)[:, :, : rank * hl * 128]
+        assert torch.all(others == 0)
+
+
+def test_peer_barrier_wait_runs_out_and_reports(iris):
+    """The barrier signals the peer's slot and, with no peer to answer, its bounded
+    wait gives up and sets the device error bit; with the peer's flag already
+    set it returns without one. (No second GPU: the "peer" is a local buffer.)"""
+    from iris_b200 import kernels as K
+
+    K.device_error(clear=True)
+    flags = torch.zeros(2, dtype=torch.int32, device="cuda")
+    peer = torch.zeros(2, dtype=torch.int32, device="cuda")
+    K.peer_barrier(flags, [0, peer.data_ptr()], 0, 7, timeout_s=0.02)
+    assert K.device_error(clear=True) & 1, "the wait on a flag nothing sets must time out"
+    assert int(peer[0]) == 7, "the barrier must signal the peer's slot for this rank"
+    flags[1] = 9
+    K.peer_barrier(flags, [0, peer.data_ptr()], 0, 8, timeout_s=0.02)
+    assert K.device_error(clear=True) == 0 and int(peer[0]) == 8
+
+
+def _ipc_child(handle, offset, numel, queue):
+    import torch
+
+    from iris_b200 import kernels as K
+
+    torch.cuda.set_device(0)
+    base = K.ipc_import(handle)
+    out = torch.empty(numel, dtype=torch.float32, device="cuda")
+    # read the parent's buffer through the mapping, then write into it
+    K.block_copy(out.view(torch.uint8), (0, 0, 0), _raw(base + offset, numel * 4), (0, 0, 0), (1, 1, 1), numel * 4)
+    K.block_copy(_raw(base + offset, numel * 4), (0, 0, 0), (out * 2).view(torch.uint8), (0, 0, 0), (1, 1, 1),
+                 numel * 4)  # fmt: skip
+    torch.cuda.synchronize()
+    K.ipc_close(base)
+    queue.put(float(out.sum()))
+
+
+def _raw(ptr, nbytes):
+    """A uint8 CUDA tensor viewing device memory at ``ptr`` (no ownership)."""
+    import torch
+
+    class _Mem:
+        __cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 3}
+
+    return torch.as_tensor(_Mem(), device="cuda")
+
+
+def test_ipc_round_trip_through_a_second_process(iris):
+    import torch.multiprocessing as mp
+
+    from iris_b200 import kernels as K
+
+    pool = torch.empty(1 << 20, dtype=torch.float32, device="cuda")
+    buf = pool[4096 : 4096 + 1000]
+    buf.copy_(torch.arange(1000, dtype=torch.float32, device="cuda"))
+    torch.cuda.synchronize()
+    handle, offset = K.ipc_export(buf)
+    # the offset is from the base of the allocation holding the buffer (at or below the pool's start)
+    assert offset >= buf.data_ptr() - pool.data_ptr() and len(handle) == 64
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    proc = ctx.Process(target=_ipc_child, args=(handle, offset, 1000, queue))
+    proc.start()
+    proc.join(timeout=120)
+    assert proc.exitcode == 0
+    assert queue.get(timeout=10) == float(sum(range(1000)))
+    assert torch.equal(buf, 2 * torch.arange(1000, dtype=torch.float32, device="cuda"))
 
 
 def test_token_range_layout_kernels_match_whole_image(iris):
