@@ -102,6 +102,25 @@ def test_euler_cfg_sample_matches_reference(iris):
     assert value >= PSNR_MIN
 
 
+def test_turbo_four_step_sample_without_cfg(iris):
+    """The Turbo loop (generate_few_step, src/iris3b/sampling.py:98-138: four
+    deterministic Euler steps at TURBO_SIGMAS, no CFG) on the engine against
+    the fp32 oracle model run through the oracle's loop on the CPU."""
+    fx = golden("released_mha")
+    cfg = _config(fx["config"])
+    params = seeded_init(cfg, seed=0)
+    engine = _engine(iris, cfg, params)
+    s = fx["euler_cfg"]
+    noise, cond = s["noise"], s["cond"]
+    sample = iris.euler_cfg(engine, noise.cuda(), cond.cuda(), None)
+    oracle = OracleModel(cfg, params)
+    with torch.no_grad():
+        want = oracle_euler(lambda x, t, y: oracle.forward(x, t, y), noise, cond, None)
+    value = psnr(sample, want)
+    print(f"turbo (no CFG) 4-step sample: psnr {value:.1f} dB")
+    assert value > PSNR_MIN
+
+
 def test_non_square_grid_and_odd_batch(iris):
     fx = golden("released_gqa")  # 24 x 16 input: a 6 x 4 patch grid
     cfg = _config(fx["config"])
