@@ -7,6 +7,9 @@
 // The reference runs on one device; this has no counterpart there.
 #include <cudaTypedefs.h>
 
+#include <cstring>
+#include <mutex>
+
 #include "common.cuh"
 #include "iris_abi_internal.h"
 
@@ -54,15 +57,14 @@ __global__ void barrier_kernel(unsigned int* __restrict__ flags, PeerFlags peers
 
 PFN_cuMemGetAddressRange_v3020 range_fn() {
   static PFN_cuMemGetAddressRange_v3020 fn = nullptr;
-  static bool looked = false;
-  if (!looked) {
+  static std::once_flag once;
+  std::call_once(once, [] {
     void* ptr = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
       fn = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(ptr);
-    looked = true;
-  }
+  });
   return fn;
 }
 

@@ -611,6 +611,14 @@ class CudaIris:
         ]
         K.gemm_grouped(problems, st)
 
+    def close(self) -> None:
+        """Unmap the other ranks' exchange buffers (sequence parallelism over
+        processes); the engine stays usable and maps them again when needed."""
+        for ws in self._work.values():
+            if "_peers" in ws:
+                ws["_peers"].close()
+        self._work.clear()
+
     def _barrier(self, ws) -> None:
         """All ranks' work enqueued so far (their stores into this rank's buffers
         included) completes before this rank's next kernel; bounded wait."""
