@@ -108,3 +108,52 @@ def test_exchanges_over_gloo_two_processes():
     assert all(p.exitcode == 0 for p in procs)
     results = dict(queue.get(timeout=10) for _ in procs)
     assert results == {0: True, 1: True}
+
+
+def test_peer_buffers_map_each_peer_allocation_once(monkeypatch):
+    """PeerBuffers' host logic with the IPC calls replaced by fakes: this rank's
+    entries are its own pointers, every peer buffer is the mapped base of its
+    allocation plus the exported offset, an allocation holding several buffers
+    is mapped once, and close() unmaps each mapping once."""
+    from iris_b200 import kernels as K
+    from iris_b200.ulysses import PeerBuffers
+
+    class Buf:  # stands in for a device tensor: only data_ptr() is read
+        def __init__(self, ptr):
+            self.ptr = ptr
+
+        def data_ptr(self):
+            return self.ptr
+
+    world, rank = 3, 1
+    names = ("qf", "flags", "o_loc")
+    # rank r: "qf" and "flags" share allocation A_r, "o_loc" lives in allocation B_r
+    layout = {r: {"qf": (f"A{r}", 0), "flags": (f"A{r}", 4096), "o_loc": (f"B{r}", 256)} for r in range(world)}
+
+    class Comm:
+        def __init__(self):
+            self.rank, self.world = rank, world
+
+        def all_gather_object(self, obj):
+            return [{n: (layout[r][n][0].encode(), layout[r][n][1]) for n in names} if r != rank else obj
+                    for r in range(world)]  # fmt: skip
+
+    exported, imported, closed = [], [], []
+    monkeypatch.setattr(K, "ipc_export", lambda t: exported.append(t) or (b"mine", 0))
+    bases = {f"{a}{r}".encode(): 0x10000 * (r + 1) + (0x1000 if a == "B" else 0) for r in range(world) for a in "AB"}
+    monkeypatch.setattr(K, "ipc_import", lambda h: imported.append(h) or bases[h])
+    monkeypatch.setattr(K, "ipc_close", lambda base: closed.append(base))
+    local = {n: Buf(0x900000 + i * 0x100) for i, n in enumerate(names)}
+    pb = PeerBuffers(Comm(), local)
+    assert len(exported) == len(names)
+    for n in names:
+        assert pb.ptrs[n][rank] == local[n].data_ptr()
+        for r in range(world):
+            if r != rank:
+                alloc, off = layout[r][n]
+                assert pb.ptrs[n][r] == bases[alloc.encode()] + off
+    assert sorted(imported) == sorted({f"{a}{r}".encode() for r in range(world) if r != rank for a in "AB"})
+    pb.close()
+    assert sorted(closed) == sorted(bases[h] for h in imported)
+    pb.close()  # a second close unmaps nothing more
+    assert len(closed) == len(imported)
