@@ -225,14 +225,16 @@ def profile_run(kind: str) -> None:
     inside the NVTX range ``profiled`` (select it with ``--nvtx --nvtx-include
     profiled/``). ``forward``: the benchmark model. ``small``: the same shapes
     with one dual and one single-stream block and one pixel block (< 1 GB of
-    weights), for multi-pass captures."""
+    weights), for multi-pass captures. ``sampler``: the small model, and in the
+    range the 4-step guided Euler loop of one image (four B = 2 calls and the
+    fused CFG + Euler updates)."""
     from dataclasses import replace
 
     from iris_b200 import CudaIris, IrisWeights, baseline_step_config, synthetic_state
     from iris_b200.config import PixelStageConfig
 
     cfg = baseline_step_config()
-    if kind == "small":
+    if kind in ("small", "sampler"):
         cfg = replace(cfg, depth=2, dual_depth=1, pixel=PixelStageConfig(depth=1))
     device = torch.device("cuda", 0)
     engine = CudaIris(IrisWeights(cfg, synthetic_state(cfg, device, seed=0)))
@@ -244,7 +246,12 @@ def profile_run(kind: str) -> None:
         engine(x, t, text)
     torch.cuda.synchronize()
     torch.cuda.nvtx.range_push("profiled")
-    v = engine(x, t, text)
+    if kind == "sampler":
+        from iris_b200.sampling import euler_cfg
+
+        v = euler_cfg(engine, x[:1], text[1:], text[:1], cfg_scale=CFG_SCALE, sigmas=SIGMAS)
+    else:
+        v = engine(x, t, text)
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     print(json.dumps({"profile": kind, "finite": bool(torch.isfinite(v).all())}))
@@ -455,7 +462,7 @@ def main() -> None:
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", default="ours", choices=["ours", "reference"])
     parser.add_argument("--no-cpu-baseline", action="store_true")
-    parser.add_argument("--profile", choices=["forward", "small"], help="one NVTX-marked B=2 call for ncu")
+    parser.add_argument("--profile", choices=["forward", "small", "sampler"], help="NVTX-marked work for ncu")
     parser.add_argument("--workload", default="loop1024", choices=["loop1024", "step2048", "ops"])
     args = parser.parse_args()
     from iris_b200.parallel import env_world, gather_images, image_shard, init_process_group  # noqa: F401
