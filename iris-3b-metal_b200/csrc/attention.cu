@@ -87,40 +87,6 @@ IRIS_DEVICE float max3(float a, float b, float c) {
   return d;
 }
 
-// 2^x on the FMA pipe for x >= -126 (a share of the softmax exponentials, so
-// the MUFU unit is not the only source of them). Range reduction: adding
-// 1.5 * 2^23 rounds x to the nearest integer j, left in the low mantissa bits
-// of t; f = x - j lies in [-0.5, 0.5]. 2^f is a degree-3 polynomial whose
-// coefficients were fitted to 2^f on [-0.5, 0.5] by iteratively reweighted
-// least squares on the relative error (Lawson's algorithm; max relative error
-// 7.5e-5, far below the bf16 rounding of P). 2^j is added to the exponent field
-// as (bits of t) << 23, which equals j << 23 modulo 2^32.
-IRIS_DEVICE float2 exp2_poly2(float2 x) {
-  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
-  x.x = fmaxf(x.x, -126.f);
-  x.y = fmaxf(x.y, -126.f);
-  const float2 t = add2(x, make_float2(kRound, kRound));
-  const float2 j = add2(t, make_float2(-kRound, -kRound));
-  const float2 f = fma2(j, make_float2(-1.f, -1.f), x);
-  float2 p = fma2(f, make_float2(0.0551716685295105f, 0.0551716685295105f),
-                  make_float2(0.2426111400127411f, 0.2426111400127411f));
-  p = fma2(p, f, make_float2(0.6932609677314758f, 0.6932609677314758f));
-  p = fma2(p, f, make_float2(0.9999280571937561f, 0.9999280571937561f));
-  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
-                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
-}
-// Of every 16 exponential pairs, how many exp2_poly2 computes (the rest go to
-// MUFU). The polynomial costs ~6 issue slots per element against 1 for MUFU,
-// so it only pays when the MUFU pipe, not issue, limits the softmax.
-#ifndef IRIS_ATTN_EMU_PAIRS
-#define IRIS_ATTN_EMU_PAIRS 0
-#endif
-constexpr int EMU_PAIRS = IRIS_ATTN_EMU_PAIRS;
-// 1: scale/shift and row sums as packed f32x2 instructions; 0: scalar FFMA/FADD.
-#ifndef IRIS_ATTN_PACKED
-#define IRIS_ATTN_PACKED 1
-#endif
-
 __global__ void __launch_bounds__(THREADS, 1)
     flash_attn_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                       const __grid_constant__ CUtensorMap tv, const Params p) {
@@ -358,24 +324,10 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           const float2 sv = make_float2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
-#if IRIS_ATTN_PACKED
           const float2 x = fma2(sv, scale2, shift2);
-#else
-          const float2 x = make_float2(fmaf(sv.x, scale2.x, shift2.x), fmaf(sv.y, scale2.y, shift2.y));
-#endif
-          float2 pe;
-          if (e < EMU_PAIRS && !tail) {
-            pe = exp2_poly2(x);
-          } else {  // MUFU; also every masked key block, where ex2(-inf) gives exact zeros
-            pe.x = ex2(x.x);
-            pe.y = ex2(x.y);
-          }
-#if IRIS_ATTN_PACKED
+          // masked keys (-inf) give exact zeros
+          const float2 pe = make_float2(ex2(x.x), ex2(x.y));
           rs2 = add2(rs2, pe);
-#else
-          rs2.x += pe.x;
-          rs2.y += pe.y;
-#endif
           pk[e] = pack_bf16x2(pe.x, pe.y);
         }
         // chunk c's P goes to columns [16c, 16c + 16) of this half, scores already read
