@@ -165,8 +165,19 @@ IRIS_DEVICE uint32_t ld_bf16x2(const __nv_bfloat16* p) { return *reinterpret_cas
 // channel of slot j (0..3) for lane quad position c
 IRIS_DEVICE int frag_channel(int c, int j) { return 2 * c + (j & 1) + ((j >> 1) << 3); }
 
+// A tile's inputs for this lane (fragment layout: pixels g and g + 8, channel
+// pairs (2c, 2c+1) and (2c+8, 2c+9)): the pixels, the attention branch and the
+// four modulation pairs (scale1, shift1, scale2, shift2).
+struct TileIn {
+  float p[2][4];
+  uint32_t at[2][2];
+  uint32_t m[2][4][2];  // [half][scale1, shift1, scale2, shift2][channel pair]
+};
+
+constexpr int MMA_THREADS = 128;  // 4 warps per block, 2 blocks per SM
+
 template <bool F32, bool HEAD>
-__global__ void __launch_bounds__(THREADS) pixel_mlp_mma_kernel(
+__global__ void __launch_bounds__(MMA_THREADS, 2) pixel_mlp_mma_kernel(
     void* pixels, const __nv_bfloat16* __restrict__ branch, const __nv_bfloat16* __restrict__ mods,
     const float* __restrict__ nw, const __nv_bfloat16* __restrict__ w1, const __nv_bfloat16* __restrict__ b1,
     const __nv_bfloat16* __restrict__ w2, const __nv_bfloat16* __restrict__ b2, const float* __restrict__ nnw,
@@ -210,31 +221,43 @@ __global__ void __launch_bounds__(THREADS) pixel_mlp_mma_kernel(
   const int64_t gw = width / patch;
   const int64_t tiles = n / 16;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
-  for (int64_t tile = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5); tile < tiles;
-       tile += warps) {
-    float x[2][4], h[2][4];
+
+  // every load of a tile is issued at once (the next tile's while this one computes)
+  auto load_tile = [&](int64_t tile, TileIn& in) {
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       const int64_t px = tile * 16 + g + 8 * half;
       const __nv_bfloat16* md = mods + px * 4 * C;
 #pragma unroll
-      for (int jj = 0; jj < 2; ++jj) {  // channel pairs (2c, 2c+1) and (2c+8, 2c+9)
+      for (int jj = 0; jj < 2; ++jj) {
         const int ch = 2 * c + 8 * jj;
-        float p0, p1;
         if (F32) {
           const float2 pv = *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(pixels) + px * C + ch);
-          p0 = pv.x;
-          p1 = pv.y;
+          in.p[half][2 * jj] = pv.x;
+          in.p[half][2 * jj + 1] = pv.y;
         } else {
           const float2 pv = unpack_bf16x2(ld_bf16x2(reinterpret_cast<const __nv_bfloat16*>(pixels) + px * C + ch));
-          p0 = pv.x;
-          p1 = pv.y;
+          in.p[half][2 * jj] = pv.x;
+          in.p[half][2 * jj + 1] = pv.y;
         }
-        const float2 at = unpack_bf16x2(ld_bf16x2(branch + px * C + ch));
-        const float2 s1 = unpack_bf16x2(ld_bf16x2(md + ch));
-        const float2 t1 = unpack_bf16x2(ld_bf16x2(md + C + ch));
-        x[half][2 * jj] = r(p0 + r(at.x * (1.f + s1.x) + t1.x));
-        x[half][2 * jj + 1] = r(p1 + r(at.y * (1.f + s1.y) + t1.y));
+        in.at[half][jj] = ld_bf16x2(branch + px * C + ch);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) in.m[half][k][jj] = ld_bf16x2(md + k * C + ch);
+      }
+    }
+  };
+
+  auto process = [&](int64_t tile, const TileIn& in) {
+    float x[2][4], h[2][4];
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) {  // channel pairs (2c, 2c+1) and (2c+8, 2c+9)
+        const float2 at = unpack_bf16x2(in.at[half][jj]);
+        const float2 s1 = unpack_bf16x2(in.m[half][0][jj]);
+        const float2 t1 = unpack_bf16x2(in.m[half][1][jj]);
+        x[half][2 * jj] = r(in.p[half][2 * jj] + r(at.x * (1.f + s1.x) + t1.x));
+        x[half][2 * jj + 1] = r(in.p[half][2 * jj + 1] + r(at.y * (1.f + s1.y) + t1.y));
       }
       float ss = 0.f;
 #pragma unroll
@@ -273,12 +296,10 @@ __global__ void __launch_bounds__(THREADS) pixel_mlp_mma_kernel(
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       const int64_t px = tile * 16 + g + 8 * half;
-      const __nv_bfloat16* md = mods + px * 4 * C;
 #pragma unroll
       for (int jj = 0; jj < 2; ++jj) {
-        const int ch = 2 * c + 8 * jj;
-        const float2 s2 = unpack_bf16x2(ld_bf16x2(md + 2 * C + ch));
-        const float2 t2 = unpack_bf16x2(ld_bf16x2(md + 3 * C + ch));
+        const float2 s2 = unpack_bf16x2(in.m[half][2][jj]);
+        const float2 t2 = unpack_bf16x2(in.m[half][3][jj]);
         const float m0 = r(out[half][2 * jj] + bias2[2 * jj]), m1 = r(out[half][2 * jj + 1] + bias2[2 * jj + 1]);
         x[half][2 * jj] = r(x[half][2 * jj] + r(m0 * (1.f + s2.x) + t2.x));
         x[half][2 * jj + 1] = r(x[half][2 * jj + 1] + r(m1 * (1.f + s2.y) + t2.y));
@@ -322,6 +343,22 @@ __global__ void __launch_bounds__(THREADS) pixel_mlp_mma_kernel(
         }
       }
     }
+  };
+
+  // two tiles in flight per warp: buffers A and B alternate
+  int64_t tile = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+  TileIn ta, tb;
+  if (tile < tiles) load_tile(tile, ta);
+  while (tile < tiles) {
+    const int64_t t1 = tile + warps;
+    if (t1 < tiles) load_tile(t1, tb);
+    process(tile, ta);
+    tile = t1;
+    if (tile >= tiles) break;
+    const int64_t t2 = tile + warps;
+    if (t2 < tiles) load_tile(t2, ta);
+    process(tile, tb);
+    tile = t2;
   }
 }
 
@@ -457,10 +494,12 @@ inline unsigned grid_for(int64_t n) {
   return static_cast<unsigned>(blocks < cap ? blocks : cap);
 }
 
-// 16-pixel tiles, one per warp, 8 warps per block, grid-stride beyond 8 blocks / SM
+// 16-pixel tiles, one per warp, 4 warps per block, grid-stride beyond the
+// resident 2 blocks / SM (each warp keeps two tiles in flight; with 3 blocks
+// the 168-register cap spills and the B = 2 call shape runs 235 us against 215)
 inline unsigned mma_grid_for(int64_t n) {
-  const int64_t blocks = (n / 16 + THREADS / 32 - 1) / (THREADS / 32);
-  const int64_t cap = static_cast<int64_t>(num_sms()) * 8;
+  const int64_t blocks = (n / 16 + MMA_THREADS / 32 - 1) / (MMA_THREADS / 32);
+  const int64_t cap = static_cast<int64_t>(num_sms()) * 2;
   return static_cast<unsigned>(blocks < cap ? blocks : cap);
 }
 
@@ -506,11 +545,11 @@ extern "C" int iris_pixel_mlp(void* pixels, int pixel_dtype, const void* branch,
     const unsigned grid = mma_grid_for(n_pixels);
     auto nxt = reinterpret_cast<__nv_bfloat16*>(next_input);
     if (pixel_dtype == IRIS_F32)
-      pixel_mlp_mma_kernel<true, false><<<grid, THREADS, 0, st>>>(
+      pixel_mlp_mma_kernel<true, false><<<grid, MMA_THREADS, 0, st>>>(
           pixels, bf(branch), bf(mods), norm_weight, bf(fc1_w), bf(fc1_b), bf(fc2_w), bf(fc2_b), next_norm_weight,
           nxt, nullptr, nullptr, nullptr, n_pixels, 16, 16, 16, 0, 1, eps);
     else
-      pixel_mlp_mma_kernel<false, false><<<grid, THREADS, 0, st>>>(
+      pixel_mlp_mma_kernel<false, false><<<grid, MMA_THREADS, 0, st>>>(
           pixels, bf(branch), bf(mods), norm_weight, bf(fc1_w), bf(fc1_b), bf(fc2_w), bf(fc2_b), next_norm_weight,
           nxt, nullptr, nullptr, nullptr, n_pixels, 16, 16, 16, 0, 1, eps);
     IRIS_CUDA(cudaGetLastError());
@@ -549,11 +588,11 @@ extern "C" int iris_pixel_mlp_head(void* pixels, int pixel_dtype, const void* br
     const unsigned grid = mma_grid_for(n);
     const int pt = static_cast<int>(patch);
     if (pixel_dtype == IRIS_F32)
-      pixel_mlp_mma_kernel<true, true><<<grid, THREADS, 0, st>>>(
+      pixel_mlp_mma_kernel<true, true><<<grid, MMA_THREADS, 0, st>>>(
           pixels, bf(branch), bf(mods), norm_weight, bf(fc1_w), bf(fc1_b), bf(fc2_w), bf(fc2_b), final_norm_weight,
           nullptr, final_w, final_b, v, n, height, width, pt, token_start, tokens, eps);
     else
-      pixel_mlp_mma_kernel<false, true><<<grid, THREADS, 0, st>>>(
+      pixel_mlp_mma_kernel<false, true><<<grid, MMA_THREADS, 0, st>>>(
           pixels, bf(branch), bf(mods), norm_weight, bf(fc1_w), bf(fc1_b), bf(fc2_w), bf(fc2_b), final_norm_weight,
           nullptr, final_w, final_b, v, n, height, width, pt, token_start, tokens, eps);
     IRIS_CUDA(cudaGetLastError());
