@@ -174,10 +174,15 @@ struct TileIn {
   uint32_t m[2][4][2];  // [half][scale1, shift1, scale2, shift2][channel pair]
 };
 
-constexpr int MMA_THREADS = 128;  // 4 warps per block, 2 blocks per SM
+constexpr int MMA_THREADS = 128;  // 4 warps per block
+// Resident blocks per SM: the intermediate blocks keep two tiles in flight per
+// warp (2 blocks / SM; with 3 the 168-register cap spills and 2.1 M pixels take
+// 235 us against 215); the head (FinalLayer + fold, whose tail per tile is
+// longer) takes one tile at a time at 4 blocks / SM.
+__host__ __device__ constexpr int mma_blocks_per_sm(bool head) { return head ? 4 : 2; }
 
 template <bool F32, bool HEAD>
-__global__ void __launch_bounds__(MMA_THREADS, 2) pixel_mlp_mma_kernel(
+__global__ void __launch_bounds__(MMA_THREADS, mma_blocks_per_sm(HEAD)) pixel_mlp_mma_kernel(
     void* pixels, const __nv_bfloat16* __restrict__ branch, const __nv_bfloat16* __restrict__ mods,
     const float* __restrict__ nw, const __nv_bfloat16* __restrict__ w1, const __nv_bfloat16* __restrict__ b1,
     const __nv_bfloat16* __restrict__ w2, const __nv_bfloat16* __restrict__ b2, const float* __restrict__ nnw,
@@ -345,9 +350,16 @@ __global__ void __launch_bounds__(MMA_THREADS, 2) pixel_mlp_mma_kernel(
     }
   };
 
-  // two tiles in flight per warp: buffers A and B alternate
   int64_t tile = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
   TileIn ta, tb;
+  if constexpr (HEAD) {  // one tile at a time, its loads issued together
+    for (; tile < tiles; tile += warps) {
+      load_tile(tile, ta);
+      process(tile, ta);
+    }
+    return;
+  }
+  // two tiles in flight per warp: buffers A and B alternate
   if (tile < tiles) load_tile(tile, ta);
   while (tile < tiles) {
     const int64_t t1 = tile + warps;
@@ -495,11 +507,10 @@ inline unsigned grid_for(int64_t n) {
 }
 
 // 16-pixel tiles, one per warp, 4 warps per block, grid-stride beyond the
-// resident 2 blocks / SM (each warp keeps two tiles in flight; with 3 blocks
-// the 168-register cap spills and the B = 2 call shape runs 235 us against 215)
-inline unsigned mma_grid_for(int64_t n) {
+// resident blocks (mma_blocks_per_sm)
+inline unsigned mma_grid_for(int64_t n, bool head) {
   const int64_t blocks = (n / 16 + MMA_THREADS / 32 - 1) / (MMA_THREADS / 32);
-  const int64_t cap = static_cast<int64_t>(num_sms()) * 2;
+  const int64_t cap = static_cast<int64_t>(num_sms()) * mma_blocks_per_sm(head);
   return static_cast<unsigned>(blocks < cap ? blocks : cap);
 }
 
@@ -542,7 +553,7 @@ extern "C" int iris_pixel_mlp(void* pixels, int pixel_dtype, const void* branch,
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   auto bf = [](const void* p) { return reinterpret_cast<const __nv_bfloat16*>(p); };
   if (n_pixels % 16 == 0) {  // whole 16-pixel tiles: tensor-core MLP
-    const unsigned grid = mma_grid_for(n_pixels);
+    const unsigned grid = mma_grid_for(n_pixels, false);
     auto nxt = reinterpret_cast<__nv_bfloat16*>(next_input);
     if (pixel_dtype == IRIS_F32)
       pixel_mlp_mma_kernel<true, false><<<grid, MMA_THREADS, 0, st>>>(
@@ -585,7 +596,7 @@ extern "C" int iris_pixel_mlp_head(void* pixels, int pixel_dtype, const void* br
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   auto bf = [](const void* p) { return reinterpret_cast<const __nv_bfloat16*>(p); };
   if (n % 16 == 0) {  // whole 16-pixel tiles: tensor-core MLP
-    const unsigned grid = mma_grid_for(n);
+    const unsigned grid = mma_grid_for(n, true);
     const int pt = static_cast<int>(patch);
     if (pixel_dtype == IRIS_F32)
       pixel_mlp_mma_kernel<true, true><<<grid, MMA_THREADS, 0, st>>>(
