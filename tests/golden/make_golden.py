@@ -134,6 +134,66 @@ def _sample_fixture(model, fixture, cfg_scale=3.0, cfg_interval=(0.0, 1.5)):
             "sample": seen[0]}
 
 
+def _turbo_fixture(model, fixture):
+    """The Turbo recipe (``IrisPipeline._turbo``, ``src/iris_metal/pipeline.py:372-428``)
+    on the toy model: every Linear weight and bias stored in BF16
+    (``linear_dtypes`` with a BF16 trunk, ``src/iris_metal/loading.py:20-38``), every
+    other parameter FP32, the forward under BF16 autocast with prepared text and
+    the shared_bias cores evaluated once per forward; the reference's own
+    ``generate_few_step`` (B = 1, no CFG, TURBO_SIGMAS). The same loop is also run
+    in FP32 on the same BF16-valued weights: the exact arithmetic that both the
+    autocast forward and the CUDA engine approximate. Each autocast step's input is
+    also kept, with its velocity under autocast and in FP32."""
+    import copy
+
+    from iris3b.sampling import generate_few_step
+    from iris_metal.loading import linear_dtypes
+    from iris_metal.turbo import TURBO_SIGMAS
+
+    turbo = copy.deepcopy(model)
+    linear = linear_dtypes(turbo, torch.bfloat16)
+    with torch.no_grad():
+        for name, p in turbo.named_parameters():
+            if name in linear:
+                p.data = p.data.to(linear[name])
+    exact = copy.deepcopy(turbo).float()
+    cond = fixture["prepared_text"][1:]
+    noise = torch.randn(1, 3, fixture["x"].shape[2], fixture["x"].shape[3], generator=torch.Generator().manual_seed(6))
+
+    def run(net, autocast, calls=None):
+        class Model:
+            cfg = net.cfg
+
+            def parameters(self):
+                return net.parameters()
+
+            def __call__(self, x, t, y, y_mask):
+                out = net(x, t, y, y_mask=y_mask, prepared_text=cond, precompute_modulation=True)
+                if calls is not None:
+                    calls.append((x.clone(), t.clone(), out.x.float()))
+                return out
+
+        class Encoder:
+            def encode(self, prompts):
+                return SimpleNamespace(embeddings=cond, mask=torch.ones(1, cond.shape[1]))
+
+        seen = []
+        with torch.no_grad(), torch.autocast("cpu", dtype=torch.bfloat16, enabled=autocast):
+            generate_few_step(Model(), Encoder(), ["p"], noise.shape[2], noise.shape[3], list(TURBO_SIGMAS),
+                              noise=noise, device="cpu", check=seen.append)  # fmt: skip
+        return seen[0].float()
+
+    calls = []
+    sample = run(turbo, True, calls)
+    steps = []
+    with torch.no_grad():
+        for x, t, v in calls:  # each step's input, also through the FP32 forward
+            exact_v = exact(x, t, cond, prepared_text=cond, precompute_modulation=True).x
+            steps.append({"x": x, "t": t, "v_autocast": v, "v_fp32": exact_v})
+    return {"noise": noise, "cond": cond, "linear": sorted(linear), "autocast": sample, "fp32": run(exact, False),
+            "steps": steps}
+
+
 def _op_fixtures():
     from iris3b.nn.embeddings import TimestepEmbedder, sincos_pos_embed_2d
     from iris3b.nn.rope import apply_rope, rope_1d, rope_2d
@@ -239,6 +299,7 @@ def main():
         fixture, model = _model_fixture(name, cfg, ModelConfig, PixelStageConfig, IrisDiT, batch, h, w, times)
         if name == "released_mha":
             fixture["euler_cfg"] = _sample_fixture(model, fixture)
+            fixture["turbo"] = _turbo_fixture(model, fixture)
         torch.save(fixture, HERE / f"{name}.pt")
         print(name, "saved", tuple(fixture["v"].shape), float(fixture["v"].abs().max()))
     torch.save(_op_fixtures(), HERE / "ops.pt")

@@ -121,6 +121,36 @@ def test_turbo_four_step_sample_without_cfg(iris):
     assert value > PSNR_MIN
 
 
+def test_turbo_recipe_matches_reference_autocast(iris):
+    """Turbo (src/iris_metal/pipeline.py:372-428): BF16-stored Linear weights,
+    the upstream forward under BF16 autocast. The engine keeps FP32 residuals and
+    accumulators instead of autocast's BF16 activations, so it is re-validated
+    rather than bit-matched: at every step's input its velocity must be within
+    the per-op tolerance of the reference's autocast velocity and at most a
+    quarter as far from the FP32 forward on the same weights as autocast itself
+    is (on B200: 3.1e-4 to 3.5e-4 against autocast's 5.6e-3 to 6.3e-3); the
+    4-step sample above PSNR_MIN against the autocast sample (88.5 dB)."""
+    from test_oracle import turbo_params
+
+    fx = golden("released_mha")
+    cfg = _config(fx["config"])
+    tb = fx["turbo"]
+    engine = _engine(iris, cfg, turbo_params(cfg, set(tb["linear"])))
+    cond = tb["cond"].cuda()
+    for step in tb["steps"]:
+        v = engine(step["x"].cuda(), step["t"].cuda(), cond)
+        to_autocast, to_fp32 = rel_err(v, step["v_autocast"]), rel_err(v, step["v_fp32"])
+        autocast_to_fp32 = rel_err(step["v_autocast"], step["v_fp32"])
+        print(f"t={float(step['t'][0]):.0f}: engine-autocast {to_autocast:.2e}, engine-fp32 {to_fp32:.2e}, "
+              f"autocast-fp32 {autocast_to_fp32:.2e}")  # fmt: skip
+        assert to_autocast < REL_TOL
+        assert to_fp32 < 0.25 * autocast_to_fp32
+    sample = iris.euler_cfg(engine, tb["noise"].cuda(), cond, None)
+    value = psnr(sample, tb["autocast"])
+    print(f"turbo sample: psnr {value:.1f} dB against autocast")
+    assert value > PSNR_MIN
+
+
 def test_non_square_grid_and_odd_batch(iris):
     fx = golden("released_gqa")  # 24 x 16 input: a 6 x 4 patch grid
     cfg = _config(fx["config"])

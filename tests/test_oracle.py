@@ -49,6 +49,31 @@ def test_oracle_euler_cfg_matches_reference():
     torch.testing.assert_close(sample, s["sample"], rtol=1e-4, atol=1e-5)
 
 
+def turbo_params(cfg, linear):
+    """Seeded weights with every Linear weight and bias rounded to BF16: the
+    values a Turbo checkpoint stores (src/iris_metal/loading.py:20-38)."""
+    params = seeded_init(cfg, seed=0)
+    return {n: (p.to(torch.bfloat16).float() if n in linear else p) for n, p in params.items()}
+
+
+def test_oracle_turbo_recipe_matches_reference():
+    """The FP32 forward on Turbo-rounded weights reproduces the reference's FP32
+    run of the Turbo loop, per step and for the sample; the reference's own
+    autocast run stays within 1e-2 of it (its BF16 rounding)."""
+    fx = golden("released_mha")
+    cfg = _config(fx["config"])
+    tb = fx["turbo"]
+    model = OracleModel(cfg, turbo_params(cfg, set(tb["linear"])))
+    with torch.no_grad():
+        for step in tb["steps"]:
+            v = model(step["x"], step["t"], tb["cond"])
+            torch.testing.assert_close(v, step["v_fp32"], rtol=1e-4, atol=1e-5)
+            rel = float((step["v_autocast"] - v).abs().max() / v.abs().max())
+            assert 0 < rel < 1e-2
+        sample = euler_cfg(model, tb["noise"], tb["cond"], None)
+    torch.testing.assert_close(sample, tb["fp32"], rtol=1e-4, atol=1e-5)
+
+
 def test_oracle_dpm_solver_matches_reference():
     fx = golden("samplers")
     z, cond, uncond = fx["inputs"]["z"], fx["inputs"]["cond"], fx["inputs"]["uncond"]
