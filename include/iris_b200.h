@@ -268,11 +268,13 @@ int iris_pixel_mlp_head(void* pixels, int pixel_dtype, const void* branch, const
  * block's pixel_rms_norm, for patch tokens l in [token_start, token_start +
  * tokens): pixels[(b, l - token_start), ky * p + kx, :] = W x[b, :, y, x] +
  * bias + pos[y * W + x, :] (pos may be null); normed = bf16
- * rms_norm(pixels) * norm_weight. d_pix == 16, channels == 3. */
+ * rms_norm(pixels) * norm_weight. d_pix == 16; W is [16, channels], 1 to 4
+ * input channels (3, or 4 for the depth fine-tune's widened embedder,
+ * src/iris3b/downstream/depth.py:30-38). */
 int iris_pixel_embed(const float* x, const float* w, const float* bias, const float* pos, void* pixels,
                      int pixel_dtype, void* normed, const float* norm_weight, float eps, int64_t batch,
-                     int64_t height, int64_t width, int64_t patch, int64_t token_start, int64_t tokens,
-                     void* stream);
+                     int64_t channels, int64_t height, int64_t width, int64_t patch, int64_t token_start,
+                     int64_t tokens, void* stream);
 
 /* ---- layout and conditioning -------------------------------------------- */
 /* Patchify, src/iris_metal/model.py:188 / F.unfold in dit.py:326, for patch

@@ -17,6 +17,9 @@ namespace pixel {
 
 constexpr int C = 16;
 constexpr int HID = 64;
+// RGB, plus the extra input channel of the depth fine-tune's widened embedders
+// (src/iris3b/downstream/depth.py:30-38)
+constexpr int MAX_IN_CHANNELS = 4;
 constexpr int THREADS = 256;
 
 IRIS_DEVICE void load16(const void* p, int64_t i, bool f32, float (&x)[C]) {
@@ -453,13 +456,16 @@ __global__ void __launch_bounds__(THREADS) pixel_embed_kernel(const float* __res
                                                                const float* __restrict__ pos, void* pixels, bool f32,
                                                                __nv_bfloat16* __restrict__ normed,
                                                                const float* __restrict__ nw, float eps, int64_t n,
-                                                               int64_t height, int64_t width, int patch,
-                                                               int64_t token_start, int64_t tokens) {
-  __shared__ float sw[3 * C + C + C];
-  for (int i = threadIdx.x; i < 3 * C; i += blockDim.x) sw[i] = w[i];
+                                                               int channels, int64_t height, int64_t width,
+                                                               int patch, int64_t token_start, int64_t tokens) {
+  // W [16, channels] (nn.Linear layout), then the bias and the norm gain
+  __shared__ float sw[MAX_IN_CHANNELS * C + C + C];
+  float* sb = sw + MAX_IN_CHANNELS * C;
+  float* sn = sb + C;
+  for (int i = threadIdx.x; i < channels * C; i += blockDim.x) sw[i] = w[i];
   for (int i = threadIdx.x; i < C; i += blockDim.x) {
-    sw[3 * C + i] = bias[i];
-    sw[4 * C + i] = nw[i];
+    sb[i] = bias[i];
+    sn[i] = nw[i];
   }
   __syncthreads();
   const int pp = patch * patch;
@@ -471,13 +477,20 @@ __global__ void __launch_bounds__(THREADS) pixel_embed_kernel(const float* __res
     const int k = static_cast<int>(i % pp);
     const int64_t b = patch_idx / tokens, l = token_start + patch_idx % tokens;
     const int64_t y = (l / gw) * patch + k / patch, xx = (l % gw) * patch + k % patch;
-    const float* xp = x + b * 3 * plane + y * width + xx;
-    const float x0 = xp[0], x1 = xp[plane], x2 = xp[2 * plane];
+    const float* xp = x + b * channels * plane + y * width + xx;
+    float xin[MAX_IN_CHANNELS];
+#pragma unroll
+    for (int k = 0; k < MAX_IN_CHANNELS; ++k) xin[k] = k < channels ? xp[k * plane] : 0.f;
     float o[C];
 #pragma unroll
     for (int c = 0; c < C; ++c) {
-      // F.linear(x, W, b): sum over the 3 input channels, then the bias
-      o[c] = fmaf(x2, sw[c * 3 + 2], fmaf(x1, sw[c * 3 + 1], x0 * sw[c * 3])) + sw[3 * C + c];
+      // F.linear(x, W, b): sum over the input channels in order, then the bias
+      const float* wc = sw + c * channels;
+      float acc = xin[0] * wc[0];
+#pragma unroll
+      for (int k = 1; k < MAX_IN_CHANNELS; ++k)
+        if (k < channels) acc = fmaf(xin[k], wc[k], acc);
+      o[c] = acc + sb[c];
     }
     if (pos != nullptr) {
       const float4* p4 = reinterpret_cast<const float4*>(pos + (y * width + xx) * C);
@@ -495,7 +508,7 @@ __global__ void __launch_bounds__(THREADS) pixel_embed_kernel(const float* __res
     const float inv = inv_rms16(o, eps);
     float h[C];
 #pragma unroll
-    for (int c = 0; c < C; ++c) h[c] = o[c] * inv * sw[4 * C + c];
+    for (int c = 0; c < C; ++c) h[c] = o[c] * inv * sn[c];
     store16(normed, i, false, h);
   }
 }
@@ -623,10 +636,11 @@ extern "C" int iris_pixel_mlp_head(void* pixels, int pixel_dtype, const void* br
 
 extern "C" int iris_pixel_embed(const float* x, const float* w, const float* bias, const float* pos, void* pixels,
                                 int pixel_dtype, void* normed, const float* norm_weight, float eps, int64_t batch,
-                                int64_t height, int64_t width, int64_t patch, int64_t token_start, int64_t tokens,
-                                void* stream) {
+                                int64_t channels, int64_t height, int64_t width, int64_t patch, int64_t token_start,
+                                int64_t tokens, void* stream) {
   using namespace iris::pixel;
   IRIS_REQUIRE(x && w && bias && pixels && normed && norm_weight, "pixel_embed: null pointer");
+  IRIS_REQUIRE(channels >= 1 && channels <= MAX_IN_CHANNELS, "pixel_embed: 1 to 4 input channels");
   IRIS_REQUIRE(pixel_dtype == IRIS_F32 || pixel_dtype == IRIS_BF16, "pixel_embed: pixels must be f32 or bf16");
   IRIS_REQUIRE(patch > 0 && height % patch == 0 && width % patch == 0 && batch >= 0, "pixel_embed: bad geometry");
   IRIS_REQUIRE(aligned16(pixels) && aligned16(normed) && (pos == nullptr || aligned16(pos)), "pixel_embed: alignment");
@@ -636,7 +650,7 @@ extern "C" int iris_pixel_embed(const float* x, const float* w, const float* bia
   if (n == 0) return IRIS_OK;
   pixel_embed_kernel<<<grid_for(n), THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
       x, w, bias, pos, pixels, pixel_dtype == IRIS_F32, reinterpret_cast<__nv_bfloat16*>(normed), norm_weight, eps, n,
-      height, width, static_cast<int>(patch), token_start, tokens);
+      static_cast<int>(channels), height, width, static_cast<int>(patch), token_start, tokens);
   IRIS_CUDA(cudaGetLastError());
   return IRIS_OK;
 }

@@ -37,7 +37,7 @@ SIGNATURES: dict[str, list] = {
     "iris_pixel_rms_norm": [P, I32, P, P, I64, F, P],
     "iris_pixel_mlp": [P, I32, P, P, P, P, P, P, P, P, P, I64, F, P],
     "iris_pixel_mlp_head": [P, I32, P, P, P, P, P, P, P, P, P, P, P, I64, I64, I64, I64, I64, I64, F, P],
-    "iris_pixel_embed": [P, P, P, P, P, I32, P, P, F, I64, I64, I64, I64, I64, I64, P],
+    "iris_pixel_embed": [P, P, P, P, P, I32, P, P, F, I64, I64, I64, I64, I64, I64, I64, P],
     "iris_patchify": [P, P, I64, I64, I64, I64, I64, I64, I64, P],
     "iris_block_copy": [P, I64, I64, I64, P, I64, I64, I64, I64, I64, I64, I64, P],
     "iris_unpatchify": [P, P, I64, I64, I64, I64, I64, P],

@@ -192,9 +192,16 @@ class CudaIris:
         def swiglu(prefix):
             return pack_swiglu(bf(f"{prefix}.w1.weight"), bf(f"{prefix}.w3.weight"), bf(f"{prefix}.w2.weight"))
 
-        if (cfg.in_channels * cfg.patch_size**2) % 8:
-            raise ValueError("CudaIris needs in_channels * patch_size^2 to be a multiple of 8")
         self.s_embed = (bf("s_embedder.proj.weight"), f32("s_embedder.proj.bias"))
+        # input channels from the patch embedder: cfg.in_channels, or one more for
+        # task exports with a widened embedder (src/iris3b/downstream/depth.py:30-38);
+        # the velocity keeps the final layer's cfg.in_channels
+        pp = cfg.patch_size**2
+        self.in_channels = self.s_embed[0].shape[1] // pp
+        if self.s_embed[0].shape[1] != self.in_channels * pp or not 1 <= self.in_channels <= 4:
+            raise ValueError("CudaIris: s_embedder.proj takes 1 to 4 channels of patch_size^2 pixels")
+        if (self.in_channels * pp) % 8:
+            raise ValueError("CudaIris needs in_channels * patch_size^2 to be a multiple of 8")
         self.t_mlp = [(f32(f"t_embedder.mlp.{i}.weight"), f32(f"t_embedder.mlp.{i}.bias")) for i in (0, 2)]
         self.cores = {s: (f32(f"modulation_cores.adaln_{s}.weight"), f32(f"modulation_cores.adaln_{s}.bias"))
                       for s in ("img", "txt")}  # fmt: skip
@@ -259,6 +266,8 @@ class CudaIris:
         self.txt_bias = torch.stack(txt_bias).contiguous() if txt_bias else None
         pix = cfg.pixel
         self.pixel_embed_w = (f32("pixel_embedder.proj.weight"), f32("pixel_embedder.proj.bias"))
+        if tuple(self.pixel_embed_w[0].shape) != (pix.hidden_size, self.in_channels):
+            raise ValueError("CudaIris: pixel_embedder.proj must take the patch embedder's input channels")
         self.pixel_blocks = []
         for i in range(pix.depth):
             b = f"pixel_blocks.{i}"
@@ -277,6 +286,8 @@ class CudaIris:
                 }
             )
         self.final = (f32("final_layer.norm.weight"), f32("final_layer.linear.weight"), f32("final_layer.linear.bias"))
+        if tuple(self.final[1].shape) != (3, pix.hidden_size):
+            raise ValueError("CudaIris: the final layer must emit 3 channels per pixel")
         self.text_adapter = None
         if cfg.text_adapter == "linear" and "y_embedder.proj.weight" in state:
             self.text_adapter = (
@@ -434,8 +445,8 @@ class CudaIris:
         batch, channels, height, width = x.shape
         if height % p or width % p:
             raise ValueError(f"input {height}x{width} is not divisible by patch_size {p}")
-        if channels != cfg.in_channels:
-            raise ValueError(f"expected {cfg.in_channels} input channels, got {channels}")
+        if channels != self.in_channels:
+            raise ValueError(f"expected {self.in_channels} input channels, got {channels}")
         if text.shape[0] != batch or text.shape[2] != cfg.hidden_size:
             raise ValueError("text must be [B, T, hidden_size] for the same batch as x")
         grid = (height // p, width // p)
@@ -493,10 +504,11 @@ class CudaIris:
             capture["s_cond"] = ws["s_cond"].float().clone()
 
         # pixel stage
+        out_channels = cfg.in_channels  # 3, also for task models with an extra input channel
         if comm is None:
-            v = torch.empty(batch, channels, height, width, device=dev, dtype=torch.float32)
+            v = torch.empty(batch, out_channels, height, width, device=dev, dtype=torch.float32)
         else:  # every rank writes its own patches; the sum assembles the image
-            v = torch.zeros(batch, channels, height, width, device=dev, dtype=torch.float32)
+            v = torch.zeros(batch, out_channels, height, width, device=dev, dtype=torch.float32)
         self._pixel_stage(x, ws, geom, grid, pcos, psin, pos, v, eps, st, capture)
         if comm is not None:
             comm.all_reduce_sum(v)
@@ -685,8 +697,8 @@ class CudaIris:
         blocks = self.pixel_blocks
         _lib.call(
             "iris_pixel_embed", x.data_ptr(), pw.data_ptr(), pb.data_ptr(), None if pos is None else pos.data_ptr(),
-            ws["pixels"].data_ptr(), pdt, ws["ph"].data_ptr(), blocks[0]["norm1"].data_ptr(), eps, g.batch, height,
-            width, p, g.shard.image_start, g.L, st,
+            ws["pixels"].data_ptr(), pdt, ws["ph"].data_ptr(), blocks[0]["norm1"].data_ptr(), eps, g.batch,
+            self.in_channels, height, width, p, g.shard.image_start, g.L, st,
         )  # fmt: skip
         heads = pix.num_heads
         if capture is not None:

@@ -170,3 +170,28 @@ def num_parameters(cfg: OracleConfig) -> int:
             n *= s
         total += n
     return total
+
+
+def depth_task_params(cfg: OracleConfig, seed: int = 0, extra_seed: int = 7) -> dict[str, torch.Tensor]:
+    """Weights of a depth fine-tune (``IrisDepth``, ``src/iris3b/downstream/depth.py:30-38``):
+    the model of ``seeded_init(cfg, seed)`` with the patch and pixel embedders
+    widened to one extra input channel, concatenated after RGB, and the 1x1
+    ``depth_reducer`` (3 -> 1). The widened weights and the reducer are drawn
+    afresh, ``N(0, 0.02)``, from a generator seeded with ``extra_seed`` in the
+    order s_embedder, pixel_embedder, depth_reducer (weight then bias each).
+    Keys of the denoiser keep their ``IrisDiT`` names; the reducer's are
+    ``depth_reducer.weight`` / ``depth_reducer.bias``."""
+    params = seeded_init(cfg, seed)
+    gen = torch.Generator().manual_seed(extra_seed)
+    d, p, c = cfg.hidden_size, cfg.patch_size, cfg.in_channels
+    shapes = {
+        "s_embedder.proj.weight": (d, p * p * (c + 1)),
+        "s_embedder.proj.bias": (d,),
+        "pixel_embedder.proj.weight": (cfg.pixel.hidden_size, c + 1),
+        "pixel_embedder.proj.bias": (cfg.pixel.hidden_size,),
+        "depth_reducer.weight": (1, c, 1, 1),
+        "depth_reducer.bias": (1,),
+    }
+    for name, shape in shapes.items():
+        params[name] = torch.randn(shape, generator=gen) * STD
+    return params

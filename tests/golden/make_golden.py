@@ -194,6 +194,33 @@ def _turbo_fixture(model, fixture):
             "steps": steps}
 
 
+def _depth_fixture(cfg, fixture, ModelConfig, PixelStageConfig):
+    """The depth fine-tune (``IrisDepth``, ``src/iris3b/downstream/depth.py:30-49``) on
+    the toy topology, weights from ``oracle.params.depth_task_params``: its own
+    ``forward`` (RGB plus a zero channel at the final timestep, then the 1x1
+    reducer), and the widened denoiser on a 4-channel input whose extra channel is
+    not zero (the general case of an engine built on ``model.pixel``)."""
+    from iris3b.downstream.depth import IrisDepth
+
+    from oracle.params import depth_task_params
+
+    model = IrisDepth(_reference_config(cfg, ModelConfig, PixelStageConfig)).eval()
+    params = depth_task_params(cfg)
+    state = {("" if k.startswith("depth_reducer") else "pixel.") + k: v for k, v in params.items()}
+    model.load_state_dict(state, strict=True)
+    gen = torch.Generator().manual_seed(8)
+    rgb = torch.rand(1, 3, fixture["x"].shape[2], fixture["x"].shape[3], generator=gen) * 2 - 1
+    x4 = torch.randn(2, 4, rgb.shape[2], rgb.shape[3], generator=gen)
+    y = fixture["y"][1:]
+    t = torch.tensor([1000.0, 431.0])
+    with torch.no_grad():
+        depth = model(rgb, y, torch.ones(1, y.shape[1], dtype=torch.bool))
+        text = model.pixel.embed_text(y)
+        v4 = model.pixel(x4, t, y.expand(2, -1, -1), prepared_text=text.expand(2, -1, -1)).x
+    return {"rgb": rgb, "y": y, "prepared_text": text, "depth": depth, "x4": x4, "t4": t, "v4": v4,
+            "time": float(model.num_train_timesteps)}
+
+
 def _op_fixtures():
     from iris3b.nn.embeddings import TimestepEmbedder, sincos_pos_embed_2d
     from iris3b.nn.rope import apply_rope, rope_1d, rope_2d
@@ -300,6 +327,7 @@ def main():
         if name == "released_mha":
             fixture["euler_cfg"] = _sample_fixture(model, fixture)
             fixture["turbo"] = _turbo_fixture(model, fixture)
+            fixture["depth"] = _depth_fixture(cfg, fixture, ModelConfig, PixelStageConfig)
         torch.save(fixture, HERE / f"{name}.pt")
         print(name, "saved", tuple(fixture["v"].shape), float(fixture["v"].abs().max()))
     torch.save(_op_fixtures(), HERE / "ops.pt")

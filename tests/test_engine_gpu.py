@@ -151,6 +151,35 @@ def test_turbo_recipe_matches_reference_autocast(iris):
     assert value > PSNR_MIN
 
 
+def test_depth_task_four_channel_input_matches_reference(iris):
+    """A depth fine-tune's widened denoiser (src/iris3b/downstream/depth.py:30-38),
+    which the reference engine accepts (src/iris_metal/model.py:181-217): 4 input
+    channels, 3 output. The engine built on it as MetalDepth builds its engine
+    (src/iris_metal/tasks.py:79-97) against IrisDepth's own outputs: a 4-channel
+    input whose extra channel is not zero, and the depth prediction (RGB plus a
+    zero channel at t = 1000, then the 1x1 reducer)."""
+    from oracle.params import depth_task_params
+    from test_oracle import depth_engine_inputs
+
+    fx = golden("released_mha")
+    cfg = _config(fx["config"])
+    d = fx["depth"]
+    params = depth_task_params(cfg)
+    reducer = [params.pop(k).cuda() for k in ("depth_reducer.weight", "depth_reducer.bias")]
+    engine = _engine(iris, cfg, params)
+    assert engine.in_channels == 4
+    v4 = engine(d["x4"].cuda(), d["t4"].cuda(), d["prepared_text"].expand(2, -1, -1).contiguous().cuda())
+    print(f"depth model, 4-channel input: max rel err {rel_err(v4, d['v4']):.3e}, psnr {psnr(v4, d['v4']):.1f} dB")
+    assert v4.shape == d["v4"].shape
+    assert rel_err(v4, d["v4"]) < REL_TOL
+    assert psnr(v4, d["v4"]) > PSNR_MIN
+    x, t, text = depth_engine_inputs(fx)
+    depth = torch.nn.functional.conv2d(engine(x.cuda(), t.cuda(), text.cuda()), *reducer)
+    assert rel_err(depth, d["depth"]) < REL_TOL
+    with pytest.raises(ValueError, match="input channels"):
+        engine(d["rgb"].cuda(), t.cuda(), text.cuda())
+
+
 def test_non_square_grid_and_odd_batch(iris):
     fx = golden("released_gqa")  # 24 x 16 input: a 6 x 4 patch grid
     cfg = _config(fx["config"])

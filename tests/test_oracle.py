@@ -74,6 +74,33 @@ def test_oracle_turbo_recipe_matches_reference():
     torch.testing.assert_close(sample, tb["fp32"], rtol=1e-4, atol=1e-5)
 
 
+def depth_engine_inputs(fx):
+    """The depth task's denoiser input (src/iris_metal/tasks.py:92-95): RGB plus a
+    zero channel at the final timestep."""
+    d = fx["depth"]
+    rgb = d["rgb"]
+    x = torch.cat([rgb, rgb.new_zeros(rgb.shape[0], 1, *rgb.shape[2:])], dim=1)
+    return x, torch.full((rgb.shape[0],), d["time"]), d["prepared_text"]
+
+
+def test_oracle_depth_task_matches_reference():
+    """The widened (4-channel) denoiser of a depth fine-tune and the depth
+    prediction (1x1 reducer over the velocity) against IrisDepth itself."""
+    from oracle.params import depth_task_params
+
+    fx = golden("released_mha")
+    cfg = _config(fx["config"])
+    params = depth_task_params(cfg)
+    reducer = params.pop("depth_reducer.weight"), params.pop("depth_reducer.bias")
+    model = OracleModel(cfg, params)
+    d = fx["depth"]
+    with torch.no_grad():
+        v4 = model(d["x4"], d["t4"], d["prepared_text"].expand(2, -1, -1))
+        depth = torch.nn.functional.conv2d(model(*depth_engine_inputs(fx)), *reducer)
+    torch.testing.assert_close(v4, d["v4"], rtol=1e-4, atol=1e-5)
+    torch.testing.assert_close(depth, d["depth"], rtol=1e-4, atol=1e-5)
+
+
 def test_oracle_dpm_solver_matches_reference():
     fx = golden("samplers")
     z, cond, uncond = fx["inputs"]["z"], fx["inputs"]["cond"], fx["inputs"]["uncond"]

@@ -294,7 +294,7 @@ def test_token_range_layout_kernels_match_whole_image(iris):
     pix_p, nrm_p = torch.empty(B * cnt * pp, 16, device="cuda"), torch.empty(B * cnt, pp * 16, device="cuda", dtype=torch.bfloat16)
     for pix, nrm, start, count in ((pix_f, nrm_f, 0, L), (pix_p, nrm_p, t0, cnt)):
         _lib.call("iris_pixel_embed", x.data_ptr(), w.data_ptr(), b.data_ptr(), pos.data_ptr(), pix.data_ptr(),
-                  _lib.F32, nrm.data_ptr(), gain.data_ptr(), 1e-6, B, H, W, p, start, count, st)  # fmt: skip
+                  _lib.F32, nrm.data_ptr(), gain.data_ptr(), 1e-6, B, 3, H, W, p, start, count, st)  # fmt: skip
     assert torch.equal(pix_p.view(B, cnt, -1), pix_f.view(B, L, -1)[:, t0 : t0 + cnt])
     assert torch.equal(nrm_p.view(B, cnt, -1), nrm_f.view(B, L, -1)[:, t0 : t0 + cnt])
 
