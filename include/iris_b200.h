@@ -200,11 +200,16 @@ int iris_flash_attn_fwd(const void* q, const void* k, const void* v, void* o, in
  * bf16 logits read from the same rows of gate_text / gate_image (both null:
  * no gate). split = 0 writes every token to o_image. q holds n queries and
  * k / v hold n_kv keys per (b, h); n_kv may differ from n (a sequence-
- * parallel rank's own queries over the keys of the whole sequence). */
+ * parallel rank's own queries over the keys of the whole sequence).
+ * score_bound: 0, or a bound B >= |q . k| * scale over every query / key pair
+ * (QK-normed heads: 128 * max|q gain| * max|k gain| * scale, with a little
+ * slack for the bf16 rounding of q and k). Once a query row's running max is
+ * within 64 log2 units of B, the row keeps it and skips the row-max pass; a
+ * bound below the true scores can overflow that row to inf / NaN. */
 int iris_flash_attn_fwd_split(const void* q, const void* k, const void* v, int64_t batch, int64_t heads_q,
-                              int64_t heads_kv, int64_t n, int64_t n_kv, int64_t head_dim, float scale, int64_t split,
-                              void* o_text, void* o_image, const void* gate_text, const void* gate_image,
-                              int64_t row_stride, void* stream);
+                              int64_t heads_kv, int64_t n, int64_t n_kv, int64_t head_dim, float scale,
+                              float score_bound, int64_t split, void* o_text, void* o_image, const void* gate_text,
+                              const void* gate_image, int64_t row_stride, void* stream);
 
 /* Sequence-parallel attention (no reference counterpart: the reference runs
  * on one device): this rank's heads_q heads over all n = world *
@@ -212,11 +217,11 @@ int iris_flash_attn_fwd_split(const void* q, const void* k, const void* v, int64
  * that owns its token, o_peers[j] (pointers valid in this process), row
  * b * tokens_per_rank + i % tokens_per_rank, columns col0 + h * 128 ... of
  * row_stride bf16. The all-to-all of the attention output, done by the
- * epilogue's stores. */
+ * epilogue's stores. score_bound as for iris_flash_attn_fwd_split. */
 int iris_flash_attn_fwd_peers(const void* q, const void* k, const void* v, int64_t batch, int64_t heads_q,
                               int64_t heads_kv, int64_t n, int64_t n_kv, int64_t head_dim, float scale,
-                              void* const* o_peers, int world, int64_t tokens_per_rank, int64_t col0,
-                              int64_t row_stride, void* stream);
+                              float score_bound, void* const* o_peers, int world, int64_t tokens_per_rank,
+                              int64_t col0, int64_t row_stride, void* stream);
 
 /* ---- peer memory (sequence parallelism across processes) ---------------- */
 /* No reference counterpart. iris_ipc_export: the IPC handle (IRIS_IPC_HANDLE_BYTES)

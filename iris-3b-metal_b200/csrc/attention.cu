@@ -21,8 +21,11 @@
 //               by the next TS MMA, which completes before the following S MMA
 //               overwrites them: the MMAs of one thread execute in issue order);
 //               O is rescaled in TMEM only when a row max grew by more than 2^8
-//               (O and l share the stale max, so the result is exact); final
-//               O / l (times the sigmoid gate, if any) -> bf16 rows per stream.
+//               (O and l share the stale max, so the result is exact). With a
+//               score bound (QK-normed heads), a row whose running max is within
+//               2^64 of the bound keeps it: no later score can overflow P, and
+//               the row-max pass and its exchange stop for the rest of the keys.
+//               Final O / l (times the sigmoid gate, if any) -> bf16 rows per stream.
 // TMEM: S_0 [0,128) S_1 [128,256) O_0 [256,384) O_1 [384,512).
 #include "common.cuh"
 #include "iris_abi_internal.h"
@@ -40,6 +43,9 @@ constexpr int SOFTMAX_WARPS_PER_TILE = 8;  // two warps per TMEM lane quarter, o
 constexpr int THREADS = 64 + TILES * SOFTMAX_WARPS_PER_TILE * 32;  // 576
 constexpr uint32_t COL_S = 0, COL_O = 256;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
+// A row whose running max is within this many log2 units of the score bound
+// keeps it for good: P <= 2^64, row sums <= 2^64 n_kv, all finite in fp32 / bf16.
+constexpr float BOUND_MARGIN = 64.0f;
 constexpr size_t SMEM_BYTES = 1024 + (TILES + 4) * TILE_BYTES + 8192;
 
 struct Smem {
@@ -56,6 +62,9 @@ struct Smem {
 struct Params {
   int64_t batch, heads_q, heads_kv, n, n_kv, row_stride, split;  // n queries and n_kv keys per (b, h)
   float scale_log2;
+  // > 0: every score * scale_log2 is at most this (QK-normed heads bound it;
+  // see iris_flash_attn_fwd_split); 0: no bound known
+  float bound_log2;
   __nv_bfloat16* o_text;   // rows b * split + i       (i < split)
   __nv_bfloat16* o_image;  // rows b * (n - split) + i - split
   const __nv_bfloat16* gate_text;  // bf16 gate logits in the same rows, or null
@@ -245,6 +254,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t s_col = COL_S + tile * BKV + half * 64;  // this half's 64 score columns
     const uint32_t o_col = COL_O + tile * D + half * 64;    // and 64 output columns
     float m_run = -INFINITY, l_run = 0.f;
+    // Once the score bound is within BOUND_MARGIN of every running max of this
+    // warp's rows, m_run is final and the row-max pass (with its exchange
+    // between the two halves) is skipped. Both warps of a row pair hold the
+    // same 32 running maxima, so they take the same branch at every block.
+    bool settled = false;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
       if (!__all_sync(0xffffffffu, mbar_wait(&s->s_full[tile], static_cast<uint32_t>(j & 1), abort))) {
@@ -254,6 +268,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_after();
       const int valid = n_kv - j * BKV - half * 64;  // keys of this half that exist
       const bool tail = valid < 64;
+      float m_new = m_run, corr = 1.f;
+      if (!settled) {
       // pass 1: this half's row max, combined with the other half's
       float mx;
       {
@@ -285,8 +301,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       // lazy rescale: keep the stale max unless it grew by more than 2^8
       const bool grow = j == 0 || mx > m_run + RESCALE_THRESHOLD;
-      const float m_new = grow ? fmaxf(m_run, mx) : m_run;
-      const float corr = ex2(m_run - m_new);  // 0 on the first block
+      m_new = grow ? fmaxf(m_run, mx) : m_run;
+      corr = ex2(m_run - m_new);  // 0 on the first block
       if (j > 0 && __any_sync(0xffffffffu, grow)) {
         // O_t holds the P V of earlier blocks: S_t(j) completing implies they completed
 #pragma unroll 1
@@ -304,6 +320,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           tmem_st16(tmem + lane_addr + o_col + c * 32 + 16, hi);
         }
       }
+      }  // !settled
       // pass 2: P = 2^(s * scale - m) for this half; packed bf16 over its first 32 columns
       const float2 scale2 = make_float2(p.scale_log2, p.scale_log2);
       const float2 shift2 = make_float2(-m_new, -m_new);
@@ -335,6 +352,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       l_run = l_run * corr + (rs2.x + rs2.y);
       m_run = m_new;
+      if (!settled && p.bound_log2 > 0.f) settled = __all_sync(0xffffffffu, p.bound_log2 - m_run <= BOUND_MARGIN);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -433,12 +451,13 @@ static int launch_attention(const void* q, const void* k, const void* v, iris::a
 
 extern "C" int iris_flash_attn_fwd_split(const void* q, const void* k, const void* v, int64_t batch,
                                          int64_t heads_q, int64_t heads_kv, int64_t n, int64_t n_kv,
-                                         int64_t head_dim, float scale,
+                                         int64_t head_dim, float scale, float score_bound,
                                          int64_t split, void* o_text, void* o_image, const void* gate_text,
                                          const void* gate_image, int64_t row_stride, void* stream) {
   using namespace iris::attn;
   IRIS_REQUIRE(q && k && v && o_image, "flash_attn_fwd: null pointer");
   IRIS_REQUIRE(head_dim == D, "flash_attn_fwd: head_dim must be 128");
+  IRIS_REQUIRE(score_bound >= 0.f && score_bound < INFINITY, "flash_attn_fwd: score_bound must be finite, >= 0");
   IRIS_REQUIRE(batch > 0 && heads_q > 0 && heads_kv > 0 && heads_q % heads_kv == 0,
                "flash_attn_fwd: heads_q must be a positive multiple of heads_kv");
   IRIS_REQUIRE(n > 0 && batch * heads_q * n < (1ll << 31), "flash_attn_fwd: sequence too long");
@@ -462,6 +481,7 @@ extern "C" int iris_flash_attn_fwd_split(const void* q, const void* k, const voi
   p.row_stride = row_stride;
   p.split = split;
   p.scale_log2 = scale * 1.4426950408889634f;
+  p.bound_log2 = score_bound * 1.4426950408889634f;
   p.o_text = reinterpret_cast<__nv_bfloat16*>(o_text);
   p.o_image = reinterpret_cast<__nv_bfloat16*>(o_image);
   p.gate_text = reinterpret_cast<const __nv_bfloat16*>(gate_text);
@@ -471,11 +491,13 @@ extern "C" int iris_flash_attn_fwd_split(const void* q, const void* k, const voi
 
 extern "C" int iris_flash_attn_fwd_peers(const void* q, const void* k, const void* v, int64_t batch, int64_t heads_q,
                                          int64_t heads_kv, int64_t n, int64_t n_kv, int64_t head_dim, float scale,
-                                         void* const* o_peers, int world, int64_t tokens_per_rank, int64_t col0,
+                                         float score_bound, void* const* o_peers, int world, int64_t tokens_per_rank,
+                                         int64_t col0,
                                          int64_t row_stride, void* stream) {
   using namespace iris::attn;
   IRIS_REQUIRE(q && k && v && o_peers, "flash_attn_fwd_peers: null pointer");
   IRIS_REQUIRE(head_dim == D, "flash_attn_fwd_peers: head_dim must be 128");
+  IRIS_REQUIRE(score_bound >= 0.f && score_bound < INFINITY, "flash_attn_fwd_peers: score_bound must be finite, >= 0");
   IRIS_REQUIRE(batch > 0 && heads_q > 0 && heads_kv > 0 && heads_q % heads_kv == 0,
                "flash_attn_fwd_peers: heads_q must be a positive multiple of heads_kv");
   IRIS_REQUIRE(world >= 1 && world <= IRIS_MAX_PEERS && tokens_per_rank > 0 && n == world * tokens_per_rank,
@@ -495,6 +517,7 @@ extern "C" int iris_flash_attn_fwd_peers(const void* q, const void* k, const voi
   p.row_stride = row_stride;
   p.split = 0;
   p.scale_log2 = scale * 1.4426950408889634f;
+  p.bound_log2 = score_bound * 1.4426950408889634f;
   p.peers = world;
   p.peer_tokens = tokens_per_rank;
   p.peer_col0 = col0;
@@ -510,6 +533,6 @@ extern "C" int iris_flash_attn_fwd_peers(const void* q, const void* k, const voi
 extern "C" int iris_flash_attn_fwd(const void* q, const void* k, const void* v, void* o, int64_t batch,
                                    int64_t heads_q, int64_t heads_kv, int64_t n, int64_t head_dim, float scale,
                                    int64_t o_row_stride, void* stream) {
-  return iris_flash_attn_fwd_split(q, k, v, batch, heads_q, heads_kv, n, n, head_dim, scale, 0, nullptr, o, nullptr,
-                                   nullptr, o_row_stride, stream);
+  return iris_flash_attn_fwd_split(q, k, v, batch, heads_q, heads_kv, n, n, head_dim, scale, 0.f, 0, nullptr, o,
+                                   nullptr, nullptr, o_row_stride, stream);
 }

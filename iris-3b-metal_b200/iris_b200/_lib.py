@@ -73,12 +73,12 @@ class GemmProblem(ctypes.Structure):
 
 
 SIGNATURES["iris_gemm_bf16_grouped"] = [ctypes.POINTER(GemmProblem), I32, P]
-SIGNATURES["iris_flash_attn_fwd_peers"] = [P, P, P, I64, I64, I64, I64, I64, I64, F, P, I32, I64, I64, I64, P]
+SIGNATURES["iris_flash_attn_fwd_peers"] = [P, P, P, I64, I64, I64, I64, I64, I64, F, F, P, I32, I64, I64, I64, P]
 SIGNATURES["iris_ipc_export"] = [P, P, ctypes.POINTER(I64)]
 SIGNATURES["iris_ipc_import"] = [P, ctypes.POINTER(P)]
 SIGNATURES["iris_ipc_close"] = [P]
 SIGNATURES["iris_peer_barrier"] = [P, P, I32, I32, ctypes.c_uint, I64, P]
-SIGNATURES["iris_flash_attn_fwd_split"] = [P, P, P, I64, I64, I64, I64, I64, I64, F, I64, P, P, P, P, I64, P]
+SIGNATURES["iris_flash_attn_fwd_split"] = [P, P, P, I64, I64, I64, I64, I64, I64, F, F, I64, P, P, P, P, I64, P]
 
 _lib: ctypes.CDLL | None = None
 

@@ -390,10 +390,24 @@ def profile_gemms(enable: bool):
     return flops, ms, len(records), sum(r[3] for r in records)
 
 
-def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor, scale: float | None = None):
+def score_bound(q_gains, k_gains, scale: float | None = None, head_dim: int = 128) -> float:
+    """An upper bound on ``|q . k| * scale`` for RMS-normed (QK-norm) heads:
+    an RMS-normed row has norm at most ``sqrt(head_dim)`` before its gain, and
+    RoPE is a rotation, so ``|q . k| <= head_dim * max|q gain| * max|k gain|``
+    (Cauchy-Schwarz). 2% slack covers the bf16 rounding of q and k. Every
+    stream's gains of a joint attention go into one bound."""
+    gq = max(float(g.abs().max()) for g in q_gains)
+    gk = max(float(g.abs().max()) for g in k_gains)
+    scale = head_dim**-0.5 if scale is None else scale
+    return 1.02 * head_dim * gq * gk * scale
+
+
+def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor, scale: float | None = None,
+                    bound: float = 0.0):  # fmt: skip
     """``softmax(q k^T * scale) v`` for ``q``: ``[B, H, N, 128]``, ``k``/``v``:
     ``[B, H_kv, N_kv, 128]`` (bf16, contiguous; ``N_kv`` may differ from ``N``);
-    ``out``: ``[B, N, >= H*128]`` bf16."""
+    ``out``: ``[B, N, >= H*128]`` bf16. ``bound``: 0 or :func:`score_bound` of
+    the heads' QK-norm gains (rows then skip the row-max pass once settled)."""
     _check_qkv(q, k, v)
     batch, heads, n, d = q.shape
     _require(out.dtype == torch.bfloat16 and out.stride(-1) == 1 and out.shape[-2] == n, "flash_attention: out layout")
@@ -401,14 +415,14 @@ def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torc
     _require_cuda(q, k, v, out)
     _lib.call(
         "iris_flash_attn_fwd_split", q.data_ptr(), k.data_ptr(), v.data_ptr(), batch, heads, k.shape[1], n,
-        k.shape[2], d, float(scale if scale is not None else d**-0.5), 0, None, out.data_ptr(), None, None,
-        out.stride(1), stream_of(q),
+        k.shape[2], d, float(scale if scale is not None else d**-0.5), float(bound), 0, None, out.data_ptr(), None,
+        None, out.stride(1), stream_of(q),
     )  # fmt: skip
     return out
 
 
 def flash_attention_peers(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out_ptrs, tokens_per_rank: int,
-                          col0: int, row_stride: int, scale: float | None = None) -> None:  # fmt: skip
+                          col0: int, row_stride: int, scale: float | None = None, bound: float = 0.0) -> None:  # fmt: skip
     """Sequence-parallel attention of this rank's heads over every token: the
     output row of query ``i`` (bf16, ``q.shape[1] * 128`` columns from ``col0``)
     goes to rank ``i // tokens_per_rank``'s token rows ``out_ptrs[j]`` (device
@@ -422,8 +436,8 @@ def flash_attention_peers(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out
     ptrs = (ctypes.c_void_p * world)(*out_ptrs)
     _lib.call(
         "iris_flash_attn_fwd_peers", q.data_ptr(), k.data_ptr(), v.data_ptr(), batch, heads, k.shape[1], n,
-        k.shape[2], d, float(scale if scale is not None else d**-0.5), ptrs, world, tokens_per_rank, col0, row_stride,
-        stream_of(q),
+        k.shape[2], d, float(scale if scale is not None else d**-0.5), float(bound), ptrs, world, tokens_per_rank, col0,
+        row_stride, stream_of(q),
     )  # fmt: skip
 
 
@@ -474,6 +488,7 @@ def flash_attention_split(
     gate_text: torch.Tensor | None = None,
     gate_image: torch.Tensor | None = None,
     scale: float | None = None,
+    bound: float = 0.0,
 ) -> None:
     """Attention whose token ``i < split`` rows land densely in ``o_text`` (row
     ``b * split + i``) and the rest in ``o_image`` (row ``b * (N - split) + i - split``),
@@ -487,8 +502,8 @@ def flash_attention_split(
     _require_cuda(q, k, v, *outs)
     _lib.call(
         "iris_flash_attn_fwd_split", q.data_ptr(), k.data_ptr(), v.data_ptr(), batch, heads, k.shape[1], n,
-        k.shape[2], d, float(scale if scale is not None else d**-0.5), split, _ptr(o_text), o_image.data_ptr(), _ptr(gate_text),
-        _ptr(gate_image), stride, stream_of(q),
+        k.shape[2], d, float(scale if scale is not None else d**-0.5), float(bound), split, _ptr(o_text),
+        o_image.data_ptr(), _ptr(gate_text), _ptr(gate_image), stride, stream_of(q),
     )  # fmt: skip
 
 

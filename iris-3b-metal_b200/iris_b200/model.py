@@ -35,7 +35,7 @@ slice of the joint sequence and every rank returns the whole velocity.
 
 from __future__ import annotations
 
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 
 import torch
 
@@ -116,6 +116,10 @@ class _Block:
     w13: dict
     w2: dict
     mod_index: dict  # stream -> row in the stacked modulation table
+    score_bound: float = field(init=False)  # of |q . k| * scale, from the QK-norm gains of every stream
+
+    def __post_init__(self):
+        self.score_bound = K.score_bound(*zip(*self.qk_norm.values()))
 
 
 class CudaIris:
@@ -279,6 +283,7 @@ class CudaIris:
                     "compress": (pad_k(bf(f"{b}.compress.weight")), f32(f"{b}.compress.bias")),
                     "qkv": bf(f"{b}.attn.qkv.weight"),
                     "qk_norm": (f32(f"{b}.attn.q_norm.weight"), f32(f"{b}.attn.k_norm.weight")),
+                    "score_bound": K.score_bound([state[f"{b}.attn.q_norm.weight"]], [state[f"{b}.attn.k_norm.weight"]]),
                     "proj": (bf(f"{b}.attn.proj.weight"), f32(f"{b}.attn.proj.bias")),
                     "expand": (bf(f"{b}.expand.weight"), f32(f"{b}.expand.bias")),
                     "fc1": (bf(f"{b}.mlp.fc1.weight"), bf(f"{b}.mlp.fc1.bias")),
@@ -584,7 +589,7 @@ class CudaIris:
             bt = g.batch * split
             K.flash_attention_split(
                 ws["q"], ws["k"], ws["v"], split, ws["og"][:bt] if bt else None, ws["og"][bt:],
-                ws["glog"][:bt] if bt else None, ws["glog"][bt:],
+                ws["glog"][:bt] if bt else None, ws["glog"][bt:], bound=block.score_bound,
             )  # fmt: skip
         else:
             self._attention_sequence_parallel(block, segs, ws, g, st)
@@ -608,12 +613,13 @@ class CudaIris:
             # stores each output row into the token rows of the rank that owns it
             self._barrier(ws)
             K.flash_attention_peers(ws["qf"], ws["kf"], ws["vf"], ws["_peers"].ptrs["o_loc"], n,
-                                    comm.rank * hql * HEAD_DIM, self.cfg.num_heads * HEAD_DIM)  # fmt: skip
+                                    comm.rank * hql * HEAD_DIM, self.cfg.num_heads * HEAD_DIM,
+                                    bound=block.score_bound)  # fmt: skip
             self._barrier(ws)
         else:
             for name, heads in (("q", hql), ("k", hkvl), ("v", hkvl)):
                 scatter_heads(comm, K.block_copy, ws[name], ws[name + "_r"], ws[name + "f"], heads, B, n, HEAD_DIM)
-            K.flash_attention(ws["qf"], ws["kf"], ws["vf"], ws["of"])
+            K.flash_attention(ws["qf"], ws["kf"], ws["vf"], ws["of"], bound=block.score_bound)
             gather_tokens(comm, K.block_copy, ws["of"], ws["o_s"], ws["o_r"], ws["o_loc"], B, n, hql * HEAD_DIM)
         h = ws[_hkey(block)]
         problems = [
@@ -728,7 +734,8 @@ class CudaIris:
                     gather_image_tokens(self.comm, K.block_copy, g.shard, ws[name + "_s"], ws[name + "_g"], ws[name],
                                         g.batch, heads, HEAD_DIM)  # fmt: skip
             full = kv if self.peer else ("pk", "pv")
-            K.flash_attention(ws["pq"], ws[full[0]], ws[full[1]], ws["po"].view(g.batch, g.L, -1))
+            K.flash_attention(ws["pq"], ws[full[0]], ws[full[1]], ws["po"].view(g.batch, g.L, -1),
+                              bound=blk["score_bound"])  # fmt: skip
             K.gemm(ws["po"], blk["proj"][0], ws["pproj"], bias=blk["proj"][1])
             K.gemm(ws["pproj"], blk["expand"][0], ws["pbranch"], bias=blk["expand"][1])
             (w1, b1), (w2, b2) = blk["fc1"], blk["fc2"]

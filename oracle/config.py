@@ -69,7 +69,9 @@ class OracleConfig:
 
 def baseline_step_config() -> OracleConfig:
     """the released hybrid at d=3072, 24 MHA heads x 128,
-    linear text adapter, 256 text tokens (SURVEY-derived; see DESIGN)."""
+    linear text adapter, 256 text tokens: ``replace(ModelConfig(), hidden_size=3072,
+    num_heads=24, num_kv_heads=None, text_len=256, text_adapter="linear")`` over the
+    released defaults of ``src/iris3b/config.py``."""
     return OracleConfig(hidden_size=3072, num_heads=24, num_kv_heads=None, text_len=256)
 
 
