@@ -153,3 +153,29 @@ def test_checkpoint_directory_loads_config_and_weights(tmp_path):
     assert set(state) == set(params)
     for key, value in params.items():
         assert torch.equal(state[key], value), key
+
+
+def test_score_bound_covers_aligned_rms_normed_rows():
+    """kernels.score_bound bounds |q . k| * scale for RMS-normed rows times their
+    gains, also for the worst case: q and k both along the largest gains."""
+    from iris_b200 import kernels as K
+
+    gen = torch.Generator().manual_seed(3)
+    for gain in (0.5, 1.0, 4.0):
+        gq = gain * (1 + 0.3 * torch.rand(128, generator=gen))
+        gk = gain * (1 + 0.3 * torch.rand(128, generator=gen))
+        bound = K.score_bound([gq], [gk])
+
+        def normed(x, g):
+            return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6) * g
+
+        worst = torch.zeros(128)
+        worst[int(gq.argmax())] = 1.0  # all mass on one dimension: norm sqrt(128) there
+        q = normed(torch.cat([torch.randn(64, 128, generator=gen), worst[None]]), gq).to(torch.bfloat16).float()
+        k = normed(torch.cat([torch.randn(64, 128, generator=gen), worst[None] * -1]), gk).to(torch.bfloat16).float()
+        scores = (q @ k.T) * 128**-0.5
+        assert float(scores.abs().max()) <= bound
+        assert float(scores.abs().max()) > 0.5 * bound  # and the bound is not loose by more than 2x
+    # several streams share one bound: the largest gains of each side
+    assert K.score_bound([torch.ones(128), 2 * torch.ones(128)], [torch.ones(128)]) == K.score_bound(
+        [2 * torch.ones(128)], [torch.ones(128)])

@@ -357,6 +357,39 @@ def test_flash_attention_sharp_softmax(K):
     assert rel_err(out, expected) < 2e-2
 
 
+@pytest.mark.parametrize("gain,sharp_tail", [(1.0, False), (1.0, True), (3.0, True)])
+def test_flash_attention_with_score_bound(K, gain, sharp_tail):
+    """QK-normed q and k with the engine's score bound. Gain 1: every row
+    settles after the first key block (bound - max < 64 log2 units) and skips
+    the row-max pass; with the sharp tail the later keys lie along the queries,
+    so the true scores climb towards the bound after the rows settled. Gain 3:
+    the bound (~118 log2 units) is too far above the scores to settle, so the
+    row-max pass and the lazy rescale keep running with a bound given."""
+    B, H, N = 1, 2, 640
+    gen = torch.Generator(device="cuda").manual_seed(17)
+
+    def normed(x, g):
+        return (x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6) * g).to(torch.bfloat16)
+
+    gq = gain * (1 + 0.05 * torch.randn(128, device="cuda", generator=gen))
+    gk = gain * (1 + 0.05 * torch.randn(128, device="cuda", generator=gen))
+    qr = torch.randn(B, H, N, 128, device="cuda", generator=gen)
+    kr = torch.randn(B, H, N, 128, device="cuda", generator=gen)
+    if sharp_tail:  # keys 400.. point along query 0's direction: large late scores
+        kr[:, :, 400:] = qr[:, :, :1] + 0.1 * kr[:, :, 400:]
+    q, k = normed(qr, gq), normed(kr, gk)
+    v = torch.randn(B, H, N, 128, device="cuda", generator=gen).to(torch.bfloat16)
+    bound = K.score_bound([gq], [gk])
+    scores = (q.float() @ k.float().transpose(-1, -2)) * 128**-0.5
+    assert float(scores.abs().max()) <= bound
+    out = torch.empty(B, N, H * 128, device="cuda", dtype=torch.bfloat16)
+    K.flash_attention(q, k, v, out, bound=bound)
+    expected = ops.sdpa(q.float(), k.float(), v.float()).transpose(1, 2).reshape(B, N, H * 128)
+    assert torch.isfinite(out).all()
+    assert rel_err(out, expected) < 2e-2
+    assert K.device_error() == 0
+
+
 # ---------------------------------------------------------- heads, layout, small
 def test_qkv_heads_matches_oracle(K):
     from iris_b200 import _lib
