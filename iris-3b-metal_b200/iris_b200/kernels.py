@@ -20,6 +20,7 @@ engine (``gemm``, ``flash_attention``, ...) follow the same rules.
 from __future__ import annotations
 
 import ctypes
+import math
 
 import torch
 
@@ -399,7 +400,8 @@ def score_bound(q_gains, k_gains, scale: float | None = None, head_dim: int = 12
     gq = max(float(g.abs().max()) for g in q_gains)
     gk = max(float(g.abs().max()) for g in k_gains)
     scale = head_dim**-0.5 if scale is None else scale
-    return 1.02 * head_dim * gq * gk * scale
+    bound = 1.02 * head_dim * gq * gk * scale
+    return bound if math.isfinite(bound) else 0.0  # 0: no bound, every block runs the row-max pass
 
 
 def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor, scale: float | None = None,
