@@ -305,11 +305,16 @@ class CudaIris:
     # -- conditioning ---------------------------------------------------------------
     @torch.no_grad()
     def encode_text(self, states: torch.Tensor, mask: torch.Tensor | None = None) -> torch.Tensor:
-        """Encoder states ``[B, T, text_dim]`` -> trunk text tokens ``[B, T, D]`` (FP32):
-        ``TextEmbedder`` (Linear + RMSNorm) + ``y_pos_embedding`` (``dit.py:263-281``).
-        The masked transformer adapters run once per prompt outside this engine."""
+        """Encoder states -> trunk text tokens ``[B, T, D]`` (FP32), once per prompt.
+
+        The linear adapter (``TextEmbedder``: Linear + RMSNorm, then
+        ``y_pos_embedding``, ``dit.py:263-281``) runs on this engine's kernels.
+        Any other adapter (the masked ``lap_blocks2`` transformer over
+        ``[B, T, layers, dim]`` states) runs through the upstream module the
+        engine was built from, under BF16 autocast, as ``MetalIris.encode_text``
+        does (``src/iris_metal/model.py:133-145``); it then needs ``mask``."""
         if self.text_adapter is None:
-            raise NotImplementedError("CudaIris.encode_text implements the linear text adapter")
+            return self._encode_text_upstream(states, mask)
         w, b, norm_w, pos = self.text_adapter
         cfg = self.cfg
         states = states[:, : cfg.text_len].to(self.device)
@@ -322,6 +327,23 @@ class CudaIris:
         _lib.call("iris_rms_norm_add_rows", out.data_ptr(), norm_w.data_ptr(), add.data_ptr(), batch * n, n,
                   cfg.hidden_size, float(cfg.norm_eps), K.stream_of(out))  # fmt: skip
         return out
+
+    @torch.no_grad()
+    def _encode_text_upstream(self, states: torch.Tensor, mask: torch.Tensor | None) -> torch.Tensor:
+        y_embedder = getattr(self.dit, "y_embedder", None)
+        if y_embedder is None:
+            raise NotImplementedError(
+                f"CudaIris.encode_text: the {self.cfg.text_adapter!r} text adapter runs through the upstream "
+                "module (build the engine from the upstream IrisDiT); the linear adapter runs on the engine"
+            )
+        if mask is None:
+            raise ValueError(f"encode_text: the {self.cfg.text_adapter!r} text adapter needs the encoder's [B, T] mask")
+        n = self.cfg.text_len
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            tokens = y_embedder(states[:, :n].to(self.device, torch.float32), mask[:, :n].to(self.device))
+        tokens = tokens.float()
+        pos = getattr(self.dit, "y_pos_embedding", None)
+        return tokens + pos[:, : tokens.shape[1]].float() if pos is not None else tokens
 
     def _rope(self, grid: tuple[int, int], n_text: int):
         key = (grid, n_text)
