@@ -311,8 +311,9 @@ class CudaIris:
         ``y_pos_embedding``, ``dit.py:263-281``) runs on this engine's kernels.
         Any other adapter (the masked ``lap_blocks2`` transformer over
         ``[B, T, layers, dim]`` states) runs through the upstream module the
-        engine was built from, under BF16 autocast, as ``MetalIris.encode_text``
-        does (``src/iris_metal/model.py:133-145``); it then needs ``mask``."""
+        engine was built from, under autocast to its linear weights' dtype, as
+        ``MetalIris.encode_text`` does (``src/iris_metal/model.py:133-145``); it
+        then needs ``mask``."""
         if self.text_adapter is None:
             return self._encode_text_upstream(states, mask)
         w, b, norm_w, pos = self.text_adapter
@@ -339,7 +340,10 @@ class CudaIris:
         if mask is None:
             raise ValueError(f"encode_text: the {self.cfg.text_adapter!r} text adapter needs the encoder's [B, T] mask")
         n = self.cfg.text_len
-        with torch.autocast("cuda", dtype=torch.bfloat16):
+        # autocast to the adapter's linear storage dtype, none for FP32 (model.py:128,141-144)
+        modules = y_embedder.modules() if isinstance(y_embedder, torch.nn.Module) else ()
+        dtype = next((m.weight.dtype for m in modules if isinstance(m, torch.nn.Linear)), torch.bfloat16)
+        with torch.autocast("cuda", dtype=dtype, enabled=dtype != torch.float32):
             tokens = y_embedder(states[:, :n].to(self.device, torch.float32), mask[:, :n].to(self.device))
         tokens = tokens.float()
         pos = getattr(self.dit, "y_pos_embedding", None)

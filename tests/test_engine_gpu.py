@@ -90,12 +90,14 @@ def test_encode_text_matches_reference(iris):
     assert rel_err(text, fx["prepared_text"]) < REL_TOL
 
 
-def test_encode_text_masked_adapter_runs_the_upstream_module(iris):
+@pytest.mark.parametrize("adapter_dtype", [torch.bfloat16, torch.float32])
+def test_encode_text_masked_adapter_runs_the_upstream_module(iris, adapter_dtype):
     """A model whose text adapter is not the linear one (the masked lap_blocks2
     transformer over [B, T, layers, dim] states): encode_text runs the module the
-    engine was built from under BF16 autocast and adds y_pos_embedding, as
-    MetalIris.encode_text does (src/iris_metal/model.py:133-145). Without the
-    mask, or without an upstream module, it raises."""
+    engine was built from, under autocast to its linear weights' dtype (none for
+    FP32), and adds y_pos_embedding, as MetalIris.encode_text does
+    (src/iris_metal/model.py:133-145). Without the mask, or without an upstream
+    module, it raises."""
     import dataclasses
 
     fx = golden("released_mha")
@@ -103,10 +105,16 @@ def test_encode_text_masked_adapter_runs_the_upstream_module(iris):
     state = {k: v.cuda() for k, v in seeded_init(_config(fx["config"]), seed=0).items()}
     gen = torch.Generator(device="cuda").manual_seed(9)
     layers = 3
-    proj = torch.nn.Linear(layers * cfg.text_dim, cfg.hidden_size).cuda()
 
-    def adapter(y, mask):  # stands in for the masked adapter: [B, T, layers, dim] + [B, T] mask
-        return proj(y.flatten(2)) * mask[..., None]
+    class Adapter(torch.nn.Module):  # stands in for the masked adapter: [B, T, layers, dim] + [B, T] mask
+        def __init__(self):
+            super().__init__()
+            self.proj = torch.nn.Linear(layers * cfg.text_dim, cfg.hidden_size).to("cuda", adapter_dtype)
+
+        def forward(self, y, mask):
+            return self.proj(y.flatten(2)) * mask[..., None]
+
+    adapter = Adapter()
 
     class Upstream:  # the attributes of an upstream IrisDiT that the engine reads
         def __init__(self):
@@ -120,7 +128,8 @@ def test_encode_text_masked_adapter_runs_the_upstream_module(iris):
     mask = torch.ones(2, cfg.text_len + 4, device="cuda", dtype=torch.bool)
     mask[0, 5:] = False
     got = engine.encode_text(states, mask)
-    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+    low = adapter_dtype != torch.float32
+    with torch.no_grad(), torch.autocast("cuda", dtype=adapter_dtype, enabled=low):
         want = adapter(states[:, : cfg.text_len], mask[:, : cfg.text_len])
     assert torch.equal(got, want.float() + state["y_pos_embedding"][:, : cfg.text_len].float())
     with pytest.raises(ValueError, match="mask"):
