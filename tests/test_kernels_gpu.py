@@ -391,6 +391,40 @@ def test_flash_attention_with_score_bound(K, gain, sharp_tail):
 
 
 # ---------------------------------------------------------- heads, layout, small
+@pytest.mark.parametrize("channels", [3, 4])
+@pytest.mark.parametrize("pixel_dtype", [torch.float32, torch.bfloat16])
+def test_pixel_embed_matches_reference(K, channels, pixel_dtype):
+    """iris_pixel_embed through the C ABI (PixelEmbedder.forward,
+    src/iris3b/nn/embeddings.py:319-328, plus the first block's pixel RMSNorm)
+    for RGB and for the depth export's widened 4-channel embedder
+    (src/iris3b/downstream/depth.py:30-38), against the fp32 restatement."""
+    from iris_b200 import _lib
+
+    B, H, W, p = 2, 32, 48, 16
+    L = (H // p) * (W // p)
+    gen = torch.Generator(device="cuda").manual_seed(21 + channels)
+    x = torch.randn(B, channels, H, W, device="cuda", generator=gen)
+    w = 0.5 * torch.randn(16, channels, device="cuda", generator=gen)
+    b = 0.1 * torch.randn(16, device="cuda", generator=gen)
+    pos = torch.randn(H * W, 16, device="cuda", generator=gen)
+    gain = torch.rand(16, device="cuda", generator=gen) + 0.5
+    pix = torch.empty(B * L * p * p, 16, device="cuda", dtype=pixel_dtype)
+    nrm = torch.empty(B * L, p * p * 16, device="cuda", dtype=torch.bfloat16)
+    code = _lib.F32 if pixel_dtype == torch.float32 else _lib.BF16
+    _lib.call("iris_pixel_embed", x.data_ptr(), w.data_ptr(), b.data_ptr(), pos.data_ptr(), pix.data_ptr(), code,
+              nrm.data_ptr(), gain.data_ptr(), 1e-6, B, channels, H, W, p, 0, L,
+              torch.cuda.current_stream().cuda_stream)  # fmt: skip
+    want = ops.pixel_regroup(ops.linear(x.permute(0, 2, 3, 1), w, b) + pos.view(H, W, 16), p)
+    got = pix.view(B * L, p * p, 16)
+    assert rel_err(got, want) < (1e-5 if pixel_dtype == torch.float32 else 1e-2)
+    want_norm = F.rms_norm(want.to(pixel_dtype).float(), (16,), gain, 1e-6)
+    assert rel_err(nrm.view(B * L, p * p, 16), want_norm) < 2e-2
+    with pytest.raises(ValueError, match="channels"):  # more than 4 input channels: rejected before any launch
+        _lib.call("iris_pixel_embed", x.data_ptr(), w.data_ptr(), b.data_ptr(), pos.data_ptr(), pix.data_ptr(), code,
+                  nrm.data_ptr(), gain.data_ptr(), 1e-6, B, 5, H, W, p, 0, L,
+                  torch.cuda.current_stream().cuda_stream)  # fmt: skip
+
+
 def test_qkv_heads_matches_oracle(K):
     from iris_b200 import _lib
 
