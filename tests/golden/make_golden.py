@@ -134,6 +134,27 @@ def _sample_fixture(model, fixture, cfg_scale=3.0, cfg_interval=(0.0, 1.5)):
             "sample": seen[0]}
 
 
+def _dpm_fixture(model, fixture, steps=10, order=2, shift=3.0, cfg_scale=3.0):
+    """The Original model's loop: the reference's ``FlowDPMSolver.sample``
+    (``src/iris3b/flow/solver.py:112-141``; 2nd-order multistep, CFG on
+    ``[uncond; cond]`` inside its default interval) driving the FP32 forward on
+    adapted text."""
+    from iris3b.flow.solver import FlowDPMSolver
+
+    prepared = fixture["prepared_text"]
+    cond, uncond = prepared[1:], prepared[:1]
+    noise = torch.randn(1, 3, fixture["x"].shape[2], fixture["x"].shape[3], generator=torch.Generator().manual_seed(7))
+
+    def velocity(x, t_model, text):
+        return model(x, t_model, text, prepared_text=text, precompute_modulation=True).x
+
+    solver = FlowDPMSolver(velocity, cfg_scale=cfg_scale)
+    with torch.no_grad():
+        sample = solver.sample(noise, cond, uncond, steps=steps, order=order, shift=shift)
+    return {"noise": noise, "cond": cond, "uncond": uncond, "steps": steps, "order": order, "shift": shift,
+            "cfg_scale": cfg_scale, "cfg_interval": solver.cfg_interval, "sample": sample}
+
+
 def _turbo_fixture(model, fixture):
     """The Turbo recipe (``IrisPipeline._turbo``, ``src/iris_metal/pipeline.py:372-428``)
     on the toy model: every Linear weight and bias stored in BF16
@@ -327,6 +348,7 @@ def main():
         if name == "released_mha":
             fixture["euler_cfg"] = _sample_fixture(model, fixture)
             fixture["turbo"] = _turbo_fixture(model, fixture)
+            fixture["dpm"] = _dpm_fixture(model, fixture)
             fixture["depth"] = _depth_fixture(cfg, fixture, ModelConfig, PixelStageConfig)
         torch.save(fixture, HERE / f"{name}.pt")
         print(name, "saved", tuple(fixture["v"].shape), float(fixture["v"].abs().max()))

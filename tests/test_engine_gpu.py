@@ -150,6 +150,24 @@ def test_euler_cfg_sample_matches_reference(iris):
     assert value >= PSNR_MIN
 
 
+def test_dpm_solver_sample_matches_reference(iris):
+    """The Original model's loop: iris_b200.FlowDPMSolver (fused CFG + DPM-Solver++
+    step per kernel) driving the engine, against the reference's FlowDPMSolver
+    driving IrisDiT (src/iris3b/flow/solver.py:112-141; 10 steps, 2nd order,
+    shift 3, CFG 3 inside the default interval)."""
+    fx = golden("released_mha")
+    cfg = _config(fx["config"])
+    engine = _engine(iris, cfg, seeded_init(cfg, seed=0))
+    d = fx["dpm"]
+    solver = iris.FlowDPMSolver(engine, cfg_scale=d["cfg_scale"], cfg_interval=d["cfg_interval"])
+    sample = solver.sample(d["noise"].cuda(), d["cond"].cuda(), d["uncond"].cuda(), steps=d["steps"], order=d["order"],
+                           shift=d["shift"])  # fmt: skip
+    value = psnr(sample, d["sample"])
+    print(f"dpm-solver++ 10-step sample: psnr {value:.1f} dB, max rel err {rel_err(sample, d['sample']):.2e}")
+    assert value > PSNR_MIN
+    assert rel_err(sample, d["sample"]) < REL_TOL
+
+
 def test_turbo_four_step_sample_without_cfg(iris):
     """The Turbo loop (generate_few_step, src/iris3b/sampling.py:98-138: four
     deterministic Euler steps at TURBO_SIGMAS, no CFG) on the engine against

@@ -49,6 +49,19 @@ def test_oracle_euler_cfg_matches_reference():
     torch.testing.assert_close(sample, s["sample"], rtol=1e-4, atol=1e-5)
 
 
+def test_oracle_dpm_sample_of_the_model_matches_reference():
+    """The reference's FlowDPMSolver.sample (10 steps, 2nd order, shift 3, CFG 3)
+    driving IrisDiT, restated: the oracle solver driving the oracle model."""
+    fx = golden("released_mha")
+    cfg = _config(fx["config"])
+    model = OracleModel(cfg, seeded_init(cfg, seed=0))
+    d = fx["dpm"]
+    solver = FlowDPMSolverOracle(model, cfg_scale=d["cfg_scale"], cfg_interval=d["cfg_interval"])
+    with torch.no_grad():
+        sample = solver.sample(d["noise"], d["cond"], d["uncond"], steps=d["steps"], order=d["order"], shift=d["shift"])
+    torch.testing.assert_close(sample, d["sample"], rtol=1e-4, atol=1e-4)
+
+
 def turbo_params(cfg, linear):
     """Seeded weights with every Linear weight and bias rounded to BF16: the
     values a Turbo checkpoint stores (src/iris_metal/loading.py:20-38)."""
