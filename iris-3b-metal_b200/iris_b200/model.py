@@ -340,7 +340,7 @@ class CudaIris:
         if mask is None:
             raise ValueError(f"encode_text: the {self.cfg.text_adapter!r} text adapter needs the encoder's [B, T] mask")
         n = self.cfg.text_len
-        # autocast to the adapter's linear storage dtype, none for FP32 (model.py:128,141-144)
+        # autocast to the adapter's linear storage dtype, none for FP32 (src/iris_metal/model.py:128,141-144)
         modules = y_embedder.modules() if isinstance(y_embedder, torch.nn.Module) else ()
         dtype = next((m.weight.dtype for m in modules if isinstance(m, torch.nn.Linear)), torch.bfloat16)
         with torch.autocast("cuda", dtype=dtype, enabled=dtype != torch.float32):
