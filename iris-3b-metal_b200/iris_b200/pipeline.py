@@ -4,8 +4,10 @@ The reference's ``IrisPipeline.__call__`` (``src/iris_metal/pipeline.py:265-330`
 encodes prompts with Qwen3-VL, adapts them once, draws CPU-seeded noise, runs
 the sampler and returns images. Prompt encoding is outside this build; this
 pipeline starts from text-encoder states (or adapted text) and keeps the rest:
-host noise copied in, text adapted once per call, the guided Euler loop on the
-device, ``require_finite`` on the pre-clamp sample, the result copied back.
+host noise copied in, text adapted once per call, the sampler on the device
+(the Turbo few-step guided Euler loop, or with ``steps`` the Original model's
+multistep DPM-Solver++), ``require_finite`` on the pre-clamp sample, the
+result copied back.
 """
 
 from __future__ import annotations
@@ -13,15 +15,31 @@ from __future__ import annotations
 import torch
 
 from iris_b200.model import CudaIris, require_finite
-from iris_b200.sampling import TURBO_SIGMAS, euler_cfg
+from iris_b200.sampling import TURBO_SIGMAS, FlowDPMSolver, euler_cfg
 
 
 class DenoisePipeline:
-    def __init__(self, engine: CudaIris, cfg_scale: float = 3.0, sigmas=TURBO_SIGMAS, cfg_interval=(0.0, 1.5)):
+    def __init__(
+        self,
+        engine: CudaIris,
+        cfg_scale: float = 3.0,
+        sigmas=TURBO_SIGMAS,
+        cfg_interval=(0.0, 1.5),
+        *,
+        steps: int | None = None,
+        order: int = 2,
+        shift: float = 1.0,
+    ):
+        """``steps=None``: the few-step Euler loop at ``sigmas`` (Turbo,
+        ``src/iris3b/sampling.py:98-138``). ``steps=N``: ``FlowDPMSolver.sample``
+        with ``N`` steps of ``order`` on the ``shift``-ed grid (the Original
+        model's loop, ``src/iris3b/flow/solver.py:112-141``; its default CFG
+        interval there is ``(0, 1)``)."""
         self.engine = engine
         self.cfg_scale = cfg_scale
         self.sigmas = tuple(sigmas)
         self.cfg_interval = cfg_interval
+        self.steps, self.order, self.shift = steps, order, shift
 
     @torch.no_grad()
     def __call__(
@@ -45,10 +63,14 @@ class DenoisePipeline:
         else:
             cond = self.engine.encode_text(cond_states)
             uncond = None if uncond_states is None else self.engine.encode_text(uncond_states)
-        sample = euler_cfg(
-            self.engine, x, cond, uncond, cfg_scale=self.cfg_scale, sigmas=self.sigmas,
-            cfg_interval=self.cfg_interval, check=require_finite,
-        )  # fmt: skip
+        if self.steps is None:
+            sample = euler_cfg(
+                self.engine, x, cond, uncond, cfg_scale=self.cfg_scale, sigmas=self.sigmas,
+                cfg_interval=self.cfg_interval, check=require_finite,
+            )  # fmt: skip
+        else:
+            solver = FlowDPMSolver(self.engine, cfg_scale=self.cfg_scale, cfg_interval=self.cfg_interval)
+            sample = require_finite(solver.sample(x, cond, uncond, steps=self.steps, order=self.order, shift=self.shift))
         sample = sample.clamp_(-1, 1)
         if out is not None:
             out.copy_(sample, non_blocking=True)

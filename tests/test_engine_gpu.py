@@ -168,6 +168,22 @@ def test_dpm_solver_sample_matches_reference(iris):
     assert rel_err(sample, d["sample"]) < REL_TOL
 
 
+def test_pipeline_runs_the_original_dpm_loop(iris):
+    """DenoisePipeline with ``steps``: host noise and adapted text in, the
+    DPM-Solver++ loop on the device, the clamped sample out into host memory."""
+    fx = golden("released_mha")
+    cfg = _config(fx["config"])
+    engine = _engine(iris, cfg, seeded_init(cfg, seed=0))
+    d = fx["dpm"]
+    pipe = iris.DenoisePipeline(engine, cfg_scale=d["cfg_scale"], cfg_interval=d["cfg_interval"], steps=d["steps"],
+                                order=d["order"], shift=d["shift"])  # fmt: skip
+    out = torch.empty_like(d["noise"]).pin_memory()
+    got = pipe(d["noise"], d["cond"], d["uncond"], adapted=True, out=out)
+    torch.cuda.synchronize()
+    assert got is out
+    assert psnr(out, d["sample"].clamp(-1, 1)) > PSNR_MIN
+
+
 def test_turbo_four_step_sample_without_cfg(iris):
     """The Turbo loop (generate_few_step, src/iris3b/sampling.py:98-138: four
     deterministic Euler steps at TURBO_SIGMAS, no CFG) on the engine against
