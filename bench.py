@@ -142,6 +142,23 @@ class ClockSampler:
         }
 
 
+MODEL = ("iris-3b-shaped: d3072, 8 dual + 16 single-stream blocks, 24 MHA heads x 128, SwiGLU 8192, "
+         "4 post-modulated PiT blocks; random-init weights (std 0.02)")
+
+
+def bench_config(world: int) -> dict:
+    """The ``config`` of the default workload's JSON line; both arms print the same dict."""
+    return {
+        "workload": WORKLOAD,
+        "model": MODEL,
+        "global_batch": IMAGES,
+        "rows_per_call_per_gpu": 2 * (IMAGES // world + (1 if IMAGES % world else 0)),
+        "seq_len": 4352,
+        "parallelism": f"dp{world}",
+        "l2": "no flush: every step streams 8.7 GB of weights, far above the 126 MB L2",
+    }
+
+
 def make_inputs(seed_noise: int = 0, seed_text: int = 4):
     gen = torch.Generator().manual_seed(seed_noise)
     noise = torch.randn(IMAGES, 3, RESOLUTION, RESOLUTION, generator=gen)
@@ -205,8 +222,7 @@ def reference_arm(args, rank: int) -> None:
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": WORKLOAD, "model": "iris-3b-shaped d3072 (BASELINE config 3), random weights",
-                   "global_batch": IMAGES, "seq_len": 4352, "parallelism": "host cores"},  # fmt: skip
+        "config": bench_config(args.gpus),
         "cpu_baseline": {
             "value": value,
             "unit": UNIT,
@@ -339,17 +355,109 @@ def fused_ops(args) -> None:
     print(json.dumps(line), flush=True)
 
 
-def step2048(args, rank: int, world: int, local: int) -> None:
-    """one B = 2 (CFG pair) denoiser call at 2048^2 per step,
-    Ulysses sequence parallelism over the ranks (the call's tokens are split,
-    every rank returns the whole velocity)."""
+RES_2048 = 2048
+
+
+def inputs_2048(engine, device):
+    """Config 5 inputs: one seeded 2048^2 noise image as the CFG pair, text states
+    [uncond; cond] adapted by the engine, model time 625."""
+    gen = torch.Generator().manual_seed(1)
+    x_h = torch.randn(1, 3, RES_2048, RES_2048, generator=gen).repeat(2, 1, 1, 1).pin_memory()
+    states = torch.randn(2, TEXT_LEN, TEXT_DIM, generator=torch.Generator().manual_seed(4)).to(device)
+    text = engine.encode_text(states)
+    return x_h, text, torch.full((2,), 625.0, device=device)
+
+
+def time_calls(fn, steps: int, warmup: int, world: int, local: int, device) -> float:
+    """ms per ``fn()`` over ``steps`` calls after ``warmup`` untimed ones; CUDA events
+    on the current stream, barrier + synchronize on both sides, max over ranks."""
     import torch.distributed as dist
 
-    from iris_b200 import CudaIris, IrisWeights, _lib, baseline_step_config, synthetic_state
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    ms = s.elapsed_time(e) / steps
+    if world > 1:
+        m = torch.tensor([ms], device=device, dtype=torch.float64)
+        dist.all_reduce(m, op=dist.ReduceOp.MAX)
+        ms = float(m.item())
+    return ms
+
+
+def measure_2048(engine, single, rank: int, world: int, local: int, steps: int, warmup: int, e2e: bool = False) -> dict:
+    """one B = 2 call at 2048^2 per step on ``engine``
+    (Ulysses sequence parallel over the ranks when it has a communicator).
+    With N > 1, rank 0 also runs the same call on ``single`` (one GPU, no
+    communicator) and reports the max relative error of the sequence-parallel
+    velocity against it."""
+    from iris_b200 import _lib
+
+    device = torch.device("cuda", local)
+    x_h, text, t = inputs_2048(engine, device)
+    x = x_h.to(device)
+    launches0 = _lib.launch_count()
+    with ClockSampler(local) as clocks:
+        ms = time_calls(lambda: engine(x, t, text), steps, warmup, world, local, device)
+    launches = (_lib.launch_count() - launches0) // (steps + warmup)
+    flops = step_flops(2, L=(RES_2048 // 16) ** 2)
+    pk = peaks()
+    per_gpu = flops / world / (ms / 1e3) / 1e12
+    record = {
+        "ms_per_step": ms,
+        "n_gpus": world,
+        "parallelism": f"ulysses{world}" if world > 1 else "one GPU",
+        "steps": steps,
+        "warmup": warmup,
+        "step_tflop": flops / 1e12,
+        "tflops_per_gpu": per_gpu,
+        "frac_of_bf16_sustained": per_gpu / pk["bf16_sustained"],
+        "gpu_launches_per_step": launches,
+        "clocks": clocks.summary(),
+    }
+    if e2e:
+        text_h = text.cpu().pin_memory()
+        v_h = torch.empty_like(x_h).pin_memory()
+
+        def through_host():
+            xd = x_h.to(device, non_blocking=True)
+            td = text_h.to(device, non_blocking=True)
+            v_h.copy_(engine(xd, t, td), non_blocking=True)
+
+        record["e2e_ms"] = time_calls(through_host, steps, warmup, world, local, device)
+        record["h2d_bytes_per_step"] = x_h.numel() * 4 + text_h.numel() * 4
+        record["d2h_bytes_per_step"] = v_h.numel() * 4
+    if world > 1:
+        import torch.distributed as dist
+
+        v = engine(x, t, text)
+        if rank == 0:
+            ref = single(x, t, text)
+            err = float((v.double() - ref.double()).abs().max() / ref.double().abs().max())
+            record["max_rel_err_vs_one_gpu"] = err
+        torch.cuda.synchronize()
+        dist.barrier(device_ids=[local])
+    return record
+
+
+def step2048(args, rank: int, world: int, local: int) -> None:
+    """BASELINE config 5 as the whole bench line (``--workload step2048``)."""
+    import torch.distributed as dist
+
+    from iris_b200 import CudaIris, IrisWeights, baseline_step_config, synthetic_state
     from iris_b200.parallel import init_process_group
     from iris_b200.ulysses import TorchComm
 
-    res = 2048
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     comm = None
@@ -357,60 +465,16 @@ def step2048(args, rank: int, world: int, local: int) -> None:
         init_process_group("nccl", timeout_s=600)
         comm = TorchComm()
     cfg = baseline_step_config()
-    engine = CudaIris(IrisWeights(cfg, synthetic_state(cfg, device, seed=0)), comm=comm)
-    gen = torch.Generator().manual_seed(1)
-    x_h = torch.randn(1, 3, res, res, generator=gen).repeat(2, 1, 1, 1).pin_memory()
-    tgen = torch.Generator().manual_seed(4)
-    states = torch.randn(2, TEXT_LEN, TEXT_DIM, generator=tgen).to(device)  # row 0 uncond, row 1 cond
-    text = engine.encode_text(states)
-    text_h = text.cpu().pin_memory()
-    t = torch.full((2,), 625.0, device=device)
-    x = x_h.to(device)
-
-    def barrier():
-        if world > 1:
-            dist.barrier(device_ids=[local])
-
-    def max_over_ranks(value: float) -> float:
-        if world == 1:
-            return value
-        m = torch.tensor([value], device=device, dtype=torch.float64)
-        dist.all_reduce(m, op=dist.ReduceOp.MAX)
-        return float(m.item())
-
-    def timed(fn):
-        for _ in range(args.warmup):
-            fn()
-        torch.cuda.synchronize()
-        barrier()
-        torch.cuda.synchronize()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        for _ in range(args.steps):
-            fn()
-        e.record()
-        torch.cuda.synchronize()
-        barrier()
-        return max_over_ranks(s.elapsed_time(e) / args.steps)
-
-    launches0 = _lib.launch_count()
-    with ClockSampler(local) as clocks:
-        ms = timed(lambda: engine(x, t, text))
-    launches = (_lib.launch_count() - launches0) // (args.steps + args.warmup)
-    v_h = torch.empty_like(x_h).pin_memory()
-
-    def e2e():
-        xd = x_h.to(device, non_blocking=True)
-        td = text_h.to(device, non_blocking=True)
-        v_h.copy_(engine(xd, t, td), non_blocking=True)
-
-    e_ms = timed(e2e)
+    weights = IrisWeights(cfg, synthetic_state(cfg, device, seed=0))
+    engine = CudaIris(weights, comm=comm)
+    single = CudaIris(weights) if world > 1 and rank == 0 else None
+    rec = measure_2048(engine, single, rank, world, local, args.steps, args.warmup, e2e=True)
+    engine.close()
     if rank != 0:
         dist.destroy_process_group()
         return
-    flops = step_flops(2, L=(res // 16) ** 2)
     pk = peaks()
-    per_gpu = flops / world / (ms / 1e3) / 1e12
+    ms = rec["ms_per_step"]
     line = {
         "metric": "ms per denoise step at 2048² (B=2 CFG), Ulysses sequence parallel over N B200",
         "value": ms,
@@ -426,30 +490,31 @@ def step2048(args, rank: int, world: int, local: int) -> None:
         "data": "synthetic",
         "config": {
             "workload": "BASELINE config 5: one guided denoiser call (B=2: [uncond; cond]) at 2048^2, t = 625, "
-            "tokens split across N GPUs (Ulysses all-to-all around attention, all-gathered pixel K/V)",
-            "model": "iris-3b-shaped: d3072, 8 dual + 16 single-stream blocks, 24 MHA heads x 128, SwiGLU 8192, "
-            "4 post-modulated PiT blocks; random-init weights (std 0.02)",
+            "tokens split across N GPUs (Ulysses: the producing kernels store Q/K/V and attention rows into "
+            "the owning rank's memory over NVLink)",
+            "model": MODEL,
             "global_batch": 2,
-            "seq_len": 256 + (res // 16) ** 2,
+            "seq_len": 256 + (RES_2048 // 16) ** 2,
             "parallelism": f"ulysses{world}",
-            "step_tflop": flops / 1e12,
             "l2": "no flush: every step streams 8.7 GB of weights, far above the 126 MB L2",
         },
         "roofline": {
             "kernel": "whole step (GEMMs + attention), per GPU",
             "bound": "tensor",
-            "achieved": per_gpu,
+            "achieved": rec["tflops_per_gpu"],
             "peak": pk["bf16_sustained"],
             "unit": "TFLOP/s",
-            "frac": per_gpu / pk["bf16_sustained"],
+            "frac": rec["frac_of_bf16_sustained"],
             "traffic": None,
             "peak_source": f"{pk['source']} bf16 sustained",
         },
-        "e2e": {"value": e_ms, "unit": "ms", "h2d_bytes_per_step": x_h.numel() * 4 + text_h.numel() * 4,
-                "d2h_bytes_per_step": v_h.numel() * 4},  # fmt: skip
-        "gpu_launches": launches * args.steps,
-        "clocks": clocks.summary(),
+        "e2e": {"value": rec["e2e_ms"], "unit": "ms", "h2d_bytes_per_step": rec["h2d_bytes_per_step"],
+                "d2h_bytes_per_step": rec["d2h_bytes_per_step"]},  # fmt: skip
+        "gpu_launches": rec["gpu_launches_per_step"] * args.steps,
+        "clocks": rec["clocks"],
     }
+    if "max_rel_err_vs_one_gpu" in rec:
+        line["max_rel_err_vs_one_gpu"] = rec["max_rel_err_vs_one_gpu"]
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
@@ -494,10 +559,10 @@ def main() -> None:
     if world > 1:
         init_process_group("nccl", timeout_s=600)
     cfg = baseline_step_config()
-    engine = CudaIris(IrisWeights(cfg, synthetic_state(cfg, device, seed=0)))
+    weights = IrisWeights(cfg, synthetic_state(cfg, device, seed=0))
+    engine = CudaIris(weights)
     noise, cond_states, uncond_states = make_inputs()
     lo, hi = image_shard(IMAGES, rank, world)
-    n_local = hi - lo
     noise_d = noise[lo:hi].to(device)
     cond = engine.encode_text(cond_states[lo:hi].to(device))
     uncond = engine.encode_text(uncond_states.to(device))
@@ -561,21 +626,28 @@ def main() -> None:
     d2h = out_h.numel() * out_h.element_size()
 
     # ---------------------------------------------------- one B = 2 denoiser call (rank 0)
-    b2_ms = None
+    b2 = None
     if rank == 0:
         x2 = noise_d[:1].repeat(2, 1, 1, 1)
         text2 = torch.cat([uncond, cond[:1]])
         t2 = torch.full((2,), 625.0, device=device)
-        for _ in range(3):
-            engine(x2, t2, text2)
-        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
-        s2.record()
-        for _ in range(5):
-            engine(x2, t2, text2)
-        e2.record()
-        torch.cuda.synchronize()
-        b2_ms = s2.elapsed_time(e2) / 5
+        with ClockSampler(local) as b2_clocks:
+            b2_ms = time_calls(lambda: engine(x2, t2, text2), 10, 3, 1, local, device)
+        b2_tflops = step_flops(2) / (b2_ms / 1e3) / 1e12
+        b2 = {"ms": b2_ms, "tflop": step_flops(2) / 1e12, "tflops": b2_tflops,
+              "frac_of_bf16_burst": b2_tflops / peaks()["bf16"], "calls": 10, "warmup": 3,
+              "clocks": b2_clocks.summary()}  # fmt: skip
+
+    # ------------------------------------- BASELINE config 5 (2048^2) on the same N GPUs
+    sp_engine = engine
+    if world > 1:
+        from iris_b200.ulysses import TorchComm
+
+        sp_engine = CudaIris(weights, comm=TorchComm())
+    step2048_rec = measure_2048(sp_engine, engine, rank, world, local, min(args.steps, 5), 3)
+    if sp_engine is not engine:
+        sp_engine.close()
+        del sp_engine
 
     pk = peaks()
     achieved = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms else None
@@ -596,7 +668,6 @@ def main() -> None:
         if world > 1:
             dist.destroy_process_group()
         return
-    flops_per_call = step_flops(2)
     line = {
         "metric": METRIC,
         "value": value,
@@ -610,18 +681,7 @@ def main() -> None:
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic",
-        "config": {
-            "workload": WORKLOAD,
-            "model": "iris-3b-shaped: d3072, 8 dual + 16 single-stream blocks, 24 MHA heads x 128, SwiGLU 8192, "
-            "4 post-modulated PiT blocks; random-init weights (std 0.02)",
-            "global_batch": IMAGES,
-            "rows_per_call_per_gpu": 2 * n_local,
-            "seq_len": 4352,
-            "parallelism": f"dp{world}",
-            "ms_per_denoise_step_b2": b2_ms,
-            "b2_step_tflops": (flops_per_call / (b2_ms / 1e3) / 1e12) if b2_ms else None,
-            "l2": "no flush: every step streams 8.7 GB of weights, far above the 126 MB L2",
-        },
+        "config": bench_config(world),
         "roofline": {
             "kernel": "gemm_bf16_pair_kernel (tcgen05 cta_group::2, all GEMM launches of the timed region)",
             "bound": "tensor",
@@ -639,6 +699,8 @@ def main() -> None:
         "e2e": {"value": IMAGES / (e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": launches * args.steps,
         "clocks": clocks.summary(),
+        "denoise_step_b2": b2,
+        "step2048": step2048_rec,
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu

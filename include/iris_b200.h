@@ -344,6 +344,14 @@ int iris_dpm_update(const float* v, const float* x, const float* x0_prev, float*
  * every x[i] is finite, else 0. */
 int iris_all_finite(const float* x, int64_t n, int* flag, void* stream);
 
+/* The raise-rather-than-return-a-bad-result contract of require_finite
+ * (src/iris_metal/model.py:102-110) extended to bounded waits, which the
+ * reference does not have: if the device error word has a bit of `mask` set
+ * (bit 0: a kernel's or a peer barrier's bounded wait gave up, so buffers the
+ * result depends on may be stale), x[0..n) is overwritten with NaN. Enqueued
+ * after every denoiser call; no host synchronisation. */
+int iris_poison_on_error(float* x, int64_t n, unsigned int mask, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

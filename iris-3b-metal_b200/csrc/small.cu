@@ -9,6 +9,7 @@
 //   dpm_update               CFG combine + x0 prediction + DPM-Solver++ (1st/2nd order) step,
 //                            src/iris3b/flow/solver.py:58-109
 //   all_finite               require_finite, src/iris_metal/model.py:102-110
+//   poison_on_error          NaN-fill of a result computed after a timed-out bounded wait
 #include "common.cuh"
 #include "iris_abi_internal.h"
 
@@ -204,6 +205,17 @@ __global__ void all_finite_kernel(const float* __restrict__ x, int64_t n, int* f
 
 __global__ void set_int_kernel(int* p, int v) { *p = v; }
 
+// x[i] = NaN for every i when the device error word has a bit of `mask` set
+// (a bounded wait gave up earlier on this device); otherwise every thread
+// reads the word once and leaves.
+__global__ void poison_on_error_kernel(float* __restrict__ x, int64_t n, unsigned int mask) {
+  if ((*reinterpret_cast<volatile unsigned int*>(&g_device_error) & mask) == 0u) return;
+  const float nan = __int_as_float(0x7fc00000);
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    x[i] = nan;
+}
+
 // Block (i0, i1, i2) of `vecs` 16-byte vectors: src + i0 s0 + i1 s1 + i2 s2 ->
 // dst + i0 d0 + i1 d1 + i2 d2 (byte strides). One CTA item = 1024 vectors of a
 // block, 4 per thread with all loads issued before the stores.
@@ -353,6 +365,16 @@ extern "C" int iris_all_finite(const float* x, int64_t n, int* flag, void* strea
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   set_int_kernel<<<1, 1, 0, st>>>(flag, 1);
   if (n > 0) all_finite_kernel<<<grid_for(n, 8), THREADS, 0, st>>>(x, n, flag);
+  IRIS_CUDA(cudaGetLastError());
+  return IRIS_OK;
+}
+
+extern "C" int iris_poison_on_error(float* x, int64_t n, unsigned int mask, void* stream) {
+  using namespace iris::small;
+  IRIS_REQUIRE(x != nullptr || n == 0, "poison_on_error: null pointer");
+  IRIS_REQUIRE(n >= 0, "poison_on_error: negative size");
+  if (n == 0 || mask == 0u) return IRIS_OK;
+  poison_on_error_kernel<<<grid_for(n, 8), THREADS, 0, static_cast<cudaStream_t>(stream)>>>(x, n, mask);
   IRIS_CUDA(cudaGetLastError());
   return IRIS_OK;
 }

@@ -47,6 +47,7 @@ SIGNATURES: dict[str, list] = {
     "iris_cfg_euler": [P, P, P, I64, I64, F, F, F, I32, P],
     "iris_dpm_update": [P, P, P, P, P, I64, I64, F, I32, F, I32, F, F, F, P],
     "iris_all_finite": [P, I64, P, P],
+    "iris_poison_on_error": [P, I64, ctypes.c_uint, P],
 }
 
 class HeadsEpilogue(ctypes.Structure):

@@ -94,13 +94,32 @@ def pack_swiglu(w1: torch.Tensor, w3: torch.Tensor, w2: torch.Tensor, tile: int 
     return w13.reshape(2 * pad, d).contiguous(), w2p
 
 
+ERR_WAIT_TIMEOUT = 1  # bit of the device error word: a kernel's bounded wait gave up
+
+
+class DeviceWaitTimeout(RuntimeError):
+    """A bounded wait on the device gave up: a sequence-parallel peer did not
+    reach a barrier in time, or a tensor-core pipeline stage never completed.
+    Buffers the result depends on may be stale, so the result is rejected."""
+
+
 def require_finite(result: torch.Tensor) -> torch.Tensor:
     """Raise rather than let an overflowed result become a black image
-    (``src/iris_metal/model.py:102-110``); one device flag, one sync."""
+    (``src/iris_metal/model.py:102-110``); one device flag, one sync. The same
+    sync reads the device error word: a result computed after a timed-out
+    bounded wait raises :class:`DeviceWaitTimeout` (the engine has also filled
+    it with NaN, so callers that only test finiteness reject it too)."""
     flag = torch.empty(1, device=result.device, dtype=torch.int32)
     data = result.float().contiguous()
     _lib.call("iris_all_finite", data.data_ptr(), data.numel(), flag.data_ptr(), K.stream_of(data))
-    if int(flag.item()) != 1:
+    finite = int(flag.item()) == 1
+    if K.device_error(clear=False, device=result.device) & ERR_WAIT_TIMEOUT:
+        K.device_error(clear=True, device=result.device)
+        raise DeviceWaitTimeout(
+            "a bounded wait on the device timed out (a sequence-parallel rank stopped answering, or a kernel "
+            "pipeline stalled); the result was discarded"
+        )
+    if not finite:
         raise FloatingPointError("the model produced non-finite values; please report the input and settings")
     return result
 
@@ -541,6 +560,9 @@ class CudaIris:
         else:  # every rank writes its own patches; the sum assembles the image
             v = torch.zeros(batch, out_channels, height, width, device=dev, dtype=torch.float32)
         self._pixel_stage(x, ws, geom, grid, pcos, psin, pos, v, eps, st, capture)
+        # a bounded wait that gave up (dead peer, stalled pipeline) leaves stale buffers behind:
+        # the velocity becomes NaN (before the sum, so every rank's copy does) and require_finite raises
+        _lib.call("iris_poison_on_error", v.data_ptr(), v.numel(), ERR_WAIT_TIMEOUT, st)
         if comm is not None:
             comm.all_reduce_sum(v)
         return v

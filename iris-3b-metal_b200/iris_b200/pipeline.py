@@ -55,14 +55,28 @@ class DenoisePipeline:
         ``[k, T, text_dim]`` / ``[1, T, text_dim]`` (or adapted ``[.., T, D]`` with
         ``adapted=True``). Returns the clamped sample, in ``out`` when given
         (e.g. pinned host memory), else on the noise's device."""
+        if self.steps is not None and self.steps < 1:
+            raise ValueError("DenoisePipeline: steps must be at least 1")
+        if self.steps is None and not self.sigmas:
+            raise ValueError("DenoisePipeline: sigmas must not be empty")
         dev = self.engine.device
         x = noise.to(dev, non_blocking=True)
+        images = x.shape[0]
         if adapted:
             cond = cond_states.to(dev)
             uncond = None if uncond_states is None else uncond_states.to(dev)
         else:
             cond = self.engine.encode_text(cond_states)
             uncond = None if uncond_states is None else self.engine.encode_text(uncond_states)
+        # one prompt (or one unconditional row) for every image, as the reference expands them
+        # (src/iris_metal/pipeline.py:297-298)
+        if cond.shape[0] not in (1, images):
+            raise ValueError(f"cond text has {cond.shape[0]} rows for {images} images")
+        cond = cond.expand(images, -1, -1)
+        if uncond is not None:
+            if uncond.shape[0] not in (1, images):
+                raise ValueError(f"uncond text has {uncond.shape[0]} rows for {images} images")
+            uncond = uncond.expand(images, -1, -1)
         if self.steps is None:
             sample = euler_cfg(
                 self.engine, x, cond, uncond, cfg_scale=self.cfg_scale, sigmas=self.sigmas,
@@ -71,7 +85,7 @@ class DenoisePipeline:
         else:
             solver = FlowDPMSolver(self.engine, cfg_scale=self.cfg_scale, cfg_interval=self.cfg_interval)
             sample = require_finite(solver.sample(x, cond, uncond, steps=self.steps, order=self.order, shift=self.shift))
-        sample = sample.clamp_(-1, 1)
+        sample = sample.clamp(-1, 1)  # out of place: never the caller's noise tensor
         if out is not None:
             out.copy_(sample, non_blocking=True)
             return out

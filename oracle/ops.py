@@ -99,7 +99,12 @@ def sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
         rep = q.shape[1] // k.shape[1]
         k = k.repeat_interleave(rep, dim=1)
         v = v.repeat_interleave(rep, dim=1)
-    return F.scaled_dot_product_attention(q, k, v)
+    # long sequences (2048^2: 16640 tokens) in query chunks, so that an fp32 score
+    # matrix never has more than 2^31 entries; rows are independent, the math is unchanged
+    rows = max(1, (1 << 31) // max(1, q.shape[0] * q.shape[1] * k.shape[2]))
+    if q.shape[2] <= rows:
+        return F.scaled_dot_product_attention(q, k, v)
+    return torch.cat([F.scaled_dot_product_attention(c, k, v) for c in q.split(rows, dim=2)], dim=2)
 
 
 # -- index maps (integer layouts, bit-exact) ------------------------------------

@@ -184,6 +184,31 @@ def test_pipeline_runs_the_original_dpm_loop(iris):
     assert psnr(out, d["sample"].clamp(-1, 1)) > PSNR_MIN
 
 
+@pytest.mark.parametrize("steps", [None, 10])
+def test_pipeline_expands_one_unconditional_row(iris, steps):
+    """Two images with one shared unconditional row (and one with a one-row
+    prompt) through both loops, as the reference pipeline expands them
+    (src/iris_metal/pipeline.py:297-298): image 0 reproduces the reference's
+    sample; image 1 matches a one-image call on its own noise. The caller's
+    noise is left untouched."""
+    fx = golden("released_mha")
+    cfg = _config(fx["config"])
+    engine = _engine(iris, cfg, seeded_init(cfg, seed=0))
+    d = fx["dpm"] if steps else fx["euler_cfg"]
+    kw = {"steps": d["steps"], "order": d["order"], "shift": d["shift"]} if steps else {}
+    pipe = iris.DenoisePipeline(engine, cfg_scale=d["cfg_scale"], cfg_interval=d["cfg_interval"], **kw)
+    other = torch.randn(d["noise"].shape, generator=torch.Generator().manual_seed(11))
+    noise = torch.cat([d["noise"], other]).cuda()
+    before = noise.clone()
+    both = pipe(noise, d["cond"], d["uncond"], adapted=True)
+    assert torch.equal(noise, before), "the pipeline must not write the caller's noise"
+    alone = pipe(other.cuda(), d["cond"], d["uncond"], adapted=True)
+    assert psnr(both[:1], d["sample"].clamp(-1, 1)) > PSNR_MIN
+    assert psnr(both[1:], alone) > PSNR_MIN
+    with pytest.raises(ValueError, match="rows for 2 images"):
+        pipe(noise, torch.cat([d["cond"]] * 3), d["uncond"], adapted=True)
+
+
 def test_turbo_four_step_sample_without_cfg(iris):
     """The Turbo loop (generate_few_step, src/iris3b/sampling.py:98-138: four
     deterministic Euler steps at TURBO_SIGMAS, no CFG) on the engine against

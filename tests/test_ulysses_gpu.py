@@ -223,6 +223,39 @@ def test_peer_barrier_wait_runs_out_and_reports(iris):
     assert K.device_error(clear=True) == 0 and int(peer[0]) == 8
 
 
+def test_timed_out_wait_makes_the_result_raise(iris):
+    """After a bounded wait has given up (the barrier on a flag nothing sets, as
+    above), the next denoiser call's velocity is NaN-filled on the device and
+    require_finite raises DeviceWaitTimeout naming the timeout (no host sync
+    inside the call); the error word is then cleared and the engine recovers.
+    The pipeline, which calls require_finite, raises the same way."""
+    from iris_b200 import kernels as K
+    from iris_b200.model import DeviceWaitTimeout
+
+    fx = golden("released_mha")
+    cfg = _config(fx["config"])
+    engine = iris.CudaIris(iris.IrisWeights(cfg, {k: v.cuda() for k, v in seeded_init(cfg, seed=0).items()}))
+    x, t, text = fx["x"].cuda(), fx["t"].cuda(), fx["prepared_text"].cuda()
+    K.device_error(clear=True)
+    flags = torch.zeros(2, dtype=torch.int32, device="cuda")
+    peer = torch.zeros(2, dtype=torch.int32, device="cuda")
+    K.peer_barrier(flags, [0, peer.data_ptr()], 0, 1, timeout_s=0.02)
+    v = engine(x, t, text)
+    assert torch.isnan(v).all(), "a result computed after a timed-out wait must not look valid"
+    with pytest.raises(DeviceWaitTimeout, match="timed out"):
+        iris.require_finite(v)
+    assert K.device_error(clear=False) == 0, "require_finite clears the word it reported"
+    v = engine(x, t, text)
+    assert rel_err(v, fx["v"]) < REL_TOL
+    iris.require_finite(v)
+    d = fx["euler_cfg"]
+    pipe = iris.DenoisePipeline(engine, cfg_scale=d["cfg_scale"], cfg_interval=d["cfg_interval"])
+    K.peer_barrier(flags, [0, peer.data_ptr()], 0, 2, timeout_s=0.02)
+    with pytest.raises(DeviceWaitTimeout):
+        pipe(d["noise"], d["cond"], d["uncond"], adapted=True)
+    assert K.device_error(clear=True) == 0
+
+
 def _ipc_child(handle, offset, numel, queue):
     import torch
 
