@@ -355,6 +355,98 @@ def fused_ops(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def attention_compare(args) -> None:
+    """The config-3 attention (B = 2, 24 heads x 128, 4352 joint tokens, QK-normed
+    rows as in the model) through this library's tcgen05 kernel (with and without
+    the QK-norm score bound) and through the library kernels the reference's
+    attention call site would reach on this box (src/iris3b/nn/attention.py:61-91:
+    F.scaled_dot_product_attention, and the flash_attn backend): torch SDPA with
+    the cuDNN and flash backends, flash_attn 2. Each launch after an L2 flush
+    (the operands, 160 MB, exceed L2 anyway), CUDA events on the stream, the mean
+    of ``max(steps, 20)`` launches after ``warmup``."""
+    import torch.nn.functional as F
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    from iris_b200 import kernels as K
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    B, H, N, D = 2, 24, 4352, 128
+    g = torch.Generator(device=device).manual_seed(3)
+    gains = [1 + 0.02 * torch.randn(D, generator=g, device=device) for _ in range(2)]
+    q, k = (F.rms_norm(torch.randn(B, H, N, D, generator=g, device=device), (D,), gn, 1e-6).to(torch.bfloat16)
+            for gn in gains)  # fmt: skip
+    v = torch.randn(B, H, N, D, generator=g, device=device).to(torch.bfloat16)
+    out = torch.empty(B * N, H * D, device=device, dtype=torch.bfloat16)
+    bound = K.score_bound([gains[0]], [gains[1]])
+    flush = torch.empty(256 * 2**20, dtype=torch.uint8, device=device)
+    flops = 4.0 * B * H * N * N * D
+    reps = max(args.steps, 20)
+
+    def timed(fn):
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        times = []
+        for _ in range(reps):
+            flush.fill_(1)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            times.append((s, e))
+        torch.cuda.synchronize()
+        ms = statistics.mean(a.elapsed_time(b) for a, b in times)
+        return {"us": ms * 1e3, "tflops": flops / (ms / 1e3) / 1e12}
+
+    ref = F.scaled_dot_product_attention(q.float(), k.float(), v.float()).transpose(1, 2).reshape(B * N, H * D)
+    results, errors = {}, {}
+
+    def check(name, o):
+        errors[name] = float((o.float() - ref).abs().max() / ref.abs().max())
+
+    K.flash_attention(q, k, v, out.view(B, N, H * D))
+    check("iris_tcgen05", out)
+    results["iris_tcgen05_score_bound"] = timed(lambda: K.flash_attention(q, k, v, out.view(B, N, H * D), bound=bound))
+    results["iris_tcgen05"] = timed(lambda: K.flash_attention(q, k, v, out.view(B, N, H * D)))
+    for name, backend in (("torch_sdpa_cudnn", SDPBackend.CUDNN_ATTENTION), ("torch_sdpa_flash", SDPBackend.FLASH_ATTENTION)):
+        try:
+            with sdpa_kernel(backend):
+                check(name, F.scaled_dot_product_attention(q, k, v).transpose(1, 2).reshape(B * N, H * D))
+                results[name] = timed(lambda: F.scaled_dot_product_attention(q, k, v))
+        except RuntimeError as exc:
+            results[name] = {"unavailable": str(exc).splitlines()[0][:200]}
+    try:
+        from flash_attn import flash_attn_func
+
+        qt, kt, vt = (t.transpose(1, 2).contiguous() for t in (q, k, v))
+        check("flash_attn2", flash_attn_func(qt, kt, vt).reshape(B * N, H * D))
+        results["flash_attn2"] = timed(lambda: flash_attn_func(qt, kt, vt))
+    except Exception as exc:  # noqa: BLE001 - report, do not fail the comparison
+        results["flash_attn2"] = {"unavailable": f"{type(exc).__name__}: {str(exc)[:200]}"}
+    pk = peaks()
+    best = max((r["tflops"] for n, r in results.items() if "tflops" in r and not n.startswith("iris")), default=None)
+    ours = results["iris_tcgen05_score_bound"]["tflops"]
+    line = {
+        "metric": "TFLOP/s of the config-3 joint attention (B=2, 24 heads x 128, N=4352) vs library kernels",
+        "value": ours,
+        "unit": "TFLOP/s",
+        "n_gpus": 1,
+        "steps": reps,
+        "warmup": max(args.warmup, 3),
+        "higher_is_better": True,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": "one attention launch, q/k RMS-normed rows (gains 1 + N(0, 0.02)), v ~ N(0, 1)",
+                   "l2": "flushed before every launch (256 MB write)"},  # fmt: skip
+        "results": results,
+        "max_rel_err_vs_fp32": errors,
+        "best_library_tflops": best,
+        "roofline": {"bound": "tensor", "achieved": ours, "peak": pk["bf16"], "unit": "TFLOP/s",
+                     "frac": ours / pk["bf16"], "traffic": None, "peak_source": f"{pk['source']} bf16 burst"},  # fmt: skip
+    }
+    print(json.dumps(line), flush=True)
+
+
 RES_2048 = 2048
 
 
@@ -528,7 +620,7 @@ def main() -> None:
     parser.add_argument("--impl", default="ours", choices=["ours", "reference"])
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--profile", choices=["forward", "small", "sampler"], help="NVTX-marked work for ncu")
-    parser.add_argument("--workload", default="loop1024", choices=["loop1024", "step2048", "ops"])
+    parser.add_argument("--workload", default="loop1024", choices=["loop1024", "step2048", "ops", "attention"])
     args = parser.parse_args()
     from iris_b200.parallel import env_world, gather_images, image_shard, init_process_group  # noqa: F401
 
@@ -546,6 +638,10 @@ def main() -> None:
     if args.workload == "ops":
         if rank == 0:
             fused_ops(args)
+        return
+    if args.workload == "attention":
+        if rank == 0:
+            attention_compare(args)
         return
     import torch.distributed as dist
 

@@ -43,6 +43,8 @@ extern "C" {
 #define IRIS_EPI_SWIGLU 1 /* out = silu(acc[w1 block]) * acc[w3 block] */
 #define IRIS_EPI_GATE 2   /* out = aux * sigmoid(acc)                  */
 #define IRIS_EPI_HEADS 3  /* [q | k | v] heads -> normed, rotated head layouts (see iris_heads_epilogue) */
+#define IRIS_EPI_ADD 4    /* out += acc (+ bias), f32 out updated in place (residual x + f(x)) */
+#define IRIS_EPI_SILU 5   /* out = silu(acc (+ bias))                  */
 
 /* Sequence parallelism over processes (peer memory) */
 #define IRIS_MAX_PEERS 8        /* ranks one call may span */
@@ -319,6 +321,30 @@ int iris_gemv(const float* x, int64_t M, int64_t K, const void* w, int w_dtype, 
  * out[j, b, :] = core[b, :] + bias[j, :] for j < n_blocks. */
 int iris_add_bias_rows(const float* core, const float* bias, float* out, int64_t batch, int64_t n_blocks,
                        int64_t width, void* stream);
+
+/* ---- text adapter (once per prompt) ------------------------------------- */
+/* Attention of the text adapters over short sequences
+ * (src/iris3b/nn/embeddings.py:79-142,144-207, SelfAttention
+ * src/iris3b/nn/attention.py:94-132 without RoPE): qkv holds seqs * n rows of
+ * row_stride bf16, columns [q | k | v] with heads * head_dim each (head h at
+ * h * head_dim); for every (sequence s, head h, query i):
+ * out[s * n + i, h * head_dim + d] = sum_j softmax_j(scale q_i . k_j) v_j[d]
+ * (bf16 out, row stride out_stride). q_gain / k_gain: both null, or per-head
+ * RMSNorm gains [head_dim] applied to q and k first (eps). key_mask: null, or
+ * uint8 [seqs, n] (1 = real token): key j is attended by query i if
+ * key_mask[s, j] != 0 or j == i (pad keys masked, the diagonal kept,
+ * embeddings.py:199-205). head_dim % 8 == 0, head_dim <= 128; the sequence's
+ * keys and values must fit in shared memory (about n * 4 * head_dim bytes,
+ * n <= 436 at head_dim 128). */
+int iris_small_attention(const void* qkv, int64_t seqs, int64_t n, int64_t heads, int64_t head_dim,
+                         int64_t row_stride, const float* q_gain, const float* k_gain, float eps,
+                         const uint8_t* key_mask, float scale, void* out, int64_t out_stride, void* stream);
+
+/* LayerwiseTextEmbedder's layer_pool, src/iris3b/nn/embeddings.py:262-264:
+ * out[r, c] = sum_l weight[l] x[r * layers + l, c] + bias[0] (x f32 [rows * layers,
+ * width], out bf16 [rows, width]; width % 4 == 0). */
+int iris_layer_pool(const float* x, int64_t rows, int64_t layers, int64_t width, const float* weight,
+                    const float* bias, void* out, void* stream);
 
 /* ---- sampler ------------------------------------------------------------ */
 /* One CFG + Euler flow step (src/iris3b/flow/solver.py:72-74 and

@@ -19,7 +19,8 @@
 //               fused epilogue math, direct vectorised global stores, then
 //               release the accumulator so the next tile's MMAs overlap.
 //
-// Epilogues: STORE (optional bias, fp32 or bf16 out), SWIGLU (each 256-wide
+// Epilogues: STORE (optional bias, fp32 or bf16 out), ADD (out += acc + bias,
+// fp32 residual updated in place), SILU (silu(acc + bias)), SWIGLU (each 256-wide
 // W tile holds 128 rows of w1 then the matching 128 rows of w3; writes
 // silu(a) * b as bf16, 128 columns per tile), GATE (out = aux * sigmoid(acc),
 // bf16), HEADS (two 128-wide [q | k | v] head slots per tile: q and k
@@ -59,7 +60,7 @@ constexpr int EPI_WARPS = 4;
 constexpr size_t SMEM_BYTES =
     1024 /*align slack*/ + STAGES * STAGE_BYTES + 256 /*barriers*/ + EPI_WARPS * EPI_STAGE_BYTES;
 
-enum Epilogue : int { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_GATE = 2, EPI_HEADS = 3 };
+enum Epilogue : int { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_GATE = 2, EPI_HEADS = 3, EPI_ADD = 4, EPI_SILU = 5 };
 
 // EPI_HEADS: the tile's 256 columns are two 128-wide head slots of a [q | k |
 // v] projection; q and k slots are RMS-normed and rotated, v copied, each to
@@ -325,12 +326,28 @@ IRIS_DEVICE void epilogue_row(const Problem& p, uint32_t t_base, int64_t m, int 
             v[e + 1] = f.y * sigmoidf_fast(__uint_as_float(r[e + 1]));
           }
         }
-      } else if (p.bias != nullptr) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) + __ldg(p.bias + col0 + j);
       } else {
+        if (p.bias != nullptr) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) + __ldg(p.bias + col0 + j);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        }
+        if (p.epilogue == EPI_SILU) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = v[j] * sigmoidf_fast(v[j]);
+        } else if (p.epilogue == EPI_ADD) {  // residual update in place (f32 out only)
+          const float4* o4 = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.out) + prow * p.ldc + col0);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 o = o4[j];
+            v[4 * j] += o.x;
+            v[4 * j + 1] += o.y;
+            v[4 * j + 2] += o.z;
+            v[4 * j + 3] += o.w;
+          }
+        }
       }
       store_row32(p, prow, col0, v);
     }
@@ -724,7 +741,7 @@ int check_problem(const iris_gemm_problem& q) {
   IRIS_REQUIRE(q.K % 8 == 0 && q.lda % 8 == 0 && q.ldw % 8 == 0 && q.lda >= q.K && q.ldw >= q.K,
                "iris_gemm_bf16: K and leading dimensions must be multiples of 8 (16-byte TMA rows)");
   IRIS_REQUIRE(q.N % 32 == 0, "iris_gemm_bf16: N must be a multiple of 32");
-  IRIS_REQUIRE(q.epilogue >= EPI_STORE && q.epilogue <= EPI_HEADS, "iris_gemm_bf16: unknown epilogue");
+  IRIS_REQUIRE(q.epilogue >= EPI_STORE && q.epilogue <= EPI_SILU, "iris_gemm_bf16: unknown epilogue");
   IRIS_REQUIRE(q.out_seg_rows > 0 && q.aux_seg_rows > 0, "iris_gemm_bf16: row maps need seg_rows > 0");
   IRIS_REQUIRE(aligned16(q.a) && aligned16(q.w), "iris_gemm_bf16: pointers must be 16-byte aligned");
   if (q.epilogue == EPI_HEADS) return check_heads(q);
@@ -737,6 +754,8 @@ int check_problem(const iris_gemm_problem& q) {
   } else {
     IRIS_REQUIRE(q.ldc >= q.N, "iris_gemm_bf16: ldc < N");
   }
+  if (q.epilogue == EPI_ADD)
+    IRIS_REQUIRE(q.out_dtype == 0, "iris_gemm_bf16: the add epilogue updates an f32 output in place");
   if (q.epilogue == EPI_GATE) {
     IRIS_REQUIRE(q.aux != nullptr && aligned16(q.aux) && q.ldaux % 8 == 0 && q.ldaux >= q.N && q.out_dtype == 1,
                  "iris_gemm_bf16: gate epilogue needs an aligned bf16 aux with ldaux % 8 == 0");

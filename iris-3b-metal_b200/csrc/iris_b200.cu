@@ -1,6 +1,7 @@
 // Single translation unit of libiris_b200.so: the device error word and the
 // kernels share one module, so no relocatable device code is needed.
 #include "abi.cu"
+#include "adapter.cu"
 #include "attention.cu"
 #include "gemm.cu"
 #include "heads.cu"

@@ -14,7 +14,7 @@ LIBRARY = Path(__file__).resolve().parent / "libiris_b200.so"
 
 IRIS_OK, IRIS_EINVAL, IRIS_ECUDA = 0, 1, 2
 F32, BF16, F16 = 0, 1, 2
-EPI_STORE, EPI_SWIGLU, EPI_GATE, EPI_HEADS = 0, 1, 2, 3
+EPI_STORE, EPI_SWIGLU, EPI_GATE, EPI_HEADS, EPI_ADD, EPI_SILU = 0, 1, 2, 3, 4, 5
 HEADS_LOCAL, HEADS_PEER_SCATTER, HEADS_PEER_BROADCAST_KV = 0, 1, 2
 MAX_PEERS = 8  # IRIS_MAX_PEERS
 IPC_HANDLE_BYTES = 64
@@ -48,6 +48,8 @@ SIGNATURES: dict[str, list] = {
     "iris_dpm_update": [P, P, P, P, P, I64, I64, F, I32, F, I32, F, F, F, P],
     "iris_all_finite": [P, I64, P, P],
     "iris_poison_on_error": [P, I64, ctypes.c_uint, P],
+    "iris_small_attention": [P, I64, I64, I64, I64, I64, P, P, F, P, F, P, I64, P],
+    "iris_layer_pool": [P, I64, I64, I64, P, P, P, P],
 }
 
 class HeadsEpilogue(ctypes.Structure):

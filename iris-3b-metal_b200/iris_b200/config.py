@@ -51,6 +51,9 @@ class ModelConfig:
     text_dim: int = 2560
     text_len: int = 300
     text_adapter: str = "lap_blocks2"
+    text_lap_num_layers: int = 12
+    text_lap_num_heads: int = 32
+    text_lap_mlp_ratio: float = 1.3
     pixel: PixelStageConfig = field(default_factory=PixelStageConfig)
 
     @property

@@ -41,6 +41,7 @@ import torch
 
 from iris_b200 import _lib
 from iris_b200 import kernels as K
+from iris_b200.adapter import TextAdapter
 from iris_b200.config import ModelConfig, from_any
 from iris_b200.tables import cos_sin, rope_1d, rope_2d, sincos_pos_embed_2d
 from iris_b200.ulysses import PeerBuffers, SequenceShard, gather_image_tokens, gather_tokens, scatter_heads
@@ -313,60 +314,46 @@ class CudaIris:
         if tuple(self.final[1].shape) != (3, pix.hidden_size):
             raise ValueError("CudaIris: the final layer must emit 3 channels per pixel")
         self.text_adapter = None
+        self.masked_adapter = None
+        self.y_pos = f32("y_pos_embedding").reshape(-1, d) if "y_pos_embedding" in state else None
         if cfg.text_adapter == "linear" and "y_embedder.proj.weight" in state:
-            self.text_adapter = (
-                pad_k(bf("y_embedder.proj.weight")),
-                f32("y_embedder.proj.bias"),
-                f32("y_embedder.norm.weight"),
-                f32("y_pos_embedding").reshape(-1, d) if "y_pos_embedding" in state else None,
-            )
+            self.text_adapter = (pad_k(bf("y_embedder.proj.weight")), f32("y_embedder.proj.bias"),
+                                 f32("y_embedder.norm.weight"))  # fmt: skip
+        elif cfg.text_adapter in ("lap_blocks2", "blocks2") and any(k.startswith("y_embedder.") for k in state):
+            self.masked_adapter = TextAdapter(cfg, state, dev)
 
     # -- conditioning ---------------------------------------------------------------
     @torch.no_grad()
     def encode_text(self, states: torch.Tensor, mask: torch.Tensor | None = None) -> torch.Tensor:
-        """Encoder states -> trunk text tokens ``[B, T, D]`` (FP32), once per prompt.
+        """Encoder states -> trunk text tokens ``[B, T, D]`` (FP32), once per prompt
+        (``MetalIris.encode_text``, ``src/iris_metal/model.py:133-145``).
 
-        The linear adapter (``TextEmbedder``: Linear + RMSNorm, then
-        ``y_pos_embedding``, ``dit.py:263-281``) runs on this engine's kernels.
-        Any other adapter (the masked ``lap_blocks2`` transformer over
-        ``[B, T, layers, dim]`` states) runs through the upstream module the
-        engine was built from, under autocast to its linear weights' dtype, as
-        ``MetalIris.encode_text`` does (``src/iris_metal/model.py:133-145``); it
-        then needs ``mask``."""
-        if self.text_adapter is None:
-            return self._encode_text_upstream(states, mask)
-        w, b, norm_w, pos = self.text_adapter
+        Both adapter families run on this engine's kernels: the linear one
+        (``TextEmbedder``: Linear + RMSNorm, then ``y_pos_embedding``,
+        ``dit.py:263-281``) and the masked transformers ``lap_blocks2`` /
+        ``blocks2`` over ``[B, T, layers, dim]`` / ``[B, T, dim]`` states
+        (:class:`iris_b200.adapter.TextAdapter`), which need the encoder's
+        ``[B, T]`` mask (nonzero = real token)."""
         cfg = self.cfg
-        states = states[:, : cfg.text_len].to(self.device)
+        n = cfg.text_len
+        if self.masked_adapter is not None:
+            if mask is None:
+                raise ValueError(f"encode_text: the {cfg.text_adapter!r} text adapter needs the encoder's [B, T] mask")
+            return self.masked_adapter(states[:, :n].to(self.device, torch.float32), mask[:, :n], pos=self.y_pos)
+        if self.text_adapter is None:
+            raise ValueError(f"encode_text: the model has no weights for its {cfg.text_adapter!r} text adapter")
+        w, b, norm_w = self.text_adapter
+        states = states[:, :n].to(self.device)
         batch, n, dim = states.shape
         a = torch.zeros(batch * n, w.shape[1], device=self.device, dtype=torch.bfloat16)
         a[:, :dim] = states.reshape(batch * n, dim)
         out = torch.empty(batch, n, cfg.hidden_size, device=self.device, dtype=torch.float32)
         K.gemm(a, w, out.view(batch * n, -1), bias=b)
+        pos = self.y_pos
         add = pos[:n].contiguous() if pos is not None else torch.zeros(n, cfg.hidden_size, device=self.device)
         _lib.call("iris_rms_norm_add_rows", out.data_ptr(), norm_w.data_ptr(), add.data_ptr(), batch * n, n,
                   cfg.hidden_size, float(cfg.norm_eps), K.stream_of(out))  # fmt: skip
         return out
-
-    @torch.no_grad()
-    def _encode_text_upstream(self, states: torch.Tensor, mask: torch.Tensor | None) -> torch.Tensor:
-        y_embedder = getattr(self.dit, "y_embedder", None)
-        if y_embedder is None:
-            raise NotImplementedError(
-                f"CudaIris.encode_text: the {self.cfg.text_adapter!r} text adapter runs through the upstream "
-                "module (build the engine from the upstream IrisDiT); the linear adapter runs on the engine"
-            )
-        if mask is None:
-            raise ValueError(f"encode_text: the {self.cfg.text_adapter!r} text adapter needs the encoder's [B, T] mask")
-        n = self.cfg.text_len
-        # autocast to the adapter's linear storage dtype, none for FP32 (src/iris_metal/model.py:128,141-144)
-        modules = y_embedder.modules() if isinstance(y_embedder, torch.nn.Module) else ()
-        dtype = next((m.weight.dtype for m in modules if isinstance(m, torch.nn.Linear)), torch.bfloat16)
-        with torch.autocast("cuda", dtype=dtype, enabled=dtype != torch.float32):
-            tokens = y_embedder(states[:, :n].to(self.device, torch.float32), mask[:, :n].to(self.device))
-        tokens = tokens.float()
-        pos = getattr(self.dit, "y_pos_embedding", None)
-        return tokens + pos[:, : tokens.shape[1]].float() if pos is not None else tokens
 
     def _rope(self, grid: tuple[int, int], n_text: int):
         key = (grid, n_text)

@@ -51,6 +51,9 @@ class OracleConfig:
     text_dim: int = 2560
     text_len: int = 300
     text_adapter: str = "linear"
+    text_lap_num_layers: int = 12
+    text_lap_num_heads: int = 32
+    text_lap_mlp_ratio: float = 1.3
     pixel: PixelConfig = field(default_factory=PixelConfig)
 
     @property

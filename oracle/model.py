@@ -36,12 +36,22 @@ class OracleModel:
         h = F.silu(self._lin(emb, "t_embedder.mlp.0"))
         return self._lin(h, "t_embedder.mlp.2").reshape(t.shape[0], -1, self.cfg.hidden_size)
 
-    def embed_text(self, y: torch.Tensor) -> torch.Tensor:
-        """``IrisDiT.embed_text`` with the linear adapter, ``dit.py:263-281`` and
-        ``TextEmbedder.forward``, ``src/iris3b/nn/embeddings.py:75-76``."""
+    def embed_text(self, y: torch.Tensor, mask: torch.Tensor | None = None) -> torch.Tensor:
+        """``IrisDiT.embed_text``, ``dit.py:263-281``: the linear adapter
+        (``TextEmbedder.forward``, ``src/iris3b/nn/embeddings.py:75-76``) or a
+        masked one (``oracle.adapter``), which needs the encoder's ``[B, T]`` mask."""
         cfg = self.cfg
         y = y[:, : cfg.text_len]
-        y = self._norm(self._lin(y, "y_embedder.proj"), "y_embedder.norm")
+        if cfg.text_adapter == "linear":
+            y = self._norm(self._lin(y, "y_embedder.proj"), "y_embedder.norm")
+        else:
+            from oracle.adapter import AdapterOracle
+
+            if mask is None:
+                raise ValueError(f"the {cfg.text_adapter} text adapter needs the encoder's [B, T] mask")
+            prefix = "y_embedder."
+            params = {k[len(prefix) :]: v for k, v in self.p.items() if k.startswith(prefix)}
+            y = AdapterOracle(cfg, params)(y, mask[:, : cfg.text_len])
         if cfg.text_abs_pos_embed:
             y = y + self.p["y_pos_embedding"][:, : y.shape[1]].to(y.dtype)
         return y

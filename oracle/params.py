@@ -45,10 +45,13 @@ def param_spec(cfg: OracleConfig) -> list[tuple[str, tuple, str]]:
     spec += _linear("s_embedder.proj", d, p * p * c, True)
     spec += _linear("t_embedder.mlp.0", d, 256, True)
     spec += _linear("t_embedder.mlp.2", d, d, True)
-    if cfg.text_adapter != "linear":
-        raise NotImplementedError("the oracle restates the linear text adapter only")
-    spec += _linear("y_embedder.proj", d, cfg.text_dim, True)
-    spec += _norm("y_embedder.norm", d)
+    if cfg.text_adapter == "linear":
+        spec += _linear("y_embedder.proj", d, cfg.text_dim, True)
+        spec += _norm("y_embedder.norm", d)
+    else:  # the masked adapters (lap_blocks2, blocks2)
+        from oracle.adapter import adapter_param_spec
+
+        spec += [(f"y_embedder.{n}", s, k) for n, s, k in adapter_param_spec(cfg)]
     if cfg.modulation == "shared_bias":
         spec += _linear("modulation_cores.adaln_img", 6 * d, d, True)
         spec += _linear("modulation_cores.adaln_txt", 6 * d, d, True)

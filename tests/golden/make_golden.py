@@ -242,6 +242,42 @@ def _depth_fixture(cfg, fixture, ModelConfig, PixelStageConfig):
             "time": float(model.num_train_timesteps)}
 
 
+def _adapter_fixtures(ModelConfig, PixelStageConfig, IrisDiT):
+    """The masked text adapters through the reference's own ``IrisDiT.embed_text``
+    (``src/iris3b/models/dit.py:263-281``): ``lap_blocks2`` (``LayerwiseTextEmbedder``,
+    ``src/iris3b/nn/embeddings.py:209-266``) and ``blocks2``
+    (``TransformerTextEmbedder``, ``:144-207``) on the toy topology with text
+    states of width 640 (8 layer-attention heads of 80, as 2560 / 32 in the
+    release) and 3 encoder layers; seeded init recipe over the whole model. The
+    masks cover a right-padded prompt, real tokens at scattered positions and a
+    prompt of padding only (identity attention on the diagonal); the states run
+    4 tokens past ``text_len`` (truncated by embed_text)."""
+    out = {}
+    mask = torch.zeros(3, 20, dtype=torch.bool)
+    mask[0, :13] = True
+    mask[1, ::3] = True
+    mask[1, 7] = True
+    for adapter in ("lap_blocks2", "blocks2"):
+        cfg = ocfg.released_topology(num_kv_heads=None, text_adapter=adapter, text_dim=640, text_lap_num_layers=3,
+                                     text_lap_num_heads=8)  # fmt: skip
+        model = IrisDiT(_reference_config(cfg, ModelConfig, PixelStageConfig)).eval()
+        ref_spec = [(n, tuple(p.shape)) for n, p in model.named_parameters()]
+        assert ref_spec == [(n, tuple(s)) for n, s, _ in param_spec(cfg)], f"{adapter}: inventory differs"
+        _seed_reference(model, seed=0)
+        gen = torch.Generator().manual_seed(12)
+        shape = (3, 20, 3, 640) if adapter == "lap_blocks2" else (3, 20, 640)
+        y = torch.randn(shape, generator=gen)
+        with torch.no_grad():
+            text = model.embed_text(y, mask)
+            bare = model.y_embedder(y[:, : cfg.text_len], mask[:, : cfg.text_len])
+        checksums = {n: (float(p.detach().double().sum()), float(p.detach().double().pow(2).sum()))
+                     for n, p in model.named_parameters() if n.startswith("y_embedder.")}  # fmt: skip
+        out[adapter] = {"config": dataclasses.asdict(cfg), "y": y, "mask": mask, "prepared_text": text,
+                        "adapter_out": bare, "param_checksums": checksums}  # fmt: skip
+        print(adapter, "adapter", tuple(text.shape), float(text.abs().max()))
+    return out
+
+
 def _op_fixtures():
     from iris3b.nn.embeddings import TimestepEmbedder, sincos_pos_embed_2d
     from iris3b.nn.rope import apply_rope, rope_1d, rope_2d
@@ -335,9 +371,16 @@ def _sampler_fixtures():
 def main():
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", required=True, type=Path)
+    parser.add_argument("--only", choices=["adapters"], help="regenerate one fixture file only")
     args = parser.parse_args()
     torch.set_num_threads(8)
     ModelConfig, PixelStageConfig, IrisDiT = _import_reference(args.reference)
+    if args.only != "adapters":
+        _model_fixtures(ModelConfig, PixelStageConfig, IrisDiT)
+    torch.save(_adapter_fixtures(ModelConfig, PixelStageConfig, IrisDiT), HERE / "adapters.pt")
+
+
+def _model_fixtures(ModelConfig, PixelStageConfig, IrisDiT):
     fixtures = {
         "released_mha": (ocfg.released_topology(num_kv_heads=None), 2, 24, 24, [125.0, 850.0]),
         "released_gqa": (ocfg.released_topology(), 2, 24, 16, [125.0, 850.0]),
@@ -356,8 +399,9 @@ def main():
     torch.save(_sampler_fixtures(), HERE / "samplers.pt")
     # the full-size inventories, built on the meta device (no memory)
     inventories = {}
-    for name, cfg in (("baseline_step", ocfg.baseline_step_config()), ("released_preset", ocfg.OracleConfig(
-            text_adapter="linear"))):
+    for name, cfg in (("baseline_step", ocfg.baseline_step_config()),
+                      ("released_preset", ocfg.OracleConfig(text_adapter="linear")),
+                      ("released_preset_lap", ocfg.OracleConfig(text_adapter="lap_blocks2"))):
         with torch.device("meta"):
             model = IrisDiT(_reference_config(cfg, ModelConfig, PixelStageConfig))
         spec = [(n, tuple(p.shape)) for n, p in model.named_parameters()]

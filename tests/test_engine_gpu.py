@@ -90,54 +90,6 @@ def test_encode_text_matches_reference(iris):
     assert rel_err(text, fx["prepared_text"]) < REL_TOL
 
 
-@pytest.mark.parametrize("adapter_dtype", [torch.bfloat16, torch.float32])
-def test_encode_text_masked_adapter_runs_the_upstream_module(iris, adapter_dtype):
-    """A model whose text adapter is not the linear one (the masked lap_blocks2
-    transformer over [B, T, layers, dim] states): encode_text runs the module the
-    engine was built from, under autocast to its linear weights' dtype (none for
-    FP32), and adds y_pos_embedding, as MetalIris.encode_text does
-    (src/iris_metal/model.py:133-145). Without the mask, or without an upstream
-    module, it raises."""
-    import dataclasses
-
-    fx = golden("released_mha")
-    cfg = dataclasses.replace(_config(fx["config"]), text_adapter="lap_blocks2")
-    state = {k: v.cuda() for k, v in seeded_init(_config(fx["config"]), seed=0).items()}
-    gen = torch.Generator(device="cuda").manual_seed(9)
-    layers = 3
-
-    class Adapter(torch.nn.Module):  # stands in for the masked adapter: [B, T, layers, dim] + [B, T] mask
-        def __init__(self):
-            super().__init__()
-            self.proj = torch.nn.Linear(layers * cfg.text_dim, cfg.hidden_size).to("cuda", adapter_dtype)
-
-        def forward(self, y, mask):
-            return self.proj(y.flatten(2)) * mask[..., None]
-
-    adapter = Adapter()
-
-    class Upstream:  # the attributes of an upstream IrisDiT that the engine reads
-        def __init__(self):
-            self.cfg, self.y_embedder, self.y_pos_embedding = cfg, adapter, state["y_pos_embedding"]
-
-        def state_dict(self):
-            return state
-
-    engine = iris.CudaIris(Upstream())
-    states = torch.randn(2, cfg.text_len + 4, layers, cfg.text_dim, device="cuda", generator=gen)
-    mask = torch.ones(2, cfg.text_len + 4, device="cuda", dtype=torch.bool)
-    mask[0, 5:] = False
-    got = engine.encode_text(states, mask)
-    low = adapter_dtype != torch.float32
-    with torch.no_grad(), torch.autocast("cuda", dtype=adapter_dtype, enabled=low):
-        want = adapter(states[:, : cfg.text_len], mask[:, : cfg.text_len])
-    assert torch.equal(got, want.float() + state["y_pos_embedding"][:, : cfg.text_len].float())
-    with pytest.raises(ValueError, match="mask"):
-        engine.encode_text(states)
-    with pytest.raises(NotImplementedError):
-        iris.CudaIris(iris.IrisWeights(cfg, state)).encode_text(states, mask)
-
-
 def test_euler_cfg_sample_matches_reference(iris):
     fx = golden("released_mha")
     cfg = _config(fx["config"])

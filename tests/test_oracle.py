@@ -170,9 +170,31 @@ def test_oracle_tables_are_bit_exact():
 
 def test_oracle_inventories_match_full_size_reference():
     fx = golden("inventories")
-    for name, cfg in (("baseline_step", baseline_step_config()), ("released_preset", OracleConfig())):
+    for name, cfg in (("baseline_step", baseline_step_config()), ("released_preset", OracleConfig()),
+                      ("released_preset_lap", OracleConfig(text_adapter="lap_blocks2"))):  # fmt: skip
         assert [n for n, _, _ in param_spec(cfg)] == fx[name]["names"]
         assert num_parameters(cfg) == fx[name]["numel"]
+    # the released preset's parameter count, tests/test_model.py:13-25 of the reference
+    assert fx["released_preset_lap"]["numel"] == 2_987_511_888
+
+
+@pytest.mark.parametrize("adapter", ["lap_blocks2", "blocks2"])
+def test_oracle_masked_adapter_matches_reference(adapter):
+    """The masked text adapters restated (oracle.adapter) against the reference's
+    embed_text on a right-padded prompt, scattered real tokens and an all-pad
+    prompt; the seeded weights reproduce the reference's parameter checksums."""
+    fx = golden("adapters")[adapter]
+    cfg = _config(fx["config"])
+    params = seeded_init(cfg, seed=0)
+    for name, (total, squares) in fx["param_checksums"].items():
+        p = params[name].double()
+        assert abs(float(p.sum()) - total) < 1e-6 * max(1.0, abs(total)) and abs(float(p.pow(2).sum()) - squares) < 1e-6
+    model = OracleModel(cfg, params)
+    with torch.no_grad():
+        text = model.embed_text(fx["y"], fx["mask"])
+    torch.testing.assert_close(text, fx["prepared_text"], rtol=1e-4, atol=1e-5)
+    with pytest.raises(ValueError, match="mask"):
+        model.embed_text(fx["y"])
 
 
 def test_index_maps_round_trip():
