@@ -11,8 +11,6 @@ src/iris3b/nn/embeddings.py:79-266) and the kernels they add.
   tokens, hidden 3072) against the fp32 oracle on the same GPU.
 """
 
-import dataclasses
-
 import pytest
 import torch
 import torch.nn.functional as F
@@ -168,7 +166,7 @@ def test_released_adapter_dimensions_match_fp32_oracle(iris):
     heads and SwiGLU 8192; seeded weights, random padding; the fp32 oracle runs on
     the same GPU."""
     from iris_b200.adapter import TextAdapter
-    from iris_b200.config import ModelConfig
+    from iris_b200.config import from_any
 
     cfg = OracleConfig(hidden_size=3072, num_heads=24, num_kv_heads=None, text_adapter="lap_blocks2")
     gen = torch.Generator(device="cuda").manual_seed(0)
@@ -180,9 +178,7 @@ def test_released_adapter_dimensions_match_fp32_oracle(iris):
     mask = torch.zeros(2, 300, dtype=torch.bool, device="cuda")
     mask[0, :300] = True
     mask[1, :117] = True
-    adapter = TextAdapter(ModelConfig(**{f.name: getattr(cfg, f.name) for f in dataclasses.fields(ModelConfig)
-                                         if f.name != "pixel"}), {f"y_embedder.{k}": v for k, v in params.items()},
-                          torch.device("cuda"))  # fmt: skip
+    adapter = TextAdapter(from_any(cfg), {f"y_embedder.{k}": v for k, v in params.items()}, torch.device("cuda"))
     got = adapter(states, mask)
     with torch.no_grad():
         want = AdapterOracle(cfg, params)(states, mask)
