@@ -542,6 +542,39 @@ def measure_2048(engine, single, rank: int, world: int, local: int, steps: int, 
     return record
 
 
+def measure_restore(engine, rank: int, world: int, local: int, steps: int, warmup: int) -> dict:
+    """The restoration / 4x upscaling task at the reference's largest budgeted
+    image (a 512 x 1024 input, 2048 x 4096 output: 21 overlapping 1024^2 tiles,
+    src/iris3b/downstream/restoration.py:18-21,104-107), tiles split over the
+    ranks, Gaussian-window fusion, one sum all-reduce of the image at the end.
+    Synthetic input and prompt (random weights, random adapted text)."""
+    import torch.distributed as dist
+
+    from iris_b200.restoration import TiledRestorer, tile_plan
+
+    device = torch.device("cuda", local)
+    gen = torch.Generator().manual_seed(9)
+    x = (torch.rand(1, 3, 2048, 4096, generator=gen) * 2 - 1).to(device)
+    states = torch.randn(1, TEXT_LEN, TEXT_DIM, generator=torch.Generator().manual_seed(10)).to(device)
+    group = dist.group.WORLD if world > 1 else None
+    restorer = TiledRestorer(engine, engine.encode_text(states), sigma=0.5, tile=1024, tiles_per_call=8, group=group)
+    tiles, mine = tile_plan(2048, 4096, 1024, rank, world)
+    with ClockSampler(local) as clocks:
+        ms = time_calls(lambda: restorer(x), steps, warmup, world, local, device)
+    return {
+        "image": "2048x4096 output (4x of a 512x1024 input)",
+        "tiles": len(tiles),
+        "tiles_on_busiest_rank": -(-len(tiles) // world),
+        "ms_per_image": ms,
+        "tiles_per_s": len(tiles) / (ms / 1e3),
+        "n_gpus": world,
+        "parallelism": f"tiles split over {world} GPU(s)",
+        "steps": steps,
+        "warmup": warmup,
+        "clocks": clocks.summary(),
+    }
+
+
 def step2048(args, rank: int, world: int, local: int) -> None:
     """BASELINE config 5 as the whole bench line (``--workload step2048``)."""
     import torch.distributed as dist
@@ -745,6 +778,9 @@ def main() -> None:
         sp_engine.close()
         del sp_engine
 
+    # -------------------------------------- tiled 4x restoration (21 tiles) on the same N GPUs
+    restore_rec = measure_restore(engine, rank, world, local, 2, 1)
+
     pk = peaks()
     achieved = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms else None
     cpu = None
@@ -797,6 +833,7 @@ def main() -> None:
         "clocks": clocks.summary(),
         "denoise_step_b2": b2,
         "step2048": step2048_rec,
+        "restore_4x": restore_rec,
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu

@@ -346,6 +346,27 @@ int iris_small_attention(const void* qkv, int64_t seqs, int64_t n, int64_t heads
 int iris_layer_pool(const float* x, int64_t rows, int64_t layers, int64_t width, const float* weight,
                     const float* bias, void* out, void* stream);
 
+/* ---- tiled restoration (the restoration / 4x upscaling task) -------------- */
+/* One tile x tile crop of the [channels, height, width] fp32 image x at (top,
+ * left) into out [channels, tile, tile] (the crops that tiled() hands to
+ * restore_tile, src/iris3b/downstream/restoration.py:87-101). */
+int iris_tile_crop(const float* x, int64_t channels, int64_t height, int64_t width, int64_t top, int64_t left,
+                   int64_t tile, float* out, void* stream);
+
+/* The restored tile fused into the image (restore_tile's x - sigma v,
+ * src/iris_metal/tasks.py:143-150, weighted by gaussian_window,
+ * restoration.py:75-84,96-100): for (i, j) < (tile, tile) and every channel c,
+ * out[c, top + i, left + j] += (x[c, top + i, left + j] - sigma v[c, i, j]) * window[i, j];
+ * weight[top + i, left + j] += window[i, j] when weight is not null. v may be
+ * null (x and out unused): only the weights are accumulated. */
+int iris_tile_accumulate(const float* x, int64_t channels, int64_t height, int64_t width, const float* v,
+                         int64_t tile, const float* window, int64_t top, int64_t left, float sigma, float* out,
+                         float* weight, void* stream);
+
+/* out[c, y, x] /= weight[y, x]: the fused tiles' weighted average (restoration.py:101). */
+int iris_tile_normalize(float* out, const float* weight, int64_t channels, int64_t height, int64_t width,
+                        void* stream);
+
 /* ---- sampler ------------------------------------------------------------ */
 /* One CFG + Euler flow step (src/iris3b/flow/solver.py:72-74 and
  * src/iris3b/sampling.py:129-135): with guided != 0, v holds [uncond; cond]

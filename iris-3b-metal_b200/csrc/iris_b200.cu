@@ -9,3 +9,4 @@
 #include "pixel.cu"
 #include "rows.cu"
 #include "small.cu"
+#include "tiles.cu"

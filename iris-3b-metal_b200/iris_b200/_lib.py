@@ -50,6 +50,9 @@ SIGNATURES: dict[str, list] = {
     "iris_poison_on_error": [P, I64, ctypes.c_uint, P],
     "iris_small_attention": [P, I64, I64, I64, I64, I64, P, P, F, P, F, P, I64, P],
     "iris_layer_pool": [P, I64, I64, I64, P, P, P, P],
+    "iris_tile_crop": [P, I64, I64, I64, I64, I64, I64, P, P],
+    "iris_tile_accumulate": [P, I64, I64, I64, P, I64, P, I64, I64, F, P, P, P],
+    "iris_tile_normalize": [P, P, I64, I64, I64, P],
 }
 
 class HeadsEpilogue(ctypes.Structure):

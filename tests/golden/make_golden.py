@@ -242,6 +242,42 @@ def _depth_fixture(cfg, fixture, ModelConfig, PixelStageConfig):
             "time": float(model.num_train_timesteps)}
 
 
+def _restoration_fixture(model, fixture):
+    """The restorer's tiling (``tiled`` / ``gaussian_window`` / ``tile_positions``,
+    ``src/iris3b/downstream/restoration.py:68-101``) with ``restore_tile``'s
+    ``x - sigma v`` at model time 500 (``src/iris_metal/tasks.py:143-150``) on the
+    toy model and adapted text standing in for the export's empty prompt: a
+    48 x 64 image in 32-pixel tiles (stride 16, six tiles, as the reference's
+    tests/test_metal_tasks.py uses tile 32), and a 32 x 32 image (one tile, no
+    window). Also the tile positions and windows at the release's tile of 1024,
+    and ``MetalRestorer.tile_count`` for several input sizes."""
+    from iris3b.downstream.restoration import gaussian_window, tile_positions, tiled
+    from iris_metal.tasks import MetalRestorer
+
+    text = fixture["prepared_text"][1:]
+    sigma, tile = 0.5, 32
+
+    def restore(crop):
+        b = crop.shape[0]
+        t = torch.full((b,), sigma * 1000.0)
+        y = text.expand(b, -1, -1)
+        return crop - sigma * model(crop, t, y, prepared_text=y, precompute_modulation=True).x
+
+    gen = torch.Generator().manual_seed(21)
+    x = torch.rand(1, 3, 48, 64, generator=gen) * 2 - 1
+    with torch.no_grad():
+        fused = tiled(restore, x, tile, tile // 2)
+        single = tiled(restore, x[..., :tile, :tile], tile, tile // 2)
+    positions = {size: tile_positions(size, 1024, 512) for size in (1024, 1040, 1536, 2048, 2064, 4096)}
+    counter = SimpleNamespace(tile=1024, patch=16)
+    sizes = ((256, 256), (512, 512), (512, 1024), (1024, 512), (300, 200), (257, 1023), (64, 256))
+    return {"x": x, "text": text, "sigma": sigma, "tile": tile, "fused": fused, "single": single,
+            "window_32": gaussian_window(tile, torch.device("cpu"))[0, 0],
+            "window_1024_every_37": gaussian_window(1024, torch.device("cpu"))[0, 0, ::37, ::37].clone(),
+            "positions_1024": positions,
+            "tile_counts": {size: MetalRestorer.tile_count(counter, size) for size in sizes}}  # fmt: skip
+
+
 def _adapter_fixtures(ModelConfig, PixelStageConfig, IrisDiT):
     """The masked text adapters through the reference's own ``IrisDiT.embed_text``
     (``src/iris3b/models/dit.py:263-281``): ``lap_blocks2`` (``LayerwiseTextEmbedder``,
@@ -393,6 +429,7 @@ def _model_fixtures(ModelConfig, PixelStageConfig, IrisDiT):
             fixture["turbo"] = _turbo_fixture(model, fixture)
             fixture["dpm"] = _dpm_fixture(model, fixture)
             fixture["depth"] = _depth_fixture(cfg, fixture, ModelConfig, PixelStageConfig)
+            torch.save(_restoration_fixture(model, fixture), HERE / "restoration.pt")
         torch.save(fixture, HERE / f"{name}.pt")
         print(name, "saved", tuple(fixture["v"].shape), float(fixture["v"].abs().max()))
     torch.save(_op_fixtures(), HERE / "ops.pt")
