@@ -79,53 +79,96 @@ __global__ void timestep_kernel(const float* __restrict__ t, float* __restrict__
 
 IRIS_DEVICE float silu(float v) { return v / (1.f + __expf(-v)); }
 
-// One warp per output column n, up to MT rows of x per pass: the weight row is
-// streamed once per pass with 16-byte loads.
-template <typename TW, int MT>
+// Small-M linear, HBM-bound on the weights: every weight element is read once
+// for all (up to 16) rows of x. A block of 8 warps owns 8 * COLS output
+// columns; K is walked in chunks of 256, each chunk of act_in(x) staged once in
+// shared memory for the whole block; lane l multiplies elements [8 l, 8 l + 8)
+// of the chunk, with the next chunk's weights loaded while this one computes.
+constexpr int GEMV_MT = 16;
+constexpr int GEMV_CHUNK = 256;
+
+template <typename TW>
+IRIS_DEVICE void gemv_load8(const TW* p, bool ok, float (&v)[8]) {
+  if (!ok) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = 0.f;
+    return;
+  }
+  if constexpr (sizeof(TW) == 2) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+    const uint32_t ws[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const float2 f = unpack_bf16x2(ws[h]);
+      v[2 * h] = f.x;
+      v[2 * h + 1] = f.y;
+    }
+  } else {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p)), b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+}
+
+template <typename TW, int COLS>
 __global__ void __launch_bounds__(THREADS) gemv_kernel(const float* __restrict__ x, int M, int K,
                                                        const TW* __restrict__ w, const float* __restrict__ bias,
                                                        float* __restrict__ out, int N, int act_in, int act_out) {
-  const int lane = threadIdx.x & 31;
-  const int64_t n = static_cast<int64_t>(blockIdx.x) * (THREADS / 32) + (threadIdx.x >> 5);
-  if (n >= N) return;
-  const TW* wr = w + n * K;
-  for (int m0 = 0; m0 < M; m0 += MT) {
-    float acc[MT];
+  __shared__ __align__(16) float xs[GEMV_MT][GEMV_CHUNK];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t n0 = (static_cast<int64_t>(blockIdx.x) * (THREADS / 32) + warp) * COLS;
+  const int chunks = (K + GEMV_CHUNK - 1) / GEMV_CHUNK;
+  for (int m0 = 0; m0 < M; m0 += GEMV_MT) {
+    const int mt = min(GEMV_MT, M - m0);
+    float acc[COLS][GEMV_MT];
 #pragma unroll
-    for (int j = 0; j < MT; ++j) acc[j] = 0.f;
-    for (int k = lane * 8; k < K; k += 32 * 8) {
-      float wv[8];
-      if constexpr (sizeof(TW) == 2) {
-        const uint4 u = *reinterpret_cast<const uint4*>(wr + k);
-        const uint32_t ws[4] = {u.x, u.y, u.z, u.w};
+    for (int c = 0; c < COLS; ++c)
 #pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          const float2 f = unpack_bf16x2(ws[h]);
-          wv[2 * h] = f.x;
-          wv[2 * h + 1] = f.y;
-        }
-      } else {
-        const float4 a = *reinterpret_cast<const float4*>(wr + k), b = *reinterpret_cast<const float4*>(wr + k + 4);
-        wv[0] = a.x; wv[1] = a.y; wv[2] = a.z; wv[3] = a.w; wv[4] = b.x; wv[5] = b.y; wv[6] = b.z; wv[7] = b.w;
+      for (int j = 0; j < GEMV_MT; ++j) acc[c][j] = 0.f;
+    float wa[COLS][8], wb[COLS][8];
+    auto load_w = [&](int chunk, float (&dst)[COLS][8]) {
+      const int k = chunk * GEMV_CHUNK + lane * 8;
+#pragma unroll
+      for (int c = 0; c < COLS; ++c) gemv_load8(w + (n0 + c) * K + k, n0 + c < N && k < K, dst[c]);
+    };
+    // one chunk: stage act_in(x), start the next chunk's weight loads, multiply
+    auto step = [&](int ch, const float (&cur)[COLS][8], float (&next)[COLS][8]) {
+      __syncthreads();  // the previous chunk's readers are done with xs
+      for (int e = threadIdx.x; e < mt * GEMV_CHUNK; e += THREADS) {
+        const int j = e / GEMV_CHUNK, kk = e % GEMV_CHUNK, k = ch * GEMV_CHUNK + kk;
+        const float v = k < K ? x[static_cast<int64_t>(m0 + j) * K + k] : 0.f;
+        xs[j][kk] = act_in ? silu(v) : v;
       }
+      __syncthreads();
+      if (ch + 1 < chunks) load_w(ch + 1, next);
 #pragma unroll
-      for (int j = 0; j < MT; ++j) {
-        if (m0 + j < M) {
-          const float* xr = x + static_cast<int64_t>(m0 + j) * K + k;
-          const float4 a = __ldg(reinterpret_cast<const float4*>(xr));
-          const float4 b = __ldg(reinterpret_cast<const float4*>(xr + 4));
-          float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+      for (int j = 0; j < GEMV_MT; ++j) {
+        if (j < mt) {
+          const float4 a = *reinterpret_cast<const float4*>(&xs[j][lane * 8]);
+          const float4 b = *reinterpret_cast<const float4*>(&xs[j][lane * 8 + 4]);
+          const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
-          for (int e = 0; e < 8; ++e) acc[j] = fmaf(act_in ? silu(xv[e]) : xv[e], wv[e], acc[j]);
+          for (int c = 0; c < COLS; ++c)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[c][j] = fmaf(xv[e], cur[c][e], acc[c][j]);
         }
       }
+    };
+    load_w(0, wa);
+    for (int ch = 0; ch < chunks; ch += 2) {
+      step(ch, wa, wb);
+      if (ch + 1 < chunks) step(ch + 1, wb, wa);
     }
 #pragma unroll
-    for (int j = 0; j < MT; ++j) {
-      const float s = warp_sum(acc[j]);
-      if (lane == 0 && m0 + j < M) {
-        float r = s + (bias ? bias[n] : 0.f);
-        out[static_cast<int64_t>(m0 + j) * N + n] = act_out ? silu(r) : r;
+    for (int c = 0; c < COLS; ++c) {
+#pragma unroll
+      for (int j = 0; j < GEMV_MT; ++j) {
+        if (j < mt) {
+          const float sum = warp_sum(acc[c][j]);
+          if (lane == 0 && n0 + c < N) {
+            const float r = sum + (bias ? bias[n0 + c] : 0.f);
+            out[static_cast<int64_t>(m0 + j) * N + n0 + c] = act_out ? silu(r) : r;
+          }
+        }
       }
     }
   }
@@ -305,16 +348,22 @@ extern "C" int iris_gemv(const float* x, int64_t M, int64_t K, const void* w, in
   IRIS_REQUIRE(M < (1 << 20) && N < (1ll << 31) && K < (1ll << 31), "gemv: size");
   IRIS_REQUIRE(w_dtype == IRIS_F32 || w_dtype == IRIS_BF16, "gemv: weights must be f32 or bf16");
   IRIS_REQUIRE(aligned16(x) && aligned16(w), "gemv: pointers must be 16-byte aligned");
-  const unsigned grid = static_cast<unsigned>((N + THREADS / 32 - 1) / (THREADS / 32));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (w_dtype == IRIS_BF16)
-    gemv_kernel<__nv_bfloat16, 4><<<grid, THREADS, 0, st>>>(x, static_cast<int>(M), static_cast<int>(K),
-                                                             reinterpret_cast<const __nv_bfloat16*>(w), bias, out,
-                                                             static_cast<int>(N), act_in, act_out);
-  else
-    gemv_kernel<float, 4><<<grid, THREADS, 0, st>>>(x, static_cast<int>(M), static_cast<int>(K),
-                                                     reinterpret_cast<const float*>(w), bias, out,
-                                                     static_cast<int>(N), act_in, act_out);
+  // two columns per warp when that still gives every SM a few blocks, else one
+  const bool wide = N >= static_cast<int64_t>(num_sms()) * 4 * (THREADS / 32) * 2;
+  const int cols = wide ? 2 : 1;
+  const int64_t per_block = static_cast<int64_t>(THREADS / 32) * cols;
+  const unsigned grid = static_cast<unsigned>((N + per_block - 1) / per_block);
+  const int Mi = static_cast<int>(M), Ki = static_cast<int>(K), Ni = static_cast<int>(N);
+  if (w_dtype == IRIS_BF16) {
+    const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(w);
+    if (wide) gemv_kernel<__nv_bfloat16, 2><<<grid, THREADS, 0, st>>>(x, Mi, Ki, wb, bias, out, Ni, act_in, act_out);
+    else gemv_kernel<__nv_bfloat16, 1><<<grid, THREADS, 0, st>>>(x, Mi, Ki, wb, bias, out, Ni, act_in, act_out);
+  } else {
+    const float* wf = reinterpret_cast<const float*>(w);
+    if (wide) gemv_kernel<float, 2><<<grid, THREADS, 0, st>>>(x, Mi, Ki, wf, bias, out, Ni, act_in, act_out);
+    else gemv_kernel<float, 1><<<grid, THREADS, 0, st>>>(x, Mi, Ki, wf, bias, out, Ni, act_in, act_out);
+  }
   IRIS_CUDA(cudaGetLastError());
   return IRIS_OK;
 }

@@ -226,8 +226,9 @@ class CudaIris:
             raise ValueError("CudaIris: s_embedder.proj takes 1 to 4 channels of patch_size^2 pixels")
         if (self.in_channels * pp) % 8:
             raise ValueError("CudaIris needs in_channels * patch_size^2 to be a multiple of 8")
-        self.t_mlp = [(f32(f"t_embedder.mlp.{i}.weight"), f32(f"t_embedder.mlp.{i}.bias")) for i in (0, 2)]
-        self.cores = {s: (f32(f"modulation_cores.adaln_{s}.weight"), f32(f"modulation_cores.adaln_{s}.bias"))
+        # conditioning linears in BF16 like every other trunk linear (the GEMV reads them once per step)
+        self.t_mlp = [(bf(f"t_embedder.mlp.{i}.weight"), f32(f"t_embedder.mlp.{i}.bias")) for i in (0, 2)]
+        self.cores = {s: (bf(f"modulation_cores.adaln_{s}.weight"), f32(f"modulation_cores.adaln_{s}.bias"))
                       for s in ("img", "txt")}  # fmt: skip
         self.blocks: list[_Block] = []
         img_bias, txt_bias = [], []
@@ -508,16 +509,16 @@ class CudaIris:
         _lib.call("iris_timestep_embedding", t.data_ptr(), ws["t_freq"].data_ptr(), batch, 256,
                   float(cfg.timestep_max_period), st)  # fmt: skip
         (w0, b0), (w2, b2) = self.t_mlp
-        _lib.call("iris_gemv", ws["t_freq"].data_ptr(), batch, 256, w0.data_ptr(), _lib.F32, b0.data_ptr(),
+        _lib.call("iris_gemv", ws["t_freq"].data_ptr(), batch, 256, w0.data_ptr(), _lib.BF16, b0.data_ptr(),
                   ws["t_h"].data_ptr(), d, 0, 1, st)  # fmt: skip
-        _lib.call("iris_gemv", ws["t_h"].data_ptr(), batch, d, w2.data_ptr(), _lib.F32, b2.data_ptr(),
+        _lib.call("iris_gemv", ws["t_h"].data_ptr(), batch, d, w2.data_ptr(), _lib.BF16, b2.data_ptr(),
                   ws["t_emb"].data_ptr(), d, 0, 0, st)  # fmt: skip
         for name, bias_table in (("img", self.img_bias), ("txt", self.txt_bias)):
             if bias_table is None:
                 continue
             w, b = self.cores[name]
             core = ws[f"core_{name}"]
-            _lib.call("iris_gemv", ws["t_emb"].data_ptr(), batch, d, w.data_ptr(), _lib.F32, b.data_ptr(),
+            _lib.call("iris_gemv", ws["t_emb"].data_ptr(), batch, d, w.data_ptr(), _lib.BF16, b.data_ptr(),
                       core.data_ptr(), 6 * d, 1, 0, st)  # fmt: skip
             _lib.call("iris_add_bias_rows", core.data_ptr(), bias_table.data_ptr(), ws[f"mods_{name}"].data_ptr(),
                       batch, bias_table.shape[0], 6 * d, st)  # fmt: skip

@@ -498,6 +498,26 @@ def test_timestep_gemv_and_cfg_euler(K):
     torch.testing.assert_close(nxt, expected, rtol=1e-5, atol=1e-5)
 
 
+@pytest.mark.parametrize("M,N,Kd", [(2, 18432, 3072), (16, 18432, 3072), (20, 3072, 3072), (1, 3072, 256),
+                                     (3, 100, 200)])  # fmt: skip
+@pytest.mark.parametrize("w_dtype", [torch.bfloat16, torch.float32])
+def test_gemv_matches_fp32_reference(K, M, N, Kd, w_dtype):
+    """The conditioning GEMV at the shared adaLN core (18432 x 3072) and
+    timestep-MLP shapes, B = 2 and the 16 rows of the benchmark's calls (one
+    pass over the weights), more rows than one pass, ragged K and N."""
+    from iris_b200 import _lib
+
+    gen = torch.Generator(device="cuda").manual_seed(M + N)
+    x = torch.randn(M, Kd, device="cuda", generator=gen)
+    w = (torch.randn(N, Kd, device="cuda", generator=gen) * 0.02).to(w_dtype)
+    b = torch.randn(N, device="cuda", generator=gen)
+    out = torch.empty(M, N, device="cuda")
+    _lib.call("iris_gemv", x.data_ptr(), M, Kd, w.data_ptr(), _lib.BF16 if w_dtype == torch.bfloat16 else _lib.F32,
+              b.data_ptr(), out.data_ptr(), N, 1, 0, torch.cuda.current_stream().cuda_stream)  # fmt: skip
+    want = F.silu(x) @ w.float().T + b
+    torch.testing.assert_close(out, want, rtol=1e-4, atol=1e-4)
+
+
 def test_require_finite_on_device(K):
     from iris_b200.model import require_finite
 
