@@ -593,8 +593,8 @@ IRIS_DEVICE void epilogue_barrier() { asm volatile("bar.sync 1, 128;" ::: "memor
 // column 0 at this warp's lane quarter). The piece's accumulator goes to its
 // slot (column quads outermost, rows contiguous: a warp's store is 512
 // contiguous bytes), then one thread counts the arrival; no thread waits on
-// another CTA. The last piece to arrive adds every other piece's partial into
-// its TMEM accumulator and returns true (it runs the tile's epilogue).
+// another CTA. The last piece to arrive writes the sum of all pieces' partials
+// into its TMEM accumulator and returns true (it runs the tile's epilogue).
 IRIS_DEVICE bool split_tile_fixup(const Batch& bt, const Unit& u, uint32_t rank, uint32_t t_acc, int row,
                                   volatile int* last_flag) {
   float4* own = reinterpret_cast<float4*>(bt.partials + (static_cast<size_t>(u.slot) * 2 + rank) * SLOT_FLOATS);
@@ -635,33 +635,41 @@ IRIS_DEVICE bool split_tile_fixup(const Batch& bt, const Unit& u, uint32_t rank,
   epilogue_barrier();
   if (*last_flag == 0) return false;
   __threadfence();
+  // the sum of every piece's partial in pair order (its own included, read back
+  // from its slot), so the result does not depend on which piece came last
 #pragma unroll 1
-  for (int q = first; q <= final_pair; ++q) {
-    const int slot = q * 2 + ((q * per) / nk == u.sk ? 0 : 1);
-    if (slot == u.slot) continue;
-    const float4* other =
-        reinterpret_cast<const float4*>(bt.partials + (static_cast<size_t>(slot) * 2 + rank) * SLOT_FLOATS);
+  for (int c = 0; c < 8; ++c) {
+    float4 sum[8];
+#pragma unroll
+    for (int g = 0; g < 8; ++g) sum[g] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 1
-    for (int c = 0; c < 8; ++c) {
-      uint32_t r[32];
-      tmem_ld32(t_acc + c * 32, r);
-      tmem_wait_ld();
-      uint32_t lo[16], hi[16];
+    for (int q = first; q <= final_pair; ++q) {
+      const int slot = q * 2 + ((q * per) / nk == u.sk ? 0 : 1);
+      const float4* part =
+          reinterpret_cast<const float4*>(bt.partials + (static_cast<size_t>(slot) * 2 + rank) * SLOT_FLOATS);
 #pragma unroll
       for (int g = 0; g < 8; ++g) {
-        const float4 v = __ldcg(other + (c * 8 + g) * 128 + row);
-        uint32_t* dst = g < 4 ? lo : hi;
-        const int e = (g & 3) * 4;
-        dst[e] = __float_as_uint(__uint_as_float(r[4 * g]) + v.x);
-        dst[e + 1] = __float_as_uint(__uint_as_float(r[4 * g + 1]) + v.y);
-        dst[e + 2] = __float_as_uint(__uint_as_float(r[4 * g + 2]) + v.z);
-        dst[e + 3] = __float_as_uint(__uint_as_float(r[4 * g + 3]) + v.w);
+        const float4 v = __ldcg(part + (c * 8 + g) * 128 + row);
+        sum[g].x += v.x;
+        sum[g].y += v.y;
+        sum[g].z += v.z;
+        sum[g].w += v.w;
       }
-      tmem_st16(t_acc + c * 32, lo);
-      tmem_st16(t_acc + c * 32 + 16, hi);
     }
-    tmem_wait_st();
+    uint32_t lo[16], hi[16];
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      uint32_t* dst = g < 4 ? lo : hi;
+      const int e = (g & 3) * 4;
+      dst[e] = __float_as_uint(sum[g].x);
+      dst[e + 1] = __float_as_uint(sum[g].y);
+      dst[e + 2] = __float_as_uint(sum[g].z);
+      dst[e + 3] = __float_as_uint(sum[g].w);
+    }
+    tmem_st16(t_acc + c * 32, lo);
+    tmem_st16(t_acc + c * 32 + 16, hi);
   }
+  tmem_wait_st();
   return true;
 }
 static_assert(SMEM_BYTES <= 232448, "pair kernel shared memory");
