@@ -90,6 +90,31 @@ int iris_gated_residual_rms_norm(float* residual, int64_t res_seg_rows, int64_t 
                                  const float* next_scale, int64_t next_mod_stride, void* next_out, int next_out_dtype,
                                  int64_t nx_seg_rows, int64_t nx_seg_stride, int64_t nx_seg_offset, void* stream);
 
+/* The arguments of iris_gated_residual_rms_norm for one stream's rows. */
+typedef struct iris_residual_problem {
+  float* residual;
+  int64_t res_seg_rows, res_seg_stride, res_seg_offset;
+  const void* branch;
+  int64_t br_seg_rows, br_seg_stride, br_seg_offset;
+  const float* weight;
+  const float* gate;
+  int64_t mod_stride, rows, rows_per_batch;
+  int next_mode;
+  const float* next_weight;
+  const float* next_shift;
+  const float* next_scale;
+  int64_t next_mod_stride;
+  void* next_out;
+  int64_t nx_seg_rows, nx_seg_stride, nx_seg_offset;
+} iris_residual_problem;
+
+/* 1 or 2 residual updates of one width and dtypes in one launch: the text- and
+ * image-stream rows of a dual block (src/iris_metal/model.py:284-289, the
+ * reference's gated_residual_rms_norm_ once per stream), each with its own
+ * weights, modulation rows and row maps. */
+int iris_gated_residual_rms_norm_grouped(const iris_residual_problem* problems, int count, int branch_dtype,
+                                         int next_out_dtype, int64_t width, float eps, void* stream);
+
 /* x[r] = rms_norm(x[r]) * weight + add[r % rows_per_batch]  (in place, fp32):
  * TextEmbedder norm + y_pos_embedding, src/iris3b/models/dit.py:263-281. */
 int iris_rms_norm_add_rows(float* x, const float* weight, const float* add, int64_t rows, int64_t rows_per_batch,

@@ -342,14 +342,52 @@ __global__ void __launch_bounds__(ROW_THREADS, CPT <= 24 ? 4 : 3) rms_norm_modul
   cp_async_wait<0>();
 }
 
+// One residual update of the row kernel: the arguments of
+// iris_gated_residual_rms_norm for one stream's rows.
+struct ResidualSeg {
+  float* residual;
+  RowMap rmap;
+  const void* branch;
+  RowMap bmap;
+  const float* weight;
+  const float* gate;
+  int64_t mod_stride, rows, rows_per_batch;
+  int next_mode;
+  const float* next_weight;
+  const float* next_shift;
+  const float* next_scale;
+  int64_t next_mod_stride;
+  void* next_out;
+  RowMap nmap;
+};
+
+// Up to two segments (a dual block's text and image rows) in one launch: CTA
+// r < seg[0].rows takes row r of segment 0, the others row r - seg[0].rows of
+// segment 1.
+struct ResidualRows {
+  ResidualSeg seg[2];
+  int count;
+};
+
 template <typename TB, typename TO, int VPT>
-__global__ void __launch_bounds__(ROW_THREADS) gated_residual_row_kernel(
-    float* __restrict__ residual, RowMap rmap, const TB* __restrict__ branch, RowMap bmap,
-    const float* __restrict__ weight, const float* __restrict__ gate, int64_t mod_stride, int64_t rows_per_batch,
-    int width, float eps, int next_mode, const float* __restrict__ next_weight, const float* __restrict__ next_shift,
-    const float* __restrict__ next_scale, int64_t next_mod_stride, TO* __restrict__ next_out, RowMap nmap) {
+__global__ void __launch_bounds__(ROW_THREADS) gated_residual_row_kernel(const __grid_constant__ ResidualRows rr,
+                                                                         int width, float eps) {
   __shared__ float red[2][4];
-  const int64_t r = blockIdx.x;
+  const bool second = rr.count > 1 && static_cast<int64_t>(blockIdx.x) >= rr.seg[0].rows;
+  const ResidualSeg& sg = rr.seg[second ? 1 : 0];
+  const int64_t r = static_cast<int64_t>(blockIdx.x) - (second ? rr.seg[0].rows : 0);
+  float* __restrict__ residual = sg.residual;
+  const RowMap rmap = sg.rmap, bmap = sg.bmap, nmap = sg.nmap;
+  const TB* __restrict__ branch = reinterpret_cast<const TB*>(sg.branch);
+  const float* __restrict__ weight = sg.weight;
+  const float* __restrict__ gate = sg.gate;
+  const int64_t mod_stride = sg.mod_stride, rows_per_batch = sg.rows_per_batch;
+  const int next_mode = sg.next_mode;
+  const float* __restrict__ next_weight = sg.next_weight;
+  const float* __restrict__ next_shift = sg.next_shift;
+  const float* __restrict__ next_scale = sg.next_scale;
+  const int64_t next_mod_stride = sg.next_mod_stride;
+  TO* __restrict__ next_out = reinterpret_cast<TO*>(sg.next_out);
   const int t = threadIdx.x;
   const TB* br = branch + bmap(r) * width;
   float* xr = residual + rmap(r) * width;
@@ -512,29 +550,42 @@ int launch_norm_modulate(const void* x, RowMap xm, void* out, const float* w, co
   return IRIS_OK;
 }
 
+bool row_kernel_width(int width) { return width % (4 * ROW_THREADS) == 0 && width / (4 * ROW_THREADS) <= 8; }
+
+// The row kernel over one or two segments (all rows of one width, branch and
+// next-output dtypes).
+template <typename TB, typename TO>
+int launch_residual_rows(const ResidualRows& rr, int width, float eps, cudaStream_t st) {
+  const int64_t rows = rr.seg[0].rows + (rr.count > 1 ? rr.seg[1].rows : 0);
+  if (rows == 0) return IRIS_OK;
+  IRIS_REQUIRE(rows < (1ll << 31), "gated_residual_rms_norm_: too many rows");
+  const int vpt = width / (4 * ROW_THREADS);
+#define IRIS_ROW(VPT) \
+  gated_residual_row_kernel<TB, TO, VPT><<<static_cast<unsigned>(rows), ROW_THREADS, 0, st>>>(rr, width, eps)
+  switch (vpt) {
+    case 1: IRIS_ROW(1); break;
+    case 2: IRIS_ROW(2); break;
+    case 3: IRIS_ROW(3); break;
+    case 4: IRIS_ROW(4); break;
+    case 5: IRIS_ROW(5); break;
+    case 6: IRIS_ROW(6); break;
+    case 7: IRIS_ROW(7); break;
+    default: IRIS_ROW(8); break;
+  }
+#undef IRIS_ROW
+  IRIS_CUDA(cudaGetLastError());
+  return IRIS_OK;
+}
+
 template <typename TB, typename TO>
 int launch_residual(float* res, RowMap rm, const void* branch, RowMap bm, const float* w, const float* gate,
                     int64_t ms, int64_t rows, int64_t rpb, int width, float eps, int mode, const float* nw,
                     const float* nsh, const float* nsc, int64_t nms, void* nout, RowMap nm, cudaStream_t st) {
-  if (width % (4 * ROW_THREADS) == 0 && width / (4 * ROW_THREADS) <= 8 && rows < (1ll << 31)) {
-    const int vpt = width / (4 * ROW_THREADS);
-#define IRIS_ROW(VPT)                                                                                              \
-  gated_residual_row_kernel<TB, TO, VPT><<<static_cast<unsigned>(rows), ROW_THREADS, 0, st>>>(                     \
-      res, rm, reinterpret_cast<const TB*>(branch), bm, w, gate, ms, rpb, width, eps, mode, nw, nsh, nsc, nms,     \
-      reinterpret_cast<TO*>(nout), nm)
-    switch (vpt) {
-      case 1: IRIS_ROW(1); break;
-      case 2: IRIS_ROW(2); break;
-      case 3: IRIS_ROW(3); break;
-      case 4: IRIS_ROW(4); break;
-      case 5: IRIS_ROW(5); break;
-      case 6: IRIS_ROW(6); break;
-      case 7: IRIS_ROW(7); break;
-      default: IRIS_ROW(8); break;
-    }
-#undef IRIS_ROW
-    IRIS_CUDA(cudaGetLastError());
-    return IRIS_OK;
+  if (row_kernel_width(width) && rows < (1ll << 31)) {
+    ResidualRows rr{};
+    rr.count = 1;
+    rr.seg[0] = ResidualSeg{res, rm, branch, bm, w, gate, ms, rows, rpb, mode, nw, nsh, nsc, nms, nout, nm};
+    return launch_residual_rows<TB, TO>(rr, width, eps, st);
   }
   const int nv = width / 128;
   const unsigned grid = static_cast<unsigned>((rows + WARPS - 1) / WARPS);
@@ -598,45 +649,65 @@ extern "C" int iris_rms_norm_modulate(const void* x, int x_dtype, int64_t x_seg_
                                                     rows_per_batch, w, eps, st);
 }
 
-extern "C" int iris_gated_residual_rms_norm(float* residual, int64_t res_seg_rows, int64_t res_seg_stride,
-                                            int64_t res_seg_offset, const void* branch, int branch_dtype,
-                                            int64_t br_seg_rows, int64_t br_seg_stride, int64_t br_seg_offset,
-                                            const float* weight, const float* gate, int64_t mod_stride, int64_t rows,
-                                            int64_t rows_per_batch, int64_t width, float eps, int next_mode,
-                                            const float* next_weight, const float* next_shift,
-                                            const float* next_scale, int64_t next_mod_stride, void* next_out,
-                                            int next_out_dtype, int64_t nx_seg_rows, int64_t nx_seg_stride,
-                                            int64_t nx_seg_offset, void* stream) {
-  using namespace iris::rows;
-  IRIS_REQUIRE(residual && branch && weight, "gated_residual_rms_norm_: null pointer");
+static int check_residual(const iris_residual_problem& q, int branch_dtype, int next_out_dtype, int64_t width) {
+  IRIS_REQUIRE(q.residual && q.branch && q.weight, "gated_residual_rms_norm_: null pointer");
   IRIS_REQUIRE(width > 0 && width % 128 == 0 && width <= 4096, "gated_residual_rms_norm_: width % 128 != 0");
-  IRIS_REQUIRE(rows >= 0 && rows_per_batch > 0 && res_seg_rows > 0 && br_seg_rows > 0,
+  IRIS_REQUIRE(q.rows >= 0 && q.rows_per_batch > 0 && q.res_seg_rows > 0 && q.br_seg_rows > 0,
                "gated_residual_rms_norm_: bad row counts");
   IRIS_REQUIRE(branch_dtype >= IRIS_F32 && branch_dtype <= IRIS_F16, "gated_residual_rms_norm_: bad branch dtype");
-  IRIS_REQUIRE(aligned16(residual) && aligned16(branch) && aligned16(weight),
+  IRIS_REQUIRE(aligned16(q.residual) && aligned16(q.branch) && aligned16(q.weight),
                "gated_residual_rms_norm_: pointers must be 16-byte aligned");
-  IRIS_CHECK_STATUS(check_mod(gate, mod_stride, "gated_residual_rms_norm_"));
-  IRIS_REQUIRE(next_mode >= IRIS_NEXT_NONE && next_mode <= IRIS_NEXT_SILU_ADD, "gated_residual_rms_norm_: bad next_mode");
-  if (next_mode != IRIS_NEXT_NONE) {
-    IRIS_REQUIRE(next_out && aligned16(next_out), "gated_residual_rms_norm_: next output must be 16-byte aligned");
+  IRIS_CHECK_STATUS(check_mod(q.gate, q.mod_stride, "gated_residual_rms_norm_"));
+  IRIS_REQUIRE(q.next_mode >= IRIS_NEXT_NONE && q.next_mode <= IRIS_NEXT_SILU_ADD,
+               "gated_residual_rms_norm_: bad next_mode");
+  if (q.next_mode != IRIS_NEXT_NONE) {
+    IRIS_REQUIRE(q.next_out && aligned16(q.next_out), "gated_residual_rms_norm_: next output must be 16-byte aligned");
     IRIS_REQUIRE(next_out_dtype == IRIS_BF16 || next_out_dtype == IRIS_F32, "gated_residual_rms_norm_: next dtype");
-    IRIS_REQUIRE(nx_seg_rows > 0, "gated_residual_rms_norm_: next row map needs seg_rows > 0");
-    IRIS_CHECK_STATUS(check_mod(next_shift, next_mod_stride, "gated_residual_rms_norm_ (next)"));
-    if (next_mode == IRIS_NEXT_NORM_MODULATE) {
-      IRIS_REQUIRE(next_weight && aligned16(next_weight), "gated_residual_rms_norm_: next weight");
-      IRIS_CHECK_STATUS(check_mod(next_scale, next_mod_stride, "gated_residual_rms_norm_ (next)"));
+    IRIS_REQUIRE(q.nx_seg_rows > 0, "gated_residual_rms_norm_: next row map needs seg_rows > 0");
+    IRIS_CHECK_STATUS(check_mod(q.next_shift, q.next_mod_stride, "gated_residual_rms_norm_ (next)"));
+    if (q.next_mode == IRIS_NEXT_NORM_MODULATE) {
+      IRIS_REQUIRE(q.next_weight && aligned16(q.next_weight), "gated_residual_rms_norm_: next weight");
+      IRIS_CHECK_STATUS(check_mod(q.next_scale, q.next_mod_stride, "gated_residual_rms_norm_ (next)"));
     }
   }
-  if (rows == 0) return IRIS_OK;
-  const RowMap rm{res_seg_rows, res_seg_stride, res_seg_offset};
-  const RowMap bm{br_seg_rows, br_seg_stride, br_seg_offset};
-  const RowMap nm{nx_seg_rows > 0 ? nx_seg_rows : 1, nx_seg_stride, nx_seg_offset};
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return IRIS_OK;
+}
+
+template <typename TB, typename TO>
+static int residual_problems(const iris_residual_problem* qs, int count, int64_t width, float eps, cudaStream_t st) {
+  using namespace iris::rows;
   const int w = static_cast<int>(width);
-#define IRIS_RES(TB, TO)                                                                                          \
-  return launch_residual<TB, TO>(residual, rm, branch, bm, weight, gate, mod_stride, rows, rows_per_batch, w, eps, \
-                                 next_mode, next_weight, next_shift, next_scale, next_mod_stride, next_out, nm, st)
+  auto seg = [](const iris_residual_problem& q) {
+    return ResidualSeg{q.residual, RowMap{q.res_seg_rows, q.res_seg_stride, q.res_seg_offset}, q.branch,
+                       RowMap{q.br_seg_rows, q.br_seg_stride, q.br_seg_offset}, q.weight, q.gate, q.mod_stride, q.rows,
+                       q.rows_per_batch, q.next_mode, q.next_weight, q.next_shift, q.next_scale, q.next_mod_stride,
+                       q.next_out, RowMap{q.nx_seg_rows > 0 ? q.nx_seg_rows : 1, q.nx_seg_stride, q.nx_seg_offset}};
+  };
+  if (row_kernel_width(w)) {
+    ResidualRows rr{};
+    rr.count = count;
+    for (int i = 0; i < count; ++i) rr.seg[i] = seg(qs[i]);
+    return launch_residual_rows<TB, TO>(rr, w, eps, st);
+  }
+  for (int i = 0; i < count; ++i) {
+    const ResidualSeg g = seg(qs[i]);
+    if (g.rows == 0) continue;
+    const int status = launch_residual<TB, TO>(g.residual, g.rmap, g.branch, g.bmap, g.weight, g.gate, g.mod_stride,
+                                               g.rows, g.rows_per_batch, w, eps, g.next_mode, g.next_weight,
+                                               g.next_shift, g.next_scale, g.next_mod_stride, g.next_out, g.nmap, st);
+    if (status != IRIS_OK) return status;
+  }
+  return IRIS_OK;
+}
+
+extern "C" int iris_gated_residual_rms_norm_grouped(const iris_residual_problem* problems, int count,
+                                                    int branch_dtype, int next_out_dtype, int64_t width, float eps,
+                                                    void* stream) {
+  IRIS_REQUIRE(problems != nullptr && count >= 1 && count <= 2, "gated_residual_rms_norm_: 1 or 2 problems per launch");
+  for (int i = 0; i < count; ++i) IRIS_CHECK_STATUS(check_residual(problems[i], branch_dtype, next_out_dtype, width));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool nf32 = next_out_dtype == IRIS_F32;
+#define IRIS_RES(TB, TO) return residual_problems<TB, TO>(problems, count, width, eps, st)
   if (branch_dtype == IRIS_BF16) {
     if (nf32) IRIS_RES(__nv_bfloat16, float);
     IRIS_RES(__nv_bfloat16, __nv_bfloat16);
@@ -648,6 +719,23 @@ extern "C" int iris_gated_residual_rms_norm(float* residual, int64_t res_seg_row
   if (nf32) IRIS_RES(float, float);
   IRIS_RES(float, __nv_bfloat16);
 #undef IRIS_RES
+}
+
+extern "C" int iris_gated_residual_rms_norm(float* residual, int64_t res_seg_rows, int64_t res_seg_stride,
+                                            int64_t res_seg_offset, const void* branch, int branch_dtype,
+                                            int64_t br_seg_rows, int64_t br_seg_stride, int64_t br_seg_offset,
+                                            const float* weight, const float* gate, int64_t mod_stride, int64_t rows,
+                                            int64_t rows_per_batch, int64_t width, float eps, int next_mode,
+                                            const float* next_weight, const float* next_shift,
+                                            const float* next_scale, int64_t next_mod_stride, void* next_out,
+                                            int next_out_dtype, int64_t nx_seg_rows, int64_t nx_seg_stride,
+                                            int64_t nx_seg_offset, void* stream) {
+  const iris_residual_problem q{residual,    res_seg_rows,    res_seg_stride, res_seg_offset, branch,
+                                br_seg_rows, br_seg_stride,   br_seg_offset,  weight,         gate,
+                                mod_stride,  rows,            rows_per_batch, next_mode,      next_weight,
+                                next_shift,  next_scale,      next_mod_stride, next_out,      nx_seg_rows,
+                                nx_seg_stride, nx_seg_offset};
+  return iris_gated_residual_rms_norm_grouped(&q, 1, branch_dtype, next_out_dtype, width, eps, stream);
 }
 
 extern "C" int iris_rms_norm_add_rows(float* x, const float* weight, const float* add, int64_t rows,

@@ -78,6 +78,19 @@ class GemmProblem(ctypes.Structure):
     ]  # fmt: skip
 
 
+class ResidualProblem(ctypes.Structure):
+    """``iris_residual_problem`` of include/iris_b200.h."""
+
+    _fields_ = [
+        ("residual", P), ("res_seg_rows", I64), ("res_seg_stride", I64), ("res_seg_offset", I64),
+        ("branch", P), ("br_seg_rows", I64), ("br_seg_stride", I64), ("br_seg_offset", I64),
+        ("weight", P), ("gate", P), ("mod_stride", I64), ("rows", I64), ("rows_per_batch", I64),
+        ("next_mode", I32), ("next_weight", P), ("next_shift", P), ("next_scale", P), ("next_mod_stride", I64),
+        ("next_out", P), ("nx_seg_rows", I64), ("nx_seg_stride", I64), ("nx_seg_offset", I64),
+    ]  # fmt: skip
+
+
+SIGNATURES["iris_gated_residual_rms_norm_grouped"] = [ctypes.POINTER(ResidualProblem), I32, I32, I32, I64, F, P]
 SIGNATURES["iris_gemm_bf16_grouped"] = [ctypes.POINTER(GemmProblem), I32, P]
 SIGNATURES["iris_gemm_bf16_grouped_ws"] = [ctypes.POINTER(GemmProblem), I32, P, I64, P]
 SIGNATURES["iris_gemm_workspace_bytes"] = [ctypes.POINTER(I64)]

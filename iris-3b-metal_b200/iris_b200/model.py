@@ -630,12 +630,12 @@ class CudaIris:
         else:
             self._attention_sequence_parallel(block, segs, ws, g, st)
         grouped("og", block.proj, "branch")
-        for s, rows, rpb, tmap, off in segs:
-            self._attn_residual(block, s, rows, rpb, tmap, off, ws, g, eps, st)
+        # one launch for both streams' residual rows, as for the GEMMs
+        _residuals([self._attn_residual(block, *seg, ws, g) for seg in segs], g.d, eps, st)
         grouped("h2", block.w13, "act", epilogue=_lib.EPI_SWIGLU)
         grouped("act", block.w2, "branch")
-        for s, rows, rpb, tmap, off in segs:
-            self._mlp_residual(block, nxt, s, rows, rpb, tmap, off, ws, g, eps, st)
+        _residuals([self._mlp_residual(block, nxt, *seg, ws, g) for seg in segs if nxt is not None or seg[0] != "y"],
+                   g.d, eps, st)  # fmt: skip
 
     def _attention_sequence_parallel(self, block, segs, ws, g, st) -> None:
         """Ulysses attention: Q/K/V (head-major, this rank's tokens) -> all-to-all
@@ -679,21 +679,20 @@ class CudaIris:
         self._epoch += 1
         K.peer_barrier(ws["flags"], ws["_peers"].ptrs["flags"], self.comm.rank, self._epoch, self.peer_timeout_s)
 
-    def _attn_residual(self, block, stream, rows, rpb, tmap, off, ws, g, eps, st) -> None:
+    def _attn_residual(self, block, stream, rows, rpb, tmap, off, ws, g) -> "_lib.ResidualProblem":
         """Post-norm + gate + residual of the attention branch, fused with the
         MLP branch's input norm-modulate (written to ``h2``)."""
         d = g.d
         mods = self._mods(ws, block, stream)
         norms = block.norms[stream]
         h2, branch = ws["h2"][off : off + rows], ws["branch"][off : off + rows]
-        _lib.call(
-            "iris_gated_residual_rms_norm", ws["tokens"].data_ptr(), *tmap, branch.data_ptr(), _lib.BF16, rows, 0, 0,
-            norms["post_attn"].data_ptr(), self._chunk(mods, 2, d), 6 * d, rows, rpb, d, eps, _lib.NEXT_NORM_MODULATE,
-            norms["norm2"].data_ptr(), self._chunk(mods, 3, d), self._chunk(mods, 4, d), 6 * d, h2.data_ptr(),
-            _lib.BF16, rows, 0, 0, st,
+        return _lib.ResidualProblem(
+            ws["tokens"].data_ptr(), *tmap, branch.data_ptr(), rows, 0, 0, norms["post_attn"].data_ptr(),
+            self._chunk(mods, 2, d), 6 * d, rows, rpb, _lib.NEXT_NORM_MODULATE, norms["norm2"].data_ptr(),
+            self._chunk(mods, 3, d), self._chunk(mods, 4, d), 6 * d, h2.data_ptr(), rows, 0, 0,
         )  # fmt: skip
 
-    def _mlp_residual(self, block, nxt, stream, rows, rpb, tmap, off, ws, g, eps, st) -> None:
+    def _mlp_residual(self, block, nxt, stream, rows, rpb, tmap, off, ws, g) -> "_lib.ResidualProblem":
         """Post-norm + gate + residual of the MLP branch; it also writes the next
         block's input (or, after the last block, ``silu(t_emb + x)`` of the image rows)."""
         d = g.d
@@ -704,13 +703,11 @@ class CudaIris:
         if nxt is None:
             # last block: only image rows continue; they leave as s = silu(t_emb + x)
             image_map = (g.L, g.N, g.T)
-            _lib.call(
-                "iris_gated_residual_rms_norm", tok, *image_map, branch.data_ptr(), _lib.BF16, *image_map,
-                norms["post_mlp"].data_ptr(), self._chunk(mods, 5, d), 6 * d, g.batch * g.L, g.L, d, eps,
-                _lib.NEXT_SILU_ADD, None, ws["t_emb"].data_ptr(), None, d, ws["s_cond"].data_ptr(), _lib.BF16,
-                g.batch * g.L, 0, 0, st,
+            return _lib.ResidualProblem(
+                tok, *image_map, branch.data_ptr(), *image_map, norms["post_mlp"].data_ptr(), self._chunk(mods, 5, d),
+                6 * d, g.batch * g.L, g.L, _lib.NEXT_SILU_ADD, None, ws["t_emb"].data_ptr(), None, d,
+                ws["s_cond"].data_ptr(), g.batch * g.L, 0, 0,
             )  # fmt: skip
-            return
         nstream = stream if nxt.dual else "j"
         nmods = self._mods(ws, nxt, nstream)
         if nxt.dual:
@@ -720,11 +717,10 @@ class CudaIris:
             next_map = tmap if stream != "j" else (rows, 0, 0)
             # a separate buffer: the other stream of this dual block may still read ws["h"]
             next_out = ws["hj"]
-        _lib.call(
-            "iris_gated_residual_rms_norm", tok, *tmap, branch.data_ptr(), _lib.BF16, rows, 0, 0,
-            norms["post_mlp"].data_ptr(), self._chunk(mods, 5, d), 6 * d, rows, rpb, d, eps, _lib.NEXT_NORM_MODULATE,
-            nxt.norms[nstream]["norm1"].data_ptr(), self._chunk(nmods, 0, d), self._chunk(nmods, 1, d), 6 * d,
-            next_out.data_ptr(), _lib.BF16, *next_map, st,
+        return _lib.ResidualProblem(
+            tok, *tmap, branch.data_ptr(), rows, 0, 0, norms["post_mlp"].data_ptr(), self._chunk(mods, 5, d), 6 * d,
+            rows, rpb, _lib.NEXT_NORM_MODULATE, nxt.norms[nstream]["norm1"].data_ptr(), self._chunk(nmods, 0, d),
+            self._chunk(nmods, 1, d), 6 * d, next_out.data_ptr(), *next_map,
         )  # fmt: skip
 
     # -- pixel stage ------------------------------------------------------------------
@@ -789,6 +785,12 @@ class CudaIris:
                     b2.data_ptr(), fn.data_ptr(), fw.data_ptr(), fb.data_ptr(), v.data_ptr(), g.batch, height, width,
                     p, g.shard.image_start, g.L, eps, st,
                 )  # fmt: skip
+
+
+def _residuals(problems: list, width: int, eps: float, st: int) -> None:
+    """The residual updates of a block's streams (bf16 branches and next inputs) in one launch."""
+    array = (_lib.ResidualProblem * len(problems))(*problems)
+    _lib.call("iris_gated_residual_rms_norm_grouped", array, len(problems), _lib.BF16, _lib.BF16, width, eps, st)
 
 
 def _hkey(block: _Block) -> str:

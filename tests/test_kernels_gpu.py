@@ -518,6 +518,45 @@ def test_gemv_matches_fp32_reference(K, M, N, Kd, w_dtype):
     torch.testing.assert_close(out, want, rtol=1e-4, atol=1e-4)
 
 
+def test_grouped_residual_matches_separate_launches(K):
+    """A dual block's text and image residual updates in one launch
+    (iris_gated_residual_rms_norm_grouped) give bit-identical rows to one launch
+    per stream, each stream with its own gains, modulation rows and row maps."""
+    from iris_b200 import _lib
+
+    gen = torch.Generator(device="cuda").manual_seed(13)
+    B, T, L, D = 2, 48, 200, 3072
+    N = T + L
+    tokens = torch.randn(B * N, D, device="cuda", generator=gen)
+    branch = torch.randn(B * N, D, device="cuda", generator=gen).to(torch.bfloat16)
+    mods = [torch.randn(B, 6 * D, device="cuda", generator=gen) * 0.1 for _ in range(2)]
+    gains = [torch.rand(D, device="cuda", generator=gen) + 0.5 for _ in range(4)]
+    st = torch.cuda.current_stream().cuda_stream
+
+    def problems(res, nxt):
+        out = []
+        for i, (rows, rpb, tmap, off) in enumerate(((B * T, T, (T, N, 0), 0), (B * L, L, (L, N, T), B * T))):
+            m = mods[i]
+            out.append(_lib.ResidualProblem(
+                res.data_ptr(), *tmap, branch[off:].data_ptr(), rows, 0, 0, gains[i].data_ptr(),
+                m.data_ptr() + 2 * D * 4, 6 * D, rows, rpb, _lib.NEXT_NORM_MODULATE, gains[2 + i].data_ptr(),
+                m.data_ptr() + 3 * D * 4, m.data_ptr() + 4 * D * 4, 6 * D, nxt[off:].data_ptr(), rows, 0, 0,
+            ))  # fmt: skip
+        return out
+
+    res_a, res_b = tokens.clone(), tokens.clone()
+    nxt_a, nxt_b = (torch.zeros(B * N, D, device="cuda", dtype=torch.bfloat16) for _ in range(2))
+    probs = problems(res_a, nxt_a)
+    _lib.call("iris_gated_residual_rms_norm_grouped", (_lib.ResidualProblem * 2)(*probs), 2, _lib.BF16, _lib.BF16, D,
+              1e-6, st)  # fmt: skip
+    for q in problems(res_b, nxt_b):
+        _lib.call("iris_gated_residual_rms_norm_grouped", (_lib.ResidualProblem * 1)(q), 1, _lib.BF16, _lib.BF16, D,
+                  1e-6, st)  # fmt: skip
+    torch.cuda.synchronize()
+    assert torch.equal(res_a, res_b) and torch.equal(nxt_a, nxt_b)
+    assert not torch.equal(res_a, tokens)
+
+
 def test_require_finite_on_device(K):
     from iris_b200.model import require_finite
 
