@@ -212,26 +212,6 @@ typedef struct iris_gemm_problem {
  * same op, separate weights); their output tiles share one tile list. */
 int iris_gemm_bf16_grouped(const iris_gemm_problem* problems, int count, void* stream);
 
-/* The same launch with a stream-K tail (no reference counterpart; F.linear is
- * one cuBLAS call there): when the batch's 256 x 256 tiles would leave the last
- * wave of CTA pairs poorly filled (under 98% of the waves used), all full
- * waves but one run whole tiles and the rest is dealt out to every pair by K
- * blocks; a tile split between pairs is finished by the piece that arrives
- * last (the others leave their fp32 partials in `workspace`; nothing waits on
- * another CTA). Output is the same up to the order of the fp32 sums.
- * `workspace`: at least iris_gemm_workspace_bytes() bytes of device memory,
- * 16-byte aligned, zero-filled before its first use, owned by the caller and
- * used by one stream at a time (launches that share a workspace must not
- * overlap). Null (or a batch that fills its waves, or problems of different K)
- * runs exactly as iris_gemm_bf16_grouped. */
-int iris_gemm_bf16_grouped_ws(const iris_gemm_problem* problems, int count, void* workspace,
-                              int64_t workspace_bytes, void* stream);
-
-/* Bytes of the stream-K workspace for the current device: 512 KB of partial
- * accumulators per resident CTA pair plus arrival counters (about 38 MB on a
- * B200 with 74 pairs). */
-int iris_gemm_workspace_bytes(int64_t* bytes);
-
 /* F.scaled_dot_product_attention, non-causal, unmasked
  * (src/iris_metal/model.py:243-250, src/iris3b/nn/attention.py:61-91):
  * q [b, heads_q, n, 128], k/v [b, heads_kv, n, 128] bf16 contiguous;

@@ -28,7 +28,6 @@
 // head-major layouts). Output and aux rows go through a segmented row map so
 // a stream's rows can live inside a joint [text | image] token buffer.
 #include <algorithm>
-#include <atomic>
 
 #include "common.cuh"
 #include "iris_abi_internal.h"
@@ -107,26 +106,6 @@ struct Batch {
   Problem prob[MAX_PROBLEMS];
   int tile_start[MAX_PROBLEMS + 1];  // prefix sums of the problems' tile counts
   int count;
-  // Stream-K tail (CTA-pair kernel): tiles [0, dp_tiles) run whole, round robin
-  // over the pairs; the K blocks of tiles [dp_tiles, num_tiles) are dealt out
-  // evenly, sk_per_pair consecutive blocks per pair (sk_nk per tile). A tile
-  // whose blocks land on several pairs is finished by the last one to arrive:
-  // every piece stores its fp32 partial accumulator to `partials`, counts
-  // itself in `counters` (tagged with this launch's epoch), and the last adds
-  // the other pieces to its TMEM accumulator and runs the epilogue.
-  int dp_tiles;
-  int sk_nk;  // 0: no stream-K region
-  int sk_per_pair;
-  int sk_total;
-  float* partials;                // [pair][2 pieces][2 CTAs][64 column quads][128 rows][4]
-  unsigned long long* counters;   // [stream-K tile][2 CTAs]: (epoch << 32) | pieces arrived
-  unsigned int epoch;
-};
-
-// One unit of a pair's work: K blocks [kb0, kb1) of tile t; slot >= 0 for a
-// piece of a split tile (its partial-accumulator slot), -1 for a whole tile.
-struct Unit {
-  int t, kb0, kb1, slot, sk;
 };
 
 struct TensorMaps {
@@ -164,35 +143,6 @@ IRIS_DEVICE Tile locate(const Batch& bt, int t) {
   const int gm = min(GROUP_M, pr.num_m - first_m);
   const int in_group = local - group * per_group;
   return Tile{p, first_m + in_group % gm, in_group / gm};
-}
-
-// Unit i of pair `pair` (of `pairs`): its whole tiles of the round-robin region
-// first, then the pieces of its stream-K range [pair * per, (pair + 1) * per)
-// of the tail's K blocks, cut at tile boundaries. False past the last unit.
-IRIS_DEVICE bool unit_at(const Batch& bt, int pair, int pairs, int i, Unit& u) {
-  const int ndp = pair < bt.dp_tiles ? (bt.dp_tiles - 1 - pair) / pairs + 1 : 0;
-  if (i < ndp) {
-    u.t = pair + i * pairs;
-    u.kb0 = 0;
-    u.kb1 = bt.prob[locate(bt, u.t).p].nk;
-    u.slot = -1;
-    u.sk = -1;
-    return true;
-  }
-  if (bt.sk_nk == 0) return false;
-  const int j = i - ndp, nk = bt.sk_nk;
-  const int a = pair * bt.sk_per_pair;
-  const int b = min(a + bt.sk_per_pair, bt.sk_total);
-  const int start = j == 0 ? a : (a / nk + j) * nk;
-  if (start >= b) return false;
-  const int sk = start / nk;
-  const int end = min(b, (sk + 1) * nk);
-  u.t = bt.dp_tiles + sk;
-  u.kb0 = start - sk * nk;
-  u.kb1 = end - sk * nk;
-  u.sk = sk;
-  u.slot = (u.kb0 == 0 && u.kb1 == nk) ? -1 : pair * 2 + (j == 0 ? 0 : 1);
-  return true;
 }
 
 IRIS_DEVICE float sigmoidf_fast(float x) { return 1.0f / (1.0f + __expf(-x)); }
@@ -579,99 +529,8 @@ struct Smem {
   uint64_t teardown;
   uint32_t tmem_base;
   int abort;
-  int split_last;  // stream-K: this CTA's piece of the current split tile arrived last
 };
 static_assert(sizeof(Smem) <= 256, "pair barriers must fit their 256-byte slot");
-
-constexpr int SLOT_FLOATS = 128 * 256;  // one CTA's 128 x 256 fp32 partial accumulator
-constexpr uint32_t kCasLimit = 1u << 20;
-
-IRIS_DEVICE void epilogue_barrier() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-
-// Stream-K fixup of this CTA's 128-row half of a split tile, run by its four
-// epilogue warps (row = this thread's TMEM lane; t_acc = the accumulator's
-// column 0 at this warp's lane quarter). The piece's accumulator goes to its
-// slot (column quads outermost, rows contiguous: a warp's store is 512
-// contiguous bytes), then one thread counts the arrival; no thread waits on
-// another CTA. The last piece to arrive writes the sum of all pieces' partials
-// into its TMEM accumulator and returns true (it runs the tile's epilogue).
-IRIS_DEVICE bool split_tile_fixup(const Batch& bt, const Unit& u, uint32_t rank, uint32_t t_acc, int row,
-                                  volatile int* last_flag) {
-  float4* own = reinterpret_cast<float4*>(bt.partials + (static_cast<size_t>(u.slot) * 2 + rank) * SLOT_FLOATS);
-#pragma unroll 1
-  for (int c = 0; c < 8; ++c) {
-    uint32_t r[32];
-    tmem_ld32(t_acc + c * 32, r);
-    tmem_wait_ld();
-#pragma unroll
-    for (int q = 0; q < 8; ++q)
-      own[(c * 8 + q) * 128 + row] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
-                                                 __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
-  }
-  __threadfence();
-  epilogue_barrier();
-  const int nk = bt.sk_nk, per = bt.sk_per_pair;
-  const int first = (u.sk * nk) / per, final_pair = ((u.sk + 1) * nk - 1) / per;
-  if (threadIdx.x == 64) {  // lane 0 of the first epilogue warp
-    unsigned long long* ctr = bt.counters + static_cast<size_t>(u.sk) * 2 + rank;
-    const unsigned long long tag = static_cast<unsigned long long>(bt.epoch) << 32;
-    unsigned long long seen = *reinterpret_cast<volatile unsigned long long*>(ctr), prev;
-    unsigned int arrived = 0;
-    bool counted = false;
-    for (uint32_t i = 0; i < kCasLimit; ++i) {  // a retry loop, not a wait: it fails only if another piece counted
-      arrived = (seen & 0xffffffff00000000ull) == tag ? static_cast<unsigned int>(seen) : 0u;
-      prev = atomicCAS(ctr, seen, tag | (arrived + 1u));
-      if (prev == seen) {
-        counted = true;
-        break;
-      }
-      seen = prev;
-    }
-    if (!counted) atomicOr(&g_device_error, kErrWaitTimeout);
-    const bool last = counted && arrived + 1u == static_cast<unsigned int>(final_pair - first + 1);
-    if (last) atomicExch(ctr, 0ull);
-    *last_flag = last ? 1 : 0;
-  }
-  epilogue_barrier();
-  if (*last_flag == 0) return false;
-  __threadfence();
-  // the sum of every piece's partial in pair order (its own included, read back
-  // from its slot), so the result does not depend on which piece came last
-#pragma unroll 1
-  for (int c = 0; c < 8; ++c) {
-    float4 sum[8];
-#pragma unroll
-    for (int g = 0; g < 8; ++g) sum[g] = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 1
-    for (int q = first; q <= final_pair; ++q) {
-      const int slot = q * 2 + ((q * per) / nk == u.sk ? 0 : 1);
-      const float4* part =
-          reinterpret_cast<const float4*>(bt.partials + (static_cast<size_t>(slot) * 2 + rank) * SLOT_FLOATS);
-#pragma unroll
-      for (int g = 0; g < 8; ++g) {
-        const float4 v = __ldcg(part + (c * 8 + g) * 128 + row);
-        sum[g].x += v.x;
-        sum[g].y += v.y;
-        sum[g].z += v.z;
-        sum[g].w += v.w;
-      }
-    }
-    uint32_t lo[16], hi[16];
-#pragma unroll
-    for (int g = 0; g < 8; ++g) {
-      uint32_t* dst = g < 4 ? lo : hi;
-      const int e = (g & 3) * 4;
-      dst[e] = __float_as_uint(sum[g].x);
-      dst[e + 1] = __float_as_uint(sum[g].y);
-      dst[e + 2] = __float_as_uint(sum[g].z);
-      dst[e + 3] = __float_as_uint(sum[g].w);
-    }
-    tmem_st16(t_acc + c * 32, lo);
-    tmem_st16(t_acc + c * 32 + 16, hi);
-  }
-  tmem_wait_st();
-  return true;
-}
 static_assert(SMEM_BYTES <= 232448, "pair kernel shared memory");
 }  // namespace pair
 
@@ -686,6 +545,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   const int lane = threadIdx.x % 32;
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
+  const int num_tiles = bt.tile_start[bt.count];
   const int pair_id = blockIdx.x / 2;
   const int pairs = gridDim.x / 2;
 
@@ -722,12 +582,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
-      Unit u;
-      for (int i = 0; ok && unit_at(bt, pair_id, pairs, i, u); ++i) {
-        const Tile tl = locate(bt, u.t);
+      for (int t = pair_id; t < num_tiles && ok; t += pairs) {
+        const Tile tl = locate(bt, t);
         const CUtensorMap* ma = &maps.a[tl.p];
         const CUtensorMap* mw = &maps.b[tl.p];
-        for (int kb = u.kb0; kb < u.kb1; ++kb) {
+        const int nk = bt.prob[tl.p].nk;
+        for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&s->empty[stage], phase ^ 1u, abort)) {
             ok = false;
             break;
@@ -762,14 +622,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
-      Unit u;
-      for (int i = 0; ok && unit_at(bt, pair_id, pairs, i, u); ++i, ++it) {
+      for (int t = pair_id; t < num_tiles && ok; t += pairs, ++it) {
+        const int nk = bt.prob[locate(bt, t).p].nk;
         const int acc = it & 1;
         const uint32_t acc_phase = static_cast<uint32_t>((it >> 1) & 1);
         if (!mbar_wait_cluster(&s->tmem_empty[acc], acc_phase ^ 1u, abort)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem + static_cast<uint32_t>(acc * BN);
-        for (int kb = u.kb0; kb < u.kb1; ++kb) {
+        for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&s->full[stage], phase, abort)) {
             ok = false;
             break;
@@ -781,7 +641,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           for (int k = 0; k < BK / 16; ++k) {
             const uint64_t ad = umma_desc(a_addr + k * 32, 16, 1024, kLayoutSw128);
             const uint64_t bd = umma_desc(b_addr + k * 32, 16, 1024, kLayoutSw128);
-            umma_ss_pair(d_tmem, ad, bd, idesc, (kb != u.kb0 || k != 0) ? 1u : 0u);
+            umma_ss_pair(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
           }
           umma_commit_pair(map_to_cta(&s->empty[stage], 0));
           umma_commit_pair(map_to_cta(&s->empty[stage], 1));
@@ -806,19 +666,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     uint8_t* stage = base + pair::STAGES * pair::STAGE_BYTES + 256 + (warp - 2) * EPI_STAGE_BYTES;
     const uint32_t empty_leader = map_to_cta(&s->tmem_empty[0], 0);
     int it = 0;
-    Unit u;
-    for (int i = 0; unit_at(bt, pair_id, pairs, i, u); ++i, ++it) {
-      const Tile tl = locate(bt, u.t);
+    for (int t = pair_id; t < num_tiles; t += pairs, ++it) {
+      const Tile tl = locate(bt, t);
       const Problem& p = bt.prob[tl.p];
       const int acc = it & 1;
       const uint32_t acc_phase = static_cast<uint32_t>((it >> 1) & 1);
       if (!__all_sync(0xffffffffu, mbar_wait_cluster(&s->tmem_full[acc], acc_phase, abort))) break;
       tc_fence_after();
       const uint32_t t_base = tmem + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(quarter * 32) << 16);
-      const bool finish = u.slot < 0 || pair::split_tile_fixup(bt, u, rank, t_base, row_in_tile, &s->split_last);
-      if (finish)
-        epilogue_row(p, t_base, static_cast<int64_t>(tl.mb) * pair::BM + static_cast<int64_t>(rank) * 128 + row_in_tile,
-                     tl.nb, stage);
+      epilogue_row(p, t_base, static_cast<int64_t>(tl.mb) * pair::BM + static_cast<int64_t>(rank) * 128 + row_in_tile,
+                   tl.nb, stage);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(empty_leader + static_cast<uint32_t>(acc) * 8u);
@@ -912,81 +769,7 @@ int check_problem(const iris_gemm_problem& q) {
 
 using namespace iris;
 
-namespace iris {
-namespace gemm {
-
-// CTA pairs of the persistent pair kernel resident at once on the current
-// device (not every SM has a partner a cluster of two can use).
-int resident_pairs(int* out) {
-  static int cache[64] = {0};
-  int dev = 0;
-  IRIS_CUDA(cudaGetDevice(&dev));
-  int limit = dev < 64 ? cache[dev] : 0;
-  if (limit == 0) {
-    IRIS_CUDA(cudaFuncSetAttribute(gemm_bf16_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   static_cast<int>(pair::SMEM_BYTES)));
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(num_sms()));
-    cfg.blockDim = dim3(THREADS);
-    cfg.dynamicSmemBytes = pair::SMEM_BYTES;
-    IRIS_CUDA(cudaOccupancyMaxActiveClusters(&limit, gemm_bf16_pair_kernel, &cfg));
-    IRIS_REQUIRE(limit > 0, "iris_gemm_bf16_grouped: no CTA pair fits on this device");
-    if (dev < 64) cache[dev] = limit;
-  }
-  *out = limit;
-  return IRIS_OK;
-}
-
-// Scratch of the stream-K tail: two partial slots per pair (both CTAs' halves),
-// then one arrival counter per stream-K tile and CTA (at most 2 x pairs tiles).
-int64_t workspace_need(int pairs) {
-  return static_cast<int64_t>(pairs) * 2 * 2 * pair::SLOT_FLOATS * 4 + static_cast<int64_t>(pairs) * 2 * 2 * 8;
-}
-
-// Whether to split the last wave: only when it is poorly filled (the whole
-// tiles of a launch fill less than 98% of their waves) and a tile has at
-// least 8 K blocks. Full waves but one run whole tiles; the rest (one full
-// wave plus the remainder) is dealt out by K blocks.
-bool plan_stream_k(Batch& bt, int64_t tiles, int pairs, int nk) {
-  if (tiles <= 0 || pairs <= 1 || nk < 8) return false;
-  const int64_t full = tiles / pairs, rem = tiles % pairs;
-  if (rem == 0) return false;
-  if (full >= 1 && static_cast<double>(tiles) / static_cast<double>((full + 1) * pairs) >= 0.98) return false;
-  const int64_t dp = full >= 1 ? (full - 1) * pairs : 0;
-  const int64_t total_k = (tiles - dp) * nk;
-  int64_t per = (total_k + pairs - 1) / pairs;
-  if (per < 4) per = 4;
-  bt.dp_tiles = static_cast<int>(dp);
-  bt.sk_nk = nk;
-  bt.sk_per_pair = static_cast<int>(per);
-  bt.sk_total = static_cast<int>(total_k);
-  return true;
-}
-
-unsigned int next_epoch() {
-  static std::atomic<unsigned int> epoch{0};
-  unsigned int e = ++epoch;
-  if (e == 0) e = ++epoch;  // 0 marks a zero-filled (never used) counter
-  return e;
-}
-
-}  // namespace gemm
-}  // namespace iris
-
-extern "C" int iris_gemm_workspace_bytes(int64_t* bytes) {
-  IRIS_REQUIRE(bytes != nullptr, "iris_gemm_workspace_bytes: null output");
-  int pairs = 0;
-  IRIS_CHECK_STATUS(iris::gemm::resident_pairs(&pairs));
-  *bytes = iris::gemm::workspace_need(pairs);
-  return IRIS_OK;
-}
-
 extern "C" int iris_gemm_bf16_grouped(const iris_gemm_problem* problems, int count, void* stream) {
-  return iris_gemm_bf16_grouped_ws(problems, count, nullptr, 0, stream);
-}
-
-extern "C" int iris_gemm_bf16_grouped_ws(const iris_gemm_problem* problems, int count, void* workspace,
-                                         int64_t workspace_bytes, void* stream) {
   using namespace iris::gemm;
   IRIS_REQUIRE(problems != nullptr && count >= 1 && count <= MAX_PROBLEMS,
                "iris_gemm_bf16_grouped: 1 to 4 problems per launch");
@@ -1067,32 +850,22 @@ extern "C" int iris_gemm_bf16_grouped_ws(const iris_gemm_problem* problems, int 
     configured[dev] = true;
   }
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  bt.dp_tiles = static_cast<int>(total);
-  bt.sk_nk = 0;
-  bt.sk_per_pair = 0;
-  bt.sk_total = 0;
-  bt.partials = nullptr;
-  bt.counters = nullptr;
-  bt.epoch = 0;
   if (use_pair) {
-    // The persistent grid is the pairs resident at once: tiles of pairs left
-    // over would run as a second wave.
-    int limit = 0;
-    IRIS_CHECK_STATUS(resident_pairs(&limit));
-    int pairs = total < limit ? static_cast<int>(total) : limit;
-    int nk = bt.prob[0].nk;
-    for (int i = 1; i < count; ++i)
-      if (bt.prob[i].nk != nk) nk = 0;  // stream-K deals out uniform K blocks only
-    if (workspace != nullptr && nk > 0 && plan_stream_k(bt, total, limit, nk)) {
-      IRIS_REQUIRE(workspace_bytes >= workspace_need(limit),
-                   "iris_gemm_bf16_grouped_ws: workspace smaller than iris_gemm_workspace_bytes()");
-      IRIS_REQUIRE(aligned16(workspace), "iris_gemm_bf16_grouped_ws: workspace must be 16-byte aligned");
-      bt.partials = static_cast<float*>(workspace);
-      bt.counters = reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(workspace) +
-                                                          static_cast<int64_t>(limit) * 2 * 2 * pair::SLOT_FLOATS * 4);
-      bt.epoch = next_epoch();
-      pairs = limit;
+    // Not every SM has a partner SM that a cluster of two can use: size the
+    // persistent grid to the clusters that are resident at once, or the tiles
+    // of the clusters left over would run as a second wave.
+    static int resident_pairs[64] = {0};
+    int limit = dev < 64 ? resident_pairs[dev] : 0;
+    if (limit == 0) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(static_cast<unsigned>(num_sms()));
+      cfg.blockDim = dim3(THREADS);
+      cfg.dynamicSmemBytes = pair::SMEM_BYTES;
+      IRIS_CUDA(cudaOccupancyMaxActiveClusters(&limit, gemm_bf16_pair_kernel, &cfg));
+      IRIS_REQUIRE(limit > 0, "iris_gemm_bf16_grouped: no CTA pair fits on this device");
+      if (dev < 64) resident_pairs[dev] = limit;
     }
+    const int pairs = total < limit ? static_cast<int>(total) : limit;
     gemm_bf16_pair_kernel<<<2 * pairs, THREADS, pair::SMEM_BYTES, st>>>(maps, bt);
   } else {
     const int grid = total < num_sms() ? static_cast<int>(total) : num_sms();

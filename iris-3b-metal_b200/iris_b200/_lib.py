@@ -92,8 +92,6 @@ class ResidualProblem(ctypes.Structure):
 
 SIGNATURES["iris_gated_residual_rms_norm_grouped"] = [ctypes.POINTER(ResidualProblem), I32, I32, I32, I64, F, P]
 SIGNATURES["iris_gemm_bf16_grouped"] = [ctypes.POINTER(GemmProblem), I32, P]
-SIGNATURES["iris_gemm_bf16_grouped_ws"] = [ctypes.POINTER(GemmProblem), I32, P, I64, P]
-SIGNATURES["iris_gemm_workspace_bytes"] = [ctypes.POINTER(I64)]
 SIGNATURES["iris_flash_attn_fwd_peers"] = [P, P, P, I64, I64, I64, I64, I64, I64, F, F, P, I32, I64, I64, I64, P]
 SIGNATURES["iris_ipc_export"] = [P, P, ctypes.POINTER(I64)]
 SIGNATURES["iris_ipc_import"] = [P, ctypes.POINTER(P)]
@@ -128,7 +126,7 @@ def load() -> ctypes.CDLL:
 _launches = 0
 # kernels each entry point enqueues (1 unless listed)
 _KERNELS_PER_CALL = {"iris_device_error": 0, "iris_all_finite": 2, "iris_ipc_export": 0, "iris_ipc_import": 0,
-                     "iris_ipc_close": 0, "iris_gemm_workspace_bytes": 0}
+                     "iris_ipc_close": 0}
 
 
 def launch_count() -> int:

@@ -342,34 +342,15 @@ class PeerHeads:
             st.q_peer[j], st.k_peer[j], st.v_peer[j] = self.q[j] or None, self.k[j], self.v[j]
 
 
-_gemm_workspaces: dict = {}
-
-
-def gemm_workspace(stream: int) -> torch.Tensor:
-    """The stream-K scratch of GEMM launches on ``stream`` of the current device
-    (``iris_gemm_workspace_bytes``, zero-filled once, kept for the process):
-    launches that share a workspace must not overlap, so each stream has its own."""
-    dev = torch.cuda.current_device()
-    key = (dev, stream)
-    ws = _gemm_workspaces.get(key)
-    if ws is None:
-        nbytes = ctypes.c_int64(0)
-        _lib.call("iris_gemm_workspace_bytes", ctypes.byref(nbytes))
-        ws = _gemm_workspaces[key] = torch.zeros(nbytes.value, dtype=torch.uint8, device=f"cuda:{dev}")
-    return ws
-
-
 def gemm_grouped(problems: list, stream: int) -> None:
-    """Run 1 to 4 problems from :func:`gemm_problem` in one persistent launch
-    (with the stream-K tail when the last wave would be poorly filled)."""
+    """Run 1 to 4 problems from :func:`gemm_problem` in one persistent launch."""
     _require(1 <= len(problems) <= 4, "gemm_grouped takes 1 to 4 problems")
     array = (_lib.GemmProblem * len(problems))(*problems)
-    ws = gemm_workspace(stream)
     timing = _gemm_profile is not None
     if timing:
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record()
-    _lib.call("iris_gemm_bf16_grouped_ws", array, len(problems), ws.data_ptr(), ws.numel(), stream)
+    _lib.call("iris_gemm_bf16_grouped", array, len(problems), stream)
     if timing:
         end.record()
         _gemm_profile.append((start, end, sum(2.0 * q.M * q.N * q.K for q in problems),
