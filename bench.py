@@ -243,14 +243,15 @@ def profile_run(kind: str) -> None:
     with one dual and one single-stream block and one pixel block (< 1 GB of
     weights), for multi-pass captures. ``sampler``: the small model, and in the
     range the 4-step guided Euler loop of one image (four B = 2 calls and the
-    fused CFG + Euler updates)."""
+    fused CFG + Euler updates). ``forward16`` / ``small16``: the benchmark's
+    16-row calls (8 images x [uncond; cond]) on the full / small model."""
     from dataclasses import replace
 
     from iris_b200 import CudaIris, IrisWeights, baseline_step_config, synthetic_state
     from iris_b200.config import PixelStageConfig
 
     cfg = baseline_step_config()
-    if kind in ("small", "sampler"):
+    if kind in ("small", "sampler", "small16"):
         cfg = replace(cfg, depth=2, dual_depth=1, pixel=PixelStageConfig(depth=1))
     device = torch.device("cuda", 0)
     engine = CudaIris(IrisWeights(cfg, synthetic_state(cfg, device, seed=0)))
@@ -258,6 +259,11 @@ def profile_run(kind: str) -> None:
     x = noise[:1].repeat(2, 1, 1, 1).to(device)
     text = torch.cat([engine.encode_text(uncond_states.to(device)), engine.encode_text(cond_states[:1].to(device))])
     t = torch.full((2,), 625.0, device=device)
+    if kind in ("forward16", "small16"):  # the benchmark's calls: 8 images x [uncond; cond]
+        x = torch.cat([noise, noise]).to(device)
+        cond = engine.encode_text(cond_states.to(device))
+        text = torch.cat([engine.encode_text(uncond_states.to(device)).expand(IMAGES, -1, -1), cond]).contiguous()
+        t = torch.full((2 * IMAGES,), 1000.0, device=device)
     for _ in range(2):
         engine(x, t, text)
     torch.cuda.synchronize()
@@ -652,7 +658,8 @@ def main() -> None:
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", default="ours", choices=["ours", "reference"])
     parser.add_argument("--no-cpu-baseline", action="store_true")
-    parser.add_argument("--profile", choices=["forward", "small", "sampler"], help="NVTX-marked work for ncu")
+    parser.add_argument("--profile", choices=["forward", "small", "sampler", "forward16", "small16"],
+                        help="NVTX-marked work for ncu")  # fmt: skip
     parser.add_argument("--workload", default="loop1024", choices=["loop1024", "step2048", "ops", "attention"])
     args = parser.parse_args()
     from iris_b200.parallel import env_world, gather_images, image_shard, init_process_group  # noqa: F401
