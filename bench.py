@@ -52,11 +52,16 @@ WORKLOAD = (
 )
 
 
-# DRAM bytes (read + write) per GEMM launch of the N = 1 workload, mean over the
-# 564 launches of one step, from
+# DRAM bytes (read + write) per GEMM launch of the N = 1 workload (the 141 GEMM
+# launches of a 16-row call, 4 calls per step), from one capture of the small
+# model's 16-row call, whose 16 GEMM launches have the full model's shapes (one
+# launch of each kind: patch embed, the dual and single blocks' QKV / gate / proj /
+# w13 / w2, the pixel block's five):
 #   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum --clock-control none \
-#       -k regex:gemm_bf16 -c 564 --csv --log-file gemm_traffic.csv python bench.py --steps 1 --warmup 3 --no-cpu-baseline
-GEMM_TRAFFIC_PER_LAUNCH = 2655.8e6
+#       --nvtx --nvtx-include "profiled/" -k regex:gemm_bf16 --csv --log-file gemm_traffic_small16.csv \
+#       python bench.py --profile small16
+# weighted by the kinds' launch counts in the full model (1 + 8 x 5 + 16 x 5 + 4 x 5).
+GEMM_TRAFFIC_PER_LAUNCH = 2750.4e6
 
 
 def peaks() -> dict:
@@ -829,8 +834,8 @@ def main() -> None:
             "unit": "TFLOP/s",
             "frac": (achieved / pk["bf16_sustained"]) if achieved else None,
             "traffic": GEMM_TRAFFIC_PER_LAUNCH if world == 1 else None,
-            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, mean over the 564 GEMM launches of "
-            "one N=1 step (4 guided calls of 16 rows); units: bytes per launch",
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch of each GEMM kind of a "
+            "16-row call (small model, same shapes), weighted by the full model's launch counts; bytes per launch",
             "algorithmic_bytes_per_launch": gemm_bytes / gemm_n if gemm_n else None,
             "launches": gemm_n,
             "peak_source": f"{pk['source']} bf16 sustained",

@@ -79,23 +79,25 @@ __global__ void timestep_kernel(const float* __restrict__ t, float* __restrict__
 
 IRIS_DEVICE float silu(float v) { return v / (1.f + __expf(-v)); }
 
-// Small-M linear, HBM-bound on the weights: every weight element is read once
-// for all (up to 16) rows of x. A block of 8 warps owns 8 * COLS output
-// columns; K is walked in chunks of 256, each chunk of act_in(x) staged once in
-// shared memory for the whole block; lane l multiplies elements [8 l, 8 l + 8)
-// of the chunk, with the next chunk's weights loaded while this one computes.
-constexpr int GEMV_MT = 16;
+// Small-M linear, HBM-bound on the weights. A block of 8 warps owns 8 * COLS
+// output columns; act_in(x) of up to 8 rows (all of K) is staged once in shared
+// memory, and each lane walks K in 256-wide chunks (elements [8 l, 8 l + 8) of
+// each chunk) with four chunks of weight loads in flight, so the weight stream
+// never waits on a barrier. More than 8 rows take further passes (the benchmark's
+// 16-row calls read the 113 MB adaLN core weights twice).
+constexpr int GEMV_MT = 8;
 constexpr int GEMV_CHUNK = 256;
+constexpr int GEMV_DEPTH = 4;
 
 template <typename TW>
-IRIS_DEVICE void gemv_load8(const TW* p, bool ok, float (&v)[8]) {
-  if (!ok) {
-#pragma unroll
-    for (int e = 0; e < 8; ++e) v[e] = 0.f;
-    return;
+struct GemvVec;
+template <>
+struct GemvVec<__nv_bfloat16> {
+  uint4 u;
+  IRIS_DEVICE void load(const __nv_bfloat16* p, bool ok) {
+    u = ok ? __ldg(reinterpret_cast<const uint4*>(p)) : make_uint4(0u, 0u, 0u, 0u);
   }
-  if constexpr (sizeof(TW) == 2) {
-    const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+  IRIS_DEVICE void get(float (&v)[8]) const {
     const uint32_t ws[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
     for (int h = 0; h < 4; ++h) {
@@ -103,60 +105,75 @@ IRIS_DEVICE void gemv_load8(const TW* p, bool ok, float (&v)[8]) {
       v[2 * h] = f.x;
       v[2 * h + 1] = f.y;
     }
-  } else {
-    const float4 a = __ldg(reinterpret_cast<const float4*>(p)), b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  }
+};
+template <>
+struct GemvVec<float> {
+  float4 a, b;
+  IRIS_DEVICE void load(const float* p, bool ok) {
+    a = ok ? __ldg(reinterpret_cast<const float4*>(p)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    b = ok ? __ldg(reinterpret_cast<const float4*>(p) + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  IRIS_DEVICE void get(float (&v)[8]) const {
     v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
   }
-}
+};
 
 template <typename TW, int COLS>
 __global__ void __launch_bounds__(THREADS) gemv_kernel(const float* __restrict__ x, int M, int K,
                                                        const TW* __restrict__ w, const float* __restrict__ bias,
                                                        float* __restrict__ out, int N, int act_in, int act_out) {
-  __shared__ __align__(16) float xs[GEMV_MT][GEMV_CHUNK];
+  extern __shared__ __align__(16) float xs[];  // [GEMV_MT][K]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t n0 = (static_cast<int64_t>(blockIdx.x) * (THREADS / 32) + warp) * COLS;
   const int chunks = (K + GEMV_CHUNK - 1) / GEMV_CHUNK;
   for (int m0 = 0; m0 < M; m0 += GEMV_MT) {
     const int mt = min(GEMV_MT, M - m0);
+    __syncthreads();  // the previous pass's readers are done with xs
+    for (int e = threadIdx.x * 4; e < mt * K; e += THREADS * 4) {  // K % 8 == 0: whole float4s
+      float4 v = __ldg(reinterpret_cast<const float4*>(x + static_cast<int64_t>(m0) * K + e));
+      if (act_in) v = make_float4(silu(v.x), silu(v.y), silu(v.z), silu(v.w));
+      *reinterpret_cast<float4*>(xs + e) = v;
+    }
+    __syncthreads();
     float acc[COLS][GEMV_MT];
 #pragma unroll
     for (int c = 0; c < COLS; ++c)
 #pragma unroll
       for (int j = 0; j < GEMV_MT; ++j) acc[c][j] = 0.f;
-    float wa[COLS][8], wb[COLS][8];
-    auto load_w = [&](int chunk, float (&dst)[COLS][8]) {
+    GemvVec<TW> wq[GEMV_DEPTH][COLS];
+    auto load = [&](int chunk, GemvVec<TW> (&dst)[COLS]) {
       const int k = chunk * GEMV_CHUNK + lane * 8;
 #pragma unroll
-      for (int c = 0; c < COLS; ++c) gemv_load8(w + (n0 + c) * K + k, n0 + c < N && k < K, dst[c]);
+      for (int c = 0; c < COLS; ++c) dst[c].load(w + (n0 + c) * K + k, chunk < chunks && n0 + c < N && k < K);
     };
-    // one chunk: stage act_in(x), start the next chunk's weight loads, multiply
-    auto step = [&](int ch, const float (&cur)[COLS][8], float (&next)[COLS][8]) {
-      __syncthreads();  // the previous chunk's readers are done with xs
-      for (int e = threadIdx.x; e < mt * GEMV_CHUNK; e += THREADS) {
-        const int j = e / GEMV_CHUNK, kk = e % GEMV_CHUNK, k = ch * GEMV_CHUNK + kk;
-        const float v = k < K ? x[static_cast<int64_t>(m0 + j) * K + k] : 0.f;
-        xs[j][kk] = act_in ? silu(v) : v;
-      }
-      __syncthreads();
-      if (ch + 1 < chunks) load_w(ch + 1, next);
+    auto compute = [&](int chunk, const GemvVec<TW> (&cur)[COLS]) {
+      const int k = chunk * GEMV_CHUNK + lane * 8;
+      if (k >= K) return;
+      float wv[COLS][8];
+#pragma unroll
+      for (int c = 0; c < COLS; ++c) cur[c].get(wv[c]);
 #pragma unroll
       for (int j = 0; j < GEMV_MT; ++j) {
         if (j < mt) {
-          const float4 a = *reinterpret_cast<const float4*>(&xs[j][lane * 8]);
-          const float4 b = *reinterpret_cast<const float4*>(&xs[j][lane * 8 + 4]);
+          const float4 a = *reinterpret_cast<const float4*>(xs + j * K + k);
+          const float4 b = *reinterpret_cast<const float4*>(xs + j * K + k + 4);
           const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
           for (int c = 0; c < COLS; ++c)
 #pragma unroll
-            for (int e = 0; e < 8; ++e) acc[c][j] = fmaf(xv[e], cur[c][e], acc[c][j]);
+            for (int e = 0; e < 8; ++e) acc[c][j] = fmaf(xv[e], wv[c][e], acc[c][j]);
         }
       }
     };
-    load_w(0, wa);
-    for (int ch = 0; ch < chunks; ch += 2) {
-      step(ch, wa, wb);
-      if (ch + 1 < chunks) step(ch + 1, wb, wa);
+#pragma unroll
+    for (int d = 0; d < GEMV_DEPTH; ++d) load(d, wq[d]);
+    for (int ch = 0; ch < chunks; ch += GEMV_DEPTH) {
+#pragma unroll
+      for (int d = 0; d < GEMV_DEPTH; ++d) {
+        compute(ch + d, wq[d]);
+        load(ch + d + GEMV_DEPTH, wq[d]);
+      }
     }
 #pragma unroll
     for (int c = 0; c < COLS; ++c) {
@@ -354,16 +371,22 @@ extern "C" int iris_gemv(const float* x, int64_t M, int64_t K, const void* w, in
   const int cols = wide ? 2 : 1;
   const int64_t per_block = static_cast<int64_t>(THREADS / 32) * cols;
   const unsigned grid = static_cast<unsigned>((N + per_block - 1) / per_block);
+  const int64_t smem64 = static_cast<int64_t>(GEMV_MT) * K * 4;
+  IRIS_REQUIRE(smem64 <= 200 * 1024, "gemv: K too large for the staged rows (K <= 6400)");
+  const int smem = static_cast<int>(smem64);
   const int Mi = static_cast<int>(M), Ki = static_cast<int>(K), Ni = static_cast<int>(N);
-  if (w_dtype == IRIS_BF16) {
-    const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(w);
-    if (wide) gemv_kernel<__nv_bfloat16, 2><<<grid, THREADS, 0, st>>>(x, Mi, Ki, wb, bias, out, Ni, act_in, act_out);
-    else gemv_kernel<__nv_bfloat16, 1><<<grid, THREADS, 0, st>>>(x, Mi, Ki, wb, bias, out, Ni, act_in, act_out);
-  } else {
-    const float* wf = reinterpret_cast<const float*>(w);
-    if (wide) gemv_kernel<float, 2><<<grid, THREADS, 0, st>>>(x, Mi, Ki, wf, bias, out, Ni, act_in, act_out);
-    else gemv_kernel<float, 1><<<grid, THREADS, 0, st>>>(x, Mi, Ki, wf, bias, out, Ni, act_in, act_out);
+#define IRIS_GEMV(TW, C, WP)                                                                                         \
+  {                                                                                                                  \
+    auto kernel = gemv_kernel<TW, C>;                                                                                \
+    if (smem > 48 * 1024) IRIS_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)); \
+    kernel<<<grid, THREADS, smem, st>>>(x, Mi, Ki, reinterpret_cast<const TW*>(WP), bias, out, Ni, act_in, act_out); \
   }
+  if (w_dtype == IRIS_BF16) {
+    if (wide) IRIS_GEMV(__nv_bfloat16, 2, w) else IRIS_GEMV(__nv_bfloat16, 1, w)
+  } else {
+    if (wide) IRIS_GEMV(float, 2, w) else IRIS_GEMV(float, 1, w)
+  }
+#undef IRIS_GEMV
   IRIS_CUDA(cudaGetLastError());
   return IRIS_OK;
 }
