@@ -130,8 +130,16 @@ _KERNELS_PER_CALL = {"iris_device_error": 0, "iris_all_finite": 2, "iris_ipc_exp
 
 
 def launch_count() -> int:
-    """Kernels of this library enqueued so far by this process."""
+    """Kernels of this library enqueued so far by this process (replays of a
+    captured CUDA graph count the library kernels the graph holds)."""
     return _launches
+
+
+def count_launches(n: int) -> None:
+    """Adjust the count for kernels enqueued other than through :func:`call`
+    (a CUDA graph replay) or counted while being captured rather than run."""
+    global _launches
+    _launches += n
 
 
 def call(name: str, *args) -> None:

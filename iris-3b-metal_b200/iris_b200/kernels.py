@@ -348,13 +348,16 @@ def gemm_grouped(problems: list, stream: int) -> None:
     array = (_lib.GemmProblem * len(problems))(*problems)
     timing = _gemm_profile is not None
     if timing:
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        # inside a CUDA-graph capture the events become record nodes of the graph
+        captured = torch.cuda.is_current_stream_capturing()
+        start = torch.cuda.Event(enable_timing=True, external=captured)
+        end = torch.cuda.Event(enable_timing=True, external=captured)
         start.record()
     _lib.call("iris_gemm_bf16_grouped", array, len(problems), stream)
     if timing:
         end.record()
         _gemm_profile.append((start, end, sum(2.0 * q.M * q.N * q.K for q in problems),
-                              sum(_gemm_bytes(q) for q in problems)))  # fmt: skip
+                              sum(_gemm_bytes(q) for q in problems), captured))  # fmt: skip
 
 
 def _gemm_bytes(q) -> float:
@@ -379,16 +382,20 @@ def profile_gemms(enable: bool):
     """Start (``True``) or stop (``False``) timing every GEMM launch with CUDA
     events on its stream. Stopping synchronises and returns
     ``(algorithmic FLOPs, milliseconds, launches, algorithmic bytes)`` summed
-    over the launches."""
+    over the launches. GEMMs captured into a CUDA graph while timing is on carry
+    event-record nodes, which every replay records again: their times are those
+    of the latest replay, and when there are any, only they are summed (the
+    eager forward that precedes a capture is left out)."""
     global _gemm_profile
     if enable:
         _gemm_profile = []
         return None
     records, _gemm_profile = _gemm_profile or [], None
     torch.cuda.synchronize()
-    flops = sum(r[2] for r in records)
-    ms = sum(r[0].elapsed_time(r[1]) for r in records)
-    return flops, ms, len(records), sum(r[3] for r in records)
+    use = [r for r in records if r[4]] or records
+    flops = sum(r[2] for r in use)
+    ms = sum(r[0].elapsed_time(r[1]) for r in use)
+    return flops, ms, len(use), sum(r[3] for r in use)
 
 
 def score_bound(q_gains, k_gains, scale: float | None = None, head_dim: int = 128) -> float:
