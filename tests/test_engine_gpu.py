@@ -95,7 +95,7 @@ def test_graph_mode_matches_eager(iris):
     assert torch.equal(outs[0], outs[3])
     n0 = _lib.launch_count()
     graphed(x, t, text)
-    assert _lib.launch_count() - n0 == graphed._graphs[(tuple(x.shape), tuple(text.shape))]["kernels"] > 100
+    assert _lib.launch_count() - n0 == graphed._graphs[(tuple(x.shape), tuple(text.shape))]["kernels"] > 20
     sample_g = iris.euler_cfg(graphed, fx["euler_cfg"]["noise"].cuda(), fx["euler_cfg"]["cond"].cuda(),
                               fx["euler_cfg"]["uncond"].cuda())  # fmt: skip
     sample_e = iris.euler_cfg(eager, fx["euler_cfg"]["noise"].cuda(), fx["euler_cfg"]["cond"].cuda(),
