@@ -358,6 +358,8 @@ def gemm_grouped(problems: list, stream: int) -> None:
         end.record()
         _gemm_profile.append((start, end, sum(2.0 * q.M * q.N * q.K for q in problems),
                               sum(_gemm_bytes(q) for q in problems), captured))  # fmt: skip
+        if captured:  # the graph's record nodes address these events for as long as the graph lives
+            _graph_events.append((start, end))
 
 
 def _gemm_bytes(q) -> float:
@@ -376,6 +378,9 @@ def gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor, **kwargs) -> torch
 
 
 _gemm_profile: list | None = None
+# events recorded by nodes of captured CUDA graphs: kept for the life of the process,
+# since a graph replay records them again whether or not timing is still on
+_graph_events: list = []
 
 
 def profile_gemms(enable: bool):
