@@ -96,6 +96,17 @@ def test_graph_mode_matches_eager(iris):
     n0 = _lib.launch_count()
     graphed(x, t, text)
     assert _lib.launch_count() - n0 == graphed._graphs[(tuple(x.shape), tuple(text.shape))]["kernels"] > 20
+    # GEMM timing through a capture: the graph's event nodes time every GEMM of the
+    # latest replay, and replays after timing stops still run
+    from iris_b200 import kernels as K
+
+    timed = iris.CudaIris(weights, graphs=True)
+    K.profile_gemms(True)
+    timed(x, t, text)
+    timed(x, t, text)
+    flops, ms, launches, _ = K.profile_gemms(False)
+    assert launches > 0 and flops > 0 and ms > 0
+    assert torch.equal(timed(x, t, text), outs[0])
     sample_g = iris.euler_cfg(graphed, fx["euler_cfg"]["noise"].cuda(), fx["euler_cfg"]["cond"].cuda(),
                               fx["euler_cfg"]["uncond"].cuda())  # fmt: skip
     sample_e = iris.euler_cfg(eager, fx["euler_cfg"]["noise"].cuda(), fx["euler_cfg"]["cond"].cuda(),
