@@ -79,13 +79,13 @@ __global__ void timestep_kernel(const float* __restrict__ t, float* __restrict__
 
 IRIS_DEVICE float silu(float v) { return v / (1.f + __expf(-v)); }
 
-// Small-M linear, HBM-bound on the weights. A block of 8 warps owns 8 * COLS
-// output columns; act_in(x) of up to 8 rows (all of K) is staged once in shared
-// memory, and each lane walks K in 256-wide chunks (elements [8 l, 8 l + 8) of
-// each chunk) with four chunks of weight loads in flight, so the weight stream
-// never waits on a barrier. More than 8 rows take further passes (the benchmark's
-// 16-row calls read the 113 MB adaLN core weights twice).
-constexpr int GEMV_MT = 8;
+// Small-M linear, HBM-bound on the weights. Each warp owns COLS output columns
+// at a time and walks K in 256-wide chunks (elements [8 l, 8 l + 8) of each
+// chunk per lane). A warp's column groups (grid-stride over the columns, the
+// grid sized to the blocks resident at once) and their chunks form one stream
+// of weight loads with GEMV_DEPTH chunks in flight, so the stream runs on from
+// one group into the next. act_in(x) of MT rows (all of K) is staged once per
+// block in shared memory; more rows take further passes over the weights.
 constexpr int GEMV_CHUNK = 256;
 constexpr int GEMV_DEPTH = 4;
 
@@ -119,16 +119,20 @@ struct GemvVec<float> {
   }
 };
 
-template <typename TW, int COLS>
-__global__ void __launch_bounds__(THREADS) gemv_kernel(const float* __restrict__ x, int M, int K,
-                                                       const TW* __restrict__ w, const float* __restrict__ bias,
-                                                       float* __restrict__ out, int N, int act_in, int act_out) {
-  extern __shared__ __align__(16) float xs[];  // [GEMV_MT][K]
+template <typename TW, int COLS, int MT>
+__global__ void __launch_bounds__(THREADS, 2)
+    gemv_kernel(const float* __restrict__ x, int M, int K, const TW* __restrict__ w, const float* __restrict__ bias,
+                float* __restrict__ out, int N, int act_in, int act_out) {
+  extern __shared__ __align__(16) float xs[];  // [MT][K]
+  constexpr int WARPS = THREADS / 32;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t n0 = (static_cast<int64_t>(blockIdx.x) * (THREADS / 32) + warp) * COLS;
   const int chunks = (K + GEMV_CHUNK - 1) / GEMV_CHUNK;
-  for (int m0 = 0; m0 < M; m0 += GEMV_MT) {
-    const int mt = min(GEMV_MT, M - m0);
+  const int groups = (N + COLS - 1) / COLS;
+  const int stride = gridDim.x * WARPS;  // groups between a warp's consecutive groups
+  const int g0 = blockIdx.x * WARPS + warp;
+  const int items = g0 < groups ? ((groups - 1 - g0) / stride + 1) * chunks : 0;  // (group, chunk) pairs
+  for (int m0 = 0; m0 < M; m0 += MT) {
+    const int mt = min(MT, M - m0);
     __syncthreads();  // the previous pass's readers are done with xs
     for (int e = threadIdx.x * 4; e < mt * K; e += THREADS * 4) {  // K % 8 == 0: whole float4s
       float4 v = __ldg(reinterpret_cast<const float4*>(x + static_cast<int64_t>(m0) * K + e));
@@ -136,56 +140,71 @@ __global__ void __launch_bounds__(THREADS) gemv_kernel(const float* __restrict__
       *reinterpret_cast<float4*>(xs + e) = v;
     }
     __syncthreads();
-    float acc[COLS][GEMV_MT];
+    float acc[COLS][MT];
 #pragma unroll
     for (int c = 0; c < COLS; ++c)
 #pragma unroll
-      for (int j = 0; j < GEMV_MT; ++j) acc[c][j] = 0.f;
+      for (int j = 0; j < MT; ++j) acc[c][j] = 0.f;
     GemvVec<TW> wq[GEMV_DEPTH][COLS];
-    auto load = [&](int chunk, GemvVec<TW> (&dst)[COLS]) {
-      const int k = chunk * GEMV_CHUNK + lane * 8;
+    // the load stream's position: item, its group's first column and its chunk
+    int l_item = 0, l_n0 = g0 * COLS, l_chunk = 0;
+    auto load = [&](GemvVec<TW> (&dst)[COLS]) {
+      const int k = l_chunk * GEMV_CHUNK + lane * 8;
 #pragma unroll
-      for (int c = 0; c < COLS; ++c) dst[c].load(w + (n0 + c) * K + k, chunk < chunks && n0 + c < N && k < K);
-    };
-    auto compute = [&](int chunk, const GemvVec<TW> (&cur)[COLS]) {
-      const int k = chunk * GEMV_CHUNK + lane * 8;
-      if (k >= K) return;
-      float wv[COLS][8];
-#pragma unroll
-      for (int c = 0; c < COLS; ++c) cur[c].get(wv[c]);
-#pragma unroll
-      for (int j = 0; j < GEMV_MT; ++j) {
-        if (j < mt) {
-          const float4 a = *reinterpret_cast<const float4*>(xs + j * K + k);
-          const float4 b = *reinterpret_cast<const float4*>(xs + j * K + k + 4);
-          const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-          for (int c = 0; c < COLS; ++c)
-#pragma unroll
-            for (int e = 0; e < 8; ++e) acc[c][j] = fmaf(xv[e], wv[c][e], acc[c][j]);
-        }
+      for (int c = 0; c < COLS; ++c)
+        dst[c].load(w + static_cast<int64_t>(l_n0 + c) * K + k, l_item < items && l_n0 + c < N && k < K);
+      ++l_item;
+      if (++l_chunk == chunks) {
+        l_chunk = 0;
+        l_n0 += stride * COLS;
       }
     };
 #pragma unroll
-    for (int d = 0; d < GEMV_DEPTH; ++d) load(d, wq[d]);
-    for (int ch = 0; ch < chunks; ch += GEMV_DEPTH) {
+    for (int d = 0; d < GEMV_DEPTH; ++d) load(wq[d]);
+    // the compute stream's position
+    int c_n0 = g0 * COLS, c_chunk = 0;
+    for (int it = 0; it < items; it += GEMV_DEPTH) {
 #pragma unroll
       for (int d = 0; d < GEMV_DEPTH; ++d) {
-        compute(ch + d, wq[d]);
-        load(ch + d + GEMV_DEPTH, wq[d]);
-      }
-    }
+        if (it + d < items) {  // warp-uniform
+          const int k = c_chunk * GEMV_CHUNK + lane * 8;
+          if (k < K) {
+            float wv[COLS][8];
 #pragma unroll
-    for (int c = 0; c < COLS; ++c) {
+            for (int c = 0; c < COLS; ++c) wq[d][c].get(wv[c]);
 #pragma unroll
-      for (int j = 0; j < GEMV_MT; ++j) {
-        if (j < mt) {
-          const float sum = warp_sum(acc[c][j]);
-          if (lane == 0 && n0 + c < N) {
-            const float r = sum + (bias ? bias[n0 + c] : 0.f);
-            out[static_cast<int64_t>(m0 + j) * N + n0 + c] = act_out ? silu(r) : r;
+            for (int j = 0; j < MT; ++j) {
+              if (j < mt) {
+                const float4 a = *reinterpret_cast<const float4*>(xs + j * K + k);
+                const float4 b = *reinterpret_cast<const float4*>(xs + j * K + k + 4);
+                const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+                for (int c = 0; c < COLS; ++c)
+#pragma unroll
+                  for (int e = 0; e < 8; ++e) acc[c][j] = fmaf(xv[e], wv[c][e], acc[c][j]);
+              }
+            }
+          }
+          if (++c_chunk == chunks) {  // the group's columns are complete
+#pragma unroll
+            for (int c = 0; c < COLS; ++c) {
+#pragma unroll
+              for (int j = 0; j < MT; ++j) {
+                if (j < mt) {
+                  const float sum = warp_sum(acc[c][j]);
+                  if (lane == 0 && c_n0 + c < N) {
+                    const float r = sum + (bias ? bias[c_n0 + c] : 0.f);
+                    out[static_cast<int64_t>(m0 + j) * N + c_n0 + c] = act_out ? silu(r) : r;
+                  }
+                }
+                acc[c][j] = 0.f;
+              }
+            }
+            c_chunk = 0;
+            c_n0 += stride * COLS;
           }
         }
+        load(wq[d]);
       }
     }
   }
@@ -366,26 +385,40 @@ extern "C" int iris_gemv(const float* x, int64_t M, int64_t K, const void* w, in
   IRIS_REQUIRE(w_dtype == IRIS_F32 || w_dtype == IRIS_BF16, "gemv: weights must be f32 or bf16");
   IRIS_REQUIRE(aligned16(x) && aligned16(w), "gemv: pointers must be 16-byte aligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // two columns per warp when that still gives every SM a few blocks, else one
+  // two columns per warp when every warp of a full grid still gets a few groups
   const bool wide = N >= static_cast<int64_t>(num_sms()) * 4 * (THREADS / 32) * 2;
-  const int cols = wide ? 2 : 1;
-  const int64_t per_block = static_cast<int64_t>(THREADS / 32) * cols;
-  const unsigned grid = static_cast<unsigned>((N + per_block - 1) / per_block);
-  const int64_t smem64 = static_cast<int64_t>(GEMV_MT) * K * 4;
+  // rows staged per pass: 2, 4 or 8 (more rows take further passes)
+  const int mt = M <= 2 ? 2 : (M <= 4 ? 4 : 8);
+  const int64_t smem64 = static_cast<int64_t>(mt) * K * 4;
   IRIS_REQUIRE(smem64 <= 200 * 1024, "gemv: K too large for the staged rows (K <= 6400)");
   const int smem = static_cast<int>(smem64);
   const int Mi = static_cast<int>(M), Ki = static_cast<int>(K), Ni = static_cast<int>(N);
-#define IRIS_GEMV(TW, C, WP)                                                                                         \
+  const int64_t per_block = static_cast<int64_t>(THREADS / 32) * (wide ? 2 : 1);
+  const int64_t needed = (N + per_block - 1) / per_block;
+  // the grid: the blocks resident at once (each warp then streams several
+  // column groups), or fewer when there are not that many groups
+#define IRIS_GEMV(TW, C, R)                                                                                          \
   {                                                                                                                  \
-    auto kernel = gemv_kernel<TW, C>;                                                                                \
+    auto kernel = gemv_kernel<TW, C, R>;                                                                             \
     if (smem > 48 * 1024) IRIS_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)); \
-    kernel<<<grid, THREADS, smem, st>>>(x, Mi, Ki, reinterpret_cast<const TW*>(WP), bias, out, Ni, act_in, act_out); \
+    int resident = 0;                                                                                                \
+    IRIS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, kernel, THREADS, smem));                      \
+    const int64_t cap = static_cast<int64_t>(num_sms()) * (resident > 0 ? resident : 1);                             \
+    const unsigned grid = static_cast<unsigned>(needed < cap ? needed : cap);                                        \
+    kernel<<<grid, THREADS, smem, st>>>(x, Mi, Ki, reinterpret_cast<const TW*>(w), bias, out, Ni, act_in, act_out);  \
+  }
+#define IRIS_GEMV_ROWS(TW, C)             \
+  {                                       \
+    if (mt == 2) IRIS_GEMV(TW, C, 2)      \
+    else if (mt == 4) IRIS_GEMV(TW, C, 4) \
+    else IRIS_GEMV(TW, C, 8)              \
   }
   if (w_dtype == IRIS_BF16) {
-    if (wide) IRIS_GEMV(__nv_bfloat16, 2, w) else IRIS_GEMV(__nv_bfloat16, 1, w)
+    if (wide) IRIS_GEMV_ROWS(__nv_bfloat16, 2) else IRIS_GEMV_ROWS(__nv_bfloat16, 1)
   } else {
-    if (wide) IRIS_GEMV(float, 2, w) else IRIS_GEMV(float, 1, w)
+    if (wide) IRIS_GEMV_ROWS(float, 2) else IRIS_GEMV_ROWS(float, 1)
   }
+#undef IRIS_GEMV_ROWS
 #undef IRIS_GEMV
   IRIS_CUDA(cudaGetLastError());
   return IRIS_OK;
