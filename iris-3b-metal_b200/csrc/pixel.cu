@@ -67,7 +67,23 @@ IRIS_DEVICE float inv_rms16(const float (&x)[C], float eps) {
   return rsqrtf(ss / C + eps);
 }
 
-IRIS_DEVICE float gelu_erf(float a) { return 0.5f * a * (1.f + erff(a * 0.70710678118654752f)); }
+// GELU(a) = a Phi(a) (the exact, erf form) with erf from Abramowitz & Stegun
+// 7.1.26 (|error| <= 1.5e-7 in erf): for x = |a| / sqrt(2),
+// 1 - erf(x) = t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-x^2), t = 1 / (1 + p x),
+// and Phi(a) = 1 - q for a >= 0, q for a < 0, with q = (1 - erf(x)) / 2. One
+// reciprocal and one exponential on the MUFU, the rest on the FMA pipe: about
+// half the instructions of erff, whose results it matches to about 1e-6
+// relative (the bf16 roundings downstream flip in rare ties only).
+IRIS_DEVICE float gelu_erf(float a) {
+  const float x = fabsf(a) * 0.70710678118654752f;
+  const float t = __fdividef(1.f, fmaf(0.3275911f, x, 1.f));
+  float poly = fmaf(t, 1.061405429f, -1.453152027f);
+  poly = fmaf(t, poly, 1.421413741f);
+  poly = fmaf(t, poly, -0.284496736f);
+  poly = fmaf(t, poly, 0.254829592f);
+  const float q = 0.5f * t * poly * __expf(-x * x);
+  return a * (a >= 0.f ? 1.f - q : q);
+}
 
 struct MlpWeights {
   float w1[HID * C];  // [64, 16]
@@ -147,8 +163,11 @@ IRIS_DEVICE void pit_tail(float (&x)[C], const float (&attn)[C], const __nv_bflo
 // (16 -> 64 -> 16) runs as mma.sync m16n8k16 BF16 -> FP32 (8 MMAs each way);
 // fc1's accumulator fragments are, after bias + GELU, exactly fc2's A
 // fragments. Every per-pixel elementwise step happens in the fragment layout:
-// lane = 4 g + c holds pixels g and g + 8 of the tile, channels
-// {2c, 2c+1, 2c+8, 2c+9}; 16-channel sums reduce over the lane quad.
+// lane = 4 g + c holds pixels g and g + 8 of the tile and its fragment slots
+// j = 0..3. The MMAs' channel axis (fc1's k, fc2's n) is permuted so that slot
+// j is channel 4c + j: a lane's four channels of a pixel are contiguous, one
+// 8-byte (bf16) or 16-byte (fp32) access each, and a warp's access covers
+// whole sectors. 16-channel sums reduce over the lane quad.
 IRIS_DEVICE void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
@@ -165,27 +184,42 @@ IRIS_DEVICE float quad_sum(float v) {
 
 IRIS_DEVICE uint32_t ld_bf16x2(const __nv_bfloat16* p) { return *reinterpret_cast<const uint32_t*>(p); }
 
-// channel of slot j (0..3) for lane quad position c
-IRIS_DEVICE int frag_channel(int c, int j) { return 2 * c + (j & 1) + ((j >> 1) << 3); }
+// the channel behind the MMAs' logical channel index k (0..15): the lane quad
+// position c = (k % 8) / 2 and slot j = k % 2 + 2 (k / 8) hold channel 4c + j
+IRIS_DEVICE int frag_channel(int k) { return 4 * ((k & 7) >> 1) + (k & 1) + 2 * (k >> 3); }
 
-// A tile's inputs for this lane (fragment layout: pixels g and g + 8, channel
-// pairs (2c, 2c+1) and (2c+8, 2c+9)): the pixels, the attention branch and the
-// four modulation pairs (scale1, shift1, scale2, shift2).
+// A tile's inputs for this lane (fragment layout: pixels g and g + 8, channels
+// 4c .. 4c + 3): the pixels, the attention branch and the four modulation
+// vectors (scale1, shift1, scale2, shift2), as bf16 pairs (slots 0-1, 2-3).
 struct TileIn {
   float p[2][4];
   uint32_t at[2][2];
-  uint32_t m[2][4][2];  // [half][scale1, shift1, scale2, shift2][channel pair]
+  uint32_t m[2][4][2];  // [half][scale1, shift1, scale2, shift2][slot pair]
 };
 
 constexpr int MMA_THREADS = 128;  // 4 warps per block
-// Resident blocks per SM: the intermediate blocks keep two tiles in flight per
-// warp (2 blocks / SM; with 3 the 168-register cap spills and 2.1 M pixels take
-// 235 us against 215); the head (FinalLayer + fold, whose tail per tile is
-// longer) takes one tile at a time at 4 blocks / SM.
-__host__ __device__ constexpr int mma_blocks_per_sm(bool head) { return head ? 4 : 2; }
+// Each warp streams its tiles' inputs through a ring of MMA_RING shared-memory
+// slots with cp.async (16-byte pieces, whole sectors), so MMA_RING - 1 tiles'
+// loads are in flight while one computes, without holding registers. A slot:
+// the tile's pixels (fp32 or bf16), its attention branch, and its modulation
+// rows padded to 144 bytes (conflict-free 8-byte reads by the fragment layout).
+constexpr int MMA_RING = 4;
+constexpr int MOD_ROW_BYTES = 4 * C * 2 + 16;
+__host__ __device__ constexpr int mma_slot_bytes(bool f32) { return 16 * C * (f32 ? 4 : 2) + 16 * C * 2 + 16 * MOD_ROW_BYTES; }
+__host__ __device__ constexpr int mma_smem_bytes(bool f32) { return (MMA_THREADS / 32) * MMA_RING * mma_slot_bytes(f32); }
+constexpr int MMA_BLOCKS_PER_SM = 3;  // 168 registers a thread
+
+IRIS_DEVICE void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(smem)), "l"(gmem) : "memory");
+}
+IRIS_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+IRIS_DEVICE void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 
 template <bool F32, bool HEAD>
-__global__ void __launch_bounds__(MMA_THREADS, mma_blocks_per_sm(HEAD)) pixel_mlp_mma_kernel(
+__global__ void __launch_bounds__(MMA_THREADS, MMA_BLOCKS_PER_SM) pixel_mlp_mma_kernel(
     void* pixels, const __nv_bfloat16* __restrict__ branch, const __nv_bfloat16* __restrict__ mods,
     const float* __restrict__ nw, const __nv_bfloat16* __restrict__ w1, const __nv_bfloat16* __restrict__ b1,
     const __nv_bfloat16* __restrict__ w2, const __nv_bfloat16* __restrict__ b2, const float* __restrict__ nnw,
@@ -199,16 +233,16 @@ __global__ void __launch_bounds__(MMA_THREADS, mma_blocks_per_sm(HEAD)) pixel_ml
   // B fragments of W1^T (k = in channel, n = hidden) and W2^T (k = hidden, n = out channel)
   uint32_t bw1[8][2], bw2[4][2][2];
 #pragma unroll
-  for (int nt = 0; nt < 8; ++nt) {
+  for (int nt = 0; nt < 8; ++nt) {  // logical k (2c, 2c+1) and (2c+8, 2c+9) = channels 4c .. 4c + 3
     const __nv_bfloat16* row = w1 + (nt * 8 + g) * C;
-    bw1[nt][0] = ld_bf16x2(row + 2 * c);
-    bw1[nt][1] = ld_bf16x2(row + 2 * c + 8);
+    bw1[nt][0] = ld_bf16x2(row + 4 * c);
+    bw1[nt][1] = ld_bf16x2(row + 4 * c + 2);
   }
 #pragma unroll
   for (int ks = 0; ks < 4; ++ks)
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
-      const __nv_bfloat16* row = w2 + (nt * 8 + g) * HID + ks * 16;
+      const __nv_bfloat16* row = w2 + frag_channel(nt * 8 + g) * HID + ks * 16;  // logical output n
       bw2[ks][nt][0] = ld_bf16x2(row + 2 * c);
       bw2[ks][nt][1] = ld_bf16x2(row + 2 * c + 8);
     }
@@ -220,7 +254,7 @@ __global__ void __launch_bounds__(MMA_THREADS, mma_blocks_per_sm(HEAD)) pixel_ml
   }
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    const int ch = frag_channel(c, j);
+    const int ch = 4 * c + j;
     bias2[j] = __bfloat162float(b2[ch]);
     gain[j] = nw[ch];
     gain_next[j] = nnw[ch];
@@ -230,27 +264,52 @@ __global__ void __launch_bounds__(MMA_THREADS, mma_blocks_per_sm(HEAD)) pixel_ml
   const int64_t tiles = n / 16;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
 
-  // every load of a tile is issued at once (the next tile's while this one computes)
-  auto load_tile = [&](int64_t tile, TileIn& in) {
+  // this warp's ring of tile slots
+  extern __shared__ __align__(16) uint8_t pix_smem[];
+  uint8_t* ring = pix_smem + (threadIdx.x >> 5) * MMA_RING * mma_slot_bytes(F32);
+  constexpr int PIX_BYTES = 16 * C * (F32 ? 4 : 2);
+  // the tile's inputs into slot `slot`: pixels, branch, modulation (three
+  // contiguous runs of global memory), 16-byte pieces spread over the lanes
+  auto issue_tile = [&](int64_t tile, int slot) {
+    uint8_t* dst = ring + slot * mma_slot_bytes(F32);
+    const uint8_t* px_src = reinterpret_cast<const uint8_t*>(pixels) + tile * PIX_BYTES;
+    const uint8_t* br_src = reinterpret_cast<const uint8_t*>(branch + tile * 16 * C);
+    const uint8_t* md_src = reinterpret_cast<const uint8_t*>(mods + tile * 16 * 4 * C);
+#pragma unroll
+    for (int e = lane; e < PIX_BYTES / 16; e += 32) cp_async16(dst + e * 16, px_src + e * 16);
+    cp_async16(dst + PIX_BYTES + lane * 16, br_src + lane * 16);  // 512 bytes: one piece per lane
+#pragma unroll
+    for (int e = lane; e < 16 * 8; e += 32)  // 16 pixels x 8 pieces of 16 bytes
+      cp_async16(dst + PIX_BYTES + 512 + (e >> 3) * MOD_ROW_BYTES + (e & 7) * 16, md_src + e * 16);
+  };
+  // this lane's fragment of the tile in `slot` (pixels g and g + 8, channels 4c .. 4c + 3)
+  auto read_tile = [&](int slot, TileIn& in) {
+    const uint8_t* src = ring + slot * mma_slot_bytes(F32);
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
-      const int64_t px = tile * 16 + g + 8 * half;
-      const __nv_bfloat16* md = mods + px * 4 * C;
+      const int px = g + 8 * half;
+      if (F32) {
+        const float4 pv = *reinterpret_cast<const float4*>(src + (px * C + 4 * c) * 4);
+        in.p[half][0] = pv.x;
+        in.p[half][1] = pv.y;
+        in.p[half][2] = pv.z;
+        in.p[half][3] = pv.w;
+      } else {
+        const uint2 pv = *reinterpret_cast<const uint2*>(src + (px * C + 4 * c) * 2);
+        const float2 lo = unpack_bf16x2(pv.x), hi = unpack_bf16x2(pv.y);
+        in.p[half][0] = lo.x;
+        in.p[half][1] = lo.y;
+        in.p[half][2] = hi.x;
+        in.p[half][3] = hi.y;
+      }
+      const uint2 at = *reinterpret_cast<const uint2*>(src + PIX_BYTES + (px * C + 4 * c) * 2);
+      in.at[half][0] = at.x;
+      in.at[half][1] = at.y;
 #pragma unroll
-      for (int jj = 0; jj < 2; ++jj) {
-        const int ch = 2 * c + 8 * jj;
-        if (F32) {
-          const float2 pv = *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(pixels) + px * C + ch);
-          in.p[half][2 * jj] = pv.x;
-          in.p[half][2 * jj + 1] = pv.y;
-        } else {
-          const float2 pv = unpack_bf16x2(ld_bf16x2(reinterpret_cast<const __nv_bfloat16*>(pixels) + px * C + ch));
-          in.p[half][2 * jj] = pv.x;
-          in.p[half][2 * jj + 1] = pv.y;
-        }
-        in.at[half][jj] = ld_bf16x2(branch + px * C + ch);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) in.m[half][k][jj] = ld_bf16x2(md + k * C + ch);
+      for (int k = 0; k < 4; ++k) {
+        const uint2 mv = *reinterpret_cast<const uint2*>(src + PIX_BYTES + 512 + px * MOD_ROW_BYTES + (k * C + 4 * c) * 2);
+        in.m[half][k][0] = mv.x;
+        in.m[half][k][1] = mv.y;
       }
     }
   };
@@ -260,7 +319,7 @@ __global__ void __launch_bounds__(MMA_THREADS, mma_blocks_per_sm(HEAD)) pixel_ml
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
 #pragma unroll
-      for (int jj = 0; jj < 2; ++jj) {  // channel pairs (2c, 2c+1) and (2c+8, 2c+9)
+      for (int jj = 0; jj < 2; ++jj) {  // slot pairs (0, 1) and (2, 3): channels 4c + 2jj, + 1
         const float2 at = unpack_bf16x2(in.at[half][jj]);
         const float2 s1 = unpack_bf16x2(in.m[half][0][jj]);
         const float2 t1 = unpack_bf16x2(in.m[half][1][jj]);
@@ -295,7 +354,7 @@ __global__ void __launch_bounds__(MMA_THREADS, mma_blocks_per_sm(HEAD)) pixel_ml
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks) mma_bf16_16816(acc, ga[ks], bw2[ks][nt][0], bw2[ks][nt][1]);
-      // acc: (g, 8nt + 2c), (g, 8nt + 2c + 1), (g + 8, ...) -> slots 2nt, 2nt + 1
+      // acc: logical outputs (g, 8nt + 2c + e) and (g + 8, ...) = channel 4c + 2nt + e -> slot 2nt + e
       out[0][2 * nt] = acc[0];
       out[0][2 * nt + 1] = acc[1];
       out[1][2 * nt] = acc[2];
@@ -317,25 +376,23 @@ __global__ void __launch_bounds__(MMA_THREADS, mma_blocks_per_sm(HEAD)) pixel_ml
       for (int j = 0; j < 4; ++j) ss += x[half][j] * x[half][j];
       const float inv = rsqrtf(quad_sum(ss) / C + eps);
       if (!HEAD) {
-#pragma unroll
-        for (int jj = 0; jj < 2; ++jj) {
-          const int ch = 2 * c + 8 * jj;
-          if (F32) {
-            *reinterpret_cast<float2*>(reinterpret_cast<float*>(pixels) + px * C + ch) =
-                make_float2(x[half][2 * jj], x[half][2 * jj + 1]);
-          } else {
-            *reinterpret_cast<uint32_t*>(reinterpret_cast<__nv_bfloat16*>(pixels) + px * C + ch) =
-                pack_bf16x2(x[half][2 * jj], x[half][2 * jj + 1]);
-          }
-          *reinterpret_cast<uint32_t*>(next_input + px * C + ch) =
-              pack_bf16x2(x[half][2 * jj] * inv * gain_next[2 * jj], x[half][2 * jj + 1] * inv * gain_next[2 * jj + 1]);
+        const int ch = 4 * c;
+        if (F32) {
+          *reinterpret_cast<float4*>(reinterpret_cast<float*>(pixels) + px * C + ch) =
+              make_float4(x[half][0], x[half][1], x[half][2], x[half][3]);
+        } else {
+          *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(pixels) + px * C + ch) =
+              make_uint2(pack_bf16x2(x[half][0], x[half][1]), pack_bf16x2(x[half][2], x[half][3]));
         }
+        *reinterpret_cast<uint2*>(next_input + px * C + ch) =
+            make_uint2(pack_bf16x2(x[half][0] * inv * gain_next[0], x[half][1] * inv * gain_next[1]),
+                       pack_bf16x2(x[half][2] * inv * gain_next[2], x[half][3] * inv * gain_next[3]));
       } else {
         float part[3] = {0.f, 0.f, 0.f};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const float hn = F32 ? x[half][j] * inv * gain_next[j] : round_bf16(x[half][j] * inv * gain_next[j]);
-          const int ch = frag_channel(c, j);
+          const int ch = 4 * c + j;
 #pragma unroll
           for (int o = 0; o < 3; ++o) part[o] = fmaf(hn, __ldg(fw + o * C + ch), part[o]);
         }
@@ -353,28 +410,26 @@ __global__ void __launch_bounds__(MMA_THREADS, mma_blocks_per_sm(HEAD)) pixel_ml
     }
   };
 
-  int64_t tile = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
-  TileIn ta, tb;
-  if constexpr (HEAD) {  // one tile at a time, its loads issued together
-    for (; tile < tiles; tile += warps) {
-      load_tile(tile, ta);
-      process(tile, ta);
-    }
-    return;
+  // this warp's tiles: first, first + warps, ...; MMA_RING - 1 of them in flight ahead
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int64_t count = first < tiles ? (tiles - 1 - first) / warps + 1 : 0;
+#pragma unroll
+  for (int s = 0; s < MMA_RING - 1; ++s) {
+    if (s < count) issue_tile(first + s * warps, s);
+    cp_async_commit();  // one group per tile, empty past the last, so the wait counts stay fixed
   }
-  // two tiles in flight per warp: buffers A and B alternate
-  if (tile < tiles) load_tile(tile, ta);
-  while (tile < tiles) {
-    const int64_t t1 = tile + warps;
-    if (t1 < tiles) load_tile(t1, tb);
-    process(tile, ta);
-    tile = t1;
-    if (tile >= tiles) break;
-    const int64_t t2 = tile + warps;
-    if (t2 < tiles) load_tile(t2, ta);
-    process(tile, tb);
-    tile = t2;
+  for (int64_t i = 0; i < count; ++i) {
+    __syncwarp();  // every lane is done reading the slot refilled next
+    const int64_t ahead = i + MMA_RING - 1;
+    if (ahead < count) issue_tile(first + ahead * warps, static_cast<int>(ahead % MMA_RING));
+    cp_async_commit();
+    cp_async_wait<MMA_RING - 1>();  // tile i's group has landed for this lane
+    __syncwarp();                   // and for every lane
+    TileIn in;
+    read_tile(static_cast<int>(i % MMA_RING), in);
+    process(first + i * warps, in);
   }
+  cp_async_wait<0>();
 }
 
 __global__ void __launch_bounds__(THREADS) pixel_rms_norm_kernel(const void* pixels, bool f32,
@@ -520,10 +575,10 @@ inline unsigned grid_for(int64_t n) {
 }
 
 // 16-pixel tiles, one per warp, 4 warps per block, grid-stride beyond the
-// resident blocks (mma_blocks_per_sm)
-inline unsigned mma_grid_for(int64_t n, bool head) {
+// resident blocks (MMA_BLOCKS_PER_SM)
+inline unsigned mma_grid_for(int64_t n) {
   const int64_t blocks = (n / 16 + MMA_THREADS / 32 - 1) / (MMA_THREADS / 32);
-  const int64_t cap = static_cast<int64_t>(num_sms()) * mma_blocks_per_sm(head);
+  const int64_t cap = static_cast<int64_t>(num_sms()) * MMA_BLOCKS_PER_SM;
   return static_cast<unsigned>(blocks < cap ? blocks : cap);
 }
 
@@ -566,16 +621,21 @@ extern "C" int iris_pixel_mlp(void* pixels, int pixel_dtype, const void* branch,
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   auto bf = [](const void* p) { return reinterpret_cast<const __nv_bfloat16*>(p); };
   if (n_pixels % 16 == 0) {  // whole 16-pixel tiles: tensor-core MLP
-    const unsigned grid = mma_grid_for(n_pixels, false);
+    const unsigned grid = mma_grid_for(n_pixels);
     auto nxt = reinterpret_cast<__nv_bfloat16*>(next_input);
-    if (pixel_dtype == IRIS_F32)
-      pixel_mlp_mma_kernel<true, false><<<grid, MMA_THREADS, 0, st>>>(
+    if (pixel_dtype == IRIS_F32) {
+      IRIS_CUDA(cudaFuncSetAttribute(pixel_mlp_mma_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     mma_smem_bytes(true)));
+      pixel_mlp_mma_kernel<true, false><<<grid, MMA_THREADS, mma_smem_bytes(true), st>>>(
           pixels, bf(branch), bf(mods), norm_weight, bf(fc1_w), bf(fc1_b), bf(fc2_w), bf(fc2_b), next_norm_weight,
           nxt, nullptr, nullptr, nullptr, n_pixels, 16, 16, 16, 0, 1, eps);
-    else
-      pixel_mlp_mma_kernel<false, false><<<grid, MMA_THREADS, 0, st>>>(
+    } else {
+      IRIS_CUDA(cudaFuncSetAttribute(pixel_mlp_mma_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     mma_smem_bytes(false)));
+      pixel_mlp_mma_kernel<false, false><<<grid, MMA_THREADS, mma_smem_bytes(false), st>>>(
           pixels, bf(branch), bf(mods), norm_weight, bf(fc1_w), bf(fc1_b), bf(fc2_w), bf(fc2_b), next_norm_weight,
           nxt, nullptr, nullptr, nullptr, n_pixels, 16, 16, 16, 0, 1, eps);
+    }
     IRIS_CUDA(cudaGetLastError());
     return IRIS_OK;
   }
@@ -609,16 +669,21 @@ extern "C" int iris_pixel_mlp_head(void* pixels, int pixel_dtype, const void* br
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   auto bf = [](const void* p) { return reinterpret_cast<const __nv_bfloat16*>(p); };
   if (n % 16 == 0) {  // whole 16-pixel tiles: tensor-core MLP
-    const unsigned grid = mma_grid_for(n, true);
+    const unsigned grid = mma_grid_for(n);
     const int pt = static_cast<int>(patch);
-    if (pixel_dtype == IRIS_F32)
-      pixel_mlp_mma_kernel<true, true><<<grid, MMA_THREADS, 0, st>>>(
+    if (pixel_dtype == IRIS_F32) {
+      IRIS_CUDA(cudaFuncSetAttribute(pixel_mlp_mma_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     mma_smem_bytes(true)));
+      pixel_mlp_mma_kernel<true, true><<<grid, MMA_THREADS, mma_smem_bytes(true), st>>>(
           pixels, bf(branch), bf(mods), norm_weight, bf(fc1_w), bf(fc1_b), bf(fc2_w), bf(fc2_b), final_norm_weight,
           nullptr, final_w, final_b, v, n, height, width, pt, token_start, tokens, eps);
-    else
-      pixel_mlp_mma_kernel<false, true><<<grid, MMA_THREADS, 0, st>>>(
+    } else {
+      IRIS_CUDA(cudaFuncSetAttribute(pixel_mlp_mma_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     mma_smem_bytes(false)));
+      pixel_mlp_mma_kernel<false, true><<<grid, MMA_THREADS, mma_smem_bytes(false), st>>>(
           pixels, bf(branch), bf(mods), norm_weight, bf(fc1_w), bf(fc1_b), bf(fc2_w), bf(fc2_b), final_norm_weight,
           nullptr, final_w, final_b, v, n, height, width, pt, token_start, tokens, eps);
+    }
     IRIS_CUDA(cudaGetLastError());
     return IRIS_OK;
   }
