@@ -126,6 +126,52 @@ def test_pixel_kernels_match_reference(K, pixel_dtype):
     torch.testing.assert_close(rms.float().cpu(), m["rms"].float(), rtol=1e-2, atol=1e-2)
 
 
+def test_pixel_mlp_gelu_matches_cuda_erf(K):
+    """The pixel tail's GELU takes erf from Abramowitz & Stegun 7.1.26 (error
+    <= 1.5e-7) instead of CUDA's erff. Against the same tail in torch on the GPU
+    (its exact GELU is erff's), with the kernel's roundings (bf16 MMA inputs,
+    fp32 sums): almost every output agrees to fp32 summation order, and the rest
+    differ by a bf16 rounding of a GELU value at a tie (2.1 M pixels)."""
+    gen = torch.Generator(device="cuda").manual_seed(29)
+    n = 2 * 4096 * 256
+    pixels = torch.randn(n, 16, device="cuda", generator=gen)
+    branch = torch.randn(n, 16, device="cuda", generator=gen).to(torch.bfloat16)
+    mods = (0.3 * torch.randn(n, 64, device="cuda", generator=gen)).to(torch.bfloat16)
+    gain = torch.rand(16, device="cuda", generator=gen) + 0.5
+    gain_next = torch.rand(16, device="cuda", generator=gen) + 0.5
+
+    class Lin:
+        def __init__(self, o, i):
+            self.weight = (0.3 * torch.randn(o, i, device="cuda", generator=gen)).to(torch.bfloat16)
+            self.bias = (0.1 * torch.randn(o, device="cuda", generator=gen)).to(torch.bfloat16)
+
+    fc1, fc2 = Lin(64, 16), Lin(16, 64)
+    eps = 1e-6
+    # the tail in torch, rounding where the kernel does
+    bf = lambda t: t.to(torch.bfloat16).float()  # noqa: E731
+    s1, t1, s2, t2 = mods.float().view(n, 4, 16).unbind(1)
+    x = pixels + (branch.float() * (1 + s1) + t1)
+    h = bf(x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * gain)
+    tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        a = h @ fc1.weight.float().T + fc1.bias.float()
+        g = bf(F.gelu(a))
+        out = g @ fc2.weight.float().T + fc2.bias.float()
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = tf32
+    want = x + (out * (1 + s2) + t2)
+    got = pixels.clone()
+    K.pixel_mlp_(got, branch, mods, gain, fc1, fc2, gain_next, eps)
+    diff = (got - want).abs()
+    close = diff <= 1e-4 * want.abs().clamp_min(1.0)
+    print(f"pixel GELU vs erff: {int((~close).sum())} of {diff.numel()} beyond fp32 order, max diff {diff.max():.3e}")
+    assert close.float().mean() > 0.999
+    # a flipped bf16 rounding of one GELU value moves an output by at most 2^-8 |g| |w2| (1 + |s2|)
+    bound = 2.0**-8 * g.abs().amax() * fc2.weight.float().abs().amax() * (1 + s2.abs().amax()) * 4
+    assert float(diff.max()) <= float(bound)
+
+
 def test_pixel_kernels_reject_short_parameter_buffers(K):
     pixels = torch.zeros(1, 1, 16, device="cuda", dtype=torch.bfloat16)
     gain = torch.ones(16, device="cuda")
