@@ -314,7 +314,28 @@ __global__ void __launch_bounds__(MMA_THREADS, MMA_BLOCKS_PER_SM) pixel_mlp_mma_
     }
   };
 
+  // where the head's tile lands in v: all 16 pixels lie in one patch (patch^2 % 16 == 0),
+  // so the patch's position is worked out once per tile
+  struct Fold {
+    int64_t base, plane;
+    int k0;
+  };
+  auto fold_of = [&](int64_t tile) {
+    Fold f;
+    const int64_t p0 = tile * 16;
+    const int64_t patch_idx = p0 / pp;
+    f.k0 = static_cast<int>(p0 - patch_idx * pp);
+    const int64_t bb = patch_idx / tokens;
+    const int64_t l = token_start + (patch_idx - bb * tokens);
+    const int64_t gy = l / gw;
+    f.plane = height * width;
+    f.base = bb * 3 * f.plane + gy * patch * width + (l - gy * gw) * patch;
+    return f;
+  };
+
   auto process = [&](int64_t tile, const TileIn& in) {
+    Fold fold = {0, 0, 0};
+    if (HEAD) fold = fold_of(tile);
     float x[2][4], h[2][4];
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
@@ -398,13 +419,12 @@ __global__ void __launch_bounds__(MMA_THREADS, MMA_BLOCKS_PER_SM) pixel_mlp_mma_
         }
 #pragma unroll
         for (int o = 0; o < 3; ++o) part[o] = quad_sum(part[o]);
-        if (c == 0) {
-          const int64_t patch_idx = px / pp;
-          const int k = static_cast<int>(px % pp);
-          const int64_t bb = patch_idx / tokens, l = token_start + patch_idx % tokens;
-          const int64_t y = (l / gw) * patch + k / patch, xx = (l % gw) * patch + k % patch;
+        if (c == 0) {  // pixel k0 + g + 8 half of the tile's patch: row k / patch, column k % patch
+          const int k = fold.k0 + g + 8 * half;
+          const int ky = k / patch;
+          float* dst = v + fold.base + static_cast<int64_t>(ky) * width + (k - ky * patch);
 #pragma unroll
-          for (int o = 0; o < 3; ++o) v[((bb * 3 + o) * height + y) * width + xx] = part[o] + __ldg(fb + o);
+          for (int o = 0; o < 3; ++o) dst[o * fold.plane] = part[o] + __ldg(fb + o);
         }
       }
     }
@@ -668,7 +688,7 @@ extern "C" int iris_pixel_mlp_head(void* pixels, int pixel_dtype, const void* br
   if (n == 0) return IRIS_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   auto bf = [](const void* p) { return reinterpret_cast<const __nv_bfloat16*>(p); };
-  if (n % 16 == 0) {  // whole 16-pixel tiles: tensor-core MLP
+  if (n % 16 == 0 && patch % 4 == 0) {  // whole 16-pixel tiles, each inside one patch: tensor-core MLP
     const unsigned grid = mma_grid_for(n);
     const int pt = static_cast<int>(patch);
     if (pixel_dtype == IRIS_F32) {
