@@ -158,9 +158,9 @@ class CudaIris:
         first call runs the forward once eagerly, captures it, and synchronises the
         host once; later calls of the geometry copy the inputs into the graph's
         buffers, replay it and return a fresh copy of its output). The kernels are
-        the same; the graph removes the per-kernel launch gaps (about 2% of a B = 2
-        call at 1024^2). Sequence-parallel engines (``comm``) always run eagerly:
-        their barriers count epochs on the host."""
+        the same; the graph removes the host's per-kernel launch cost (a B = 2 call
+        at 1024^2: 62.2 ms eager, 61.9 ms replayed). Sequence-parallel engines
+        (``comm``) always run eagerly: their barriers count epochs on the host."""
         cfg = from_any(dit.cfg)
         state = dit.state_dict()
         check_supported(cfg, state)
