@@ -158,6 +158,22 @@ IRIS_DEVICE void pit_tail(float (&x)[C], const float (&attn)[C], const __nv_bflo
   for (int c = 0; c < C; ++c) x[c] = r(x[c] + r(r(out[c]) * (1.f + m[2 * C + c]) + m[3 * C + c]));
 }
 
+// gelu_erf on a pair, the polynomial and products on packed f32x2 instructions
+IRIS_DEVICE float2 gelu_erf2(float2 a) {
+  const float2 x = __fmul2_rn(make_float2(fabsf(a.x), fabsf(a.y)), make_float2(0.70710678118654752f, 0.70710678118654752f));
+  const float2 d = __ffma2_rn(x, make_float2(0.3275911f, 0.3275911f), make_float2(1.f, 1.f));
+  const float2 t = make_float2(__fdividef(1.f, d.x), __fdividef(1.f, d.y));
+  // half the published coefficients: q = (1 - erf(x)) / 2 directly
+  float2 poly = __ffma2_rn(t, make_float2(0.5307027145f, 0.5307027145f), make_float2(-0.7265760135f, -0.7265760135f));
+  poly = __ffma2_rn(t, poly, make_float2(0.7107068705f, 0.7107068705f));
+  poly = __ffma2_rn(t, poly, make_float2(-0.142248368f, -0.142248368f));
+  poly = __ffma2_rn(t, poly, make_float2(0.127414796f, 0.127414796f));
+  const float2 x2 = __fmul2_rn(x, x);
+  const float2 e = make_float2(__expf(-x2.x), __expf(-x2.y));
+  const float2 q = __fmul2_rn(__fmul2_rn(t, poly), e);
+  return make_float2(a.x * (a.x >= 0.f ? 1.f - q.x : q.x), a.y * (a.y >= 0.f ? 1.f - q.y : q.y));
+}
+
 // ---------------------------------------------------------------------------
 // Tensor-core form of the pixel tail: one warp per 16-pixel tile. The MLP
 // (16 -> 64 -> 16) runs as mma.sync m16n8k16 BF16 -> FP32 (8 MMAs each way);
@@ -364,7 +380,11 @@ __global__ void __launch_bounds__(MMA_THREADS, MMA_BLOCKS_PER_SM) pixel_mlp_mma_
       mma_bf16_16816(acc, a, bw1[nt][0], bw1[nt][1]);
       float gl[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) gl[j] = gelu_erf(r(acc[j] + bias1[nt][j & 1]));
+      for (int j = 0; j < 4; j += 2) {
+        const float2 gv = gelu_erf2(make_float2(r(acc[j] + bias1[nt][0]), r(acc[j + 1] + bias1[nt][1])));
+        gl[j] = gv.x;
+        gl[j + 1] = gv.y;
+      }
       const int ks = nt >> 1, hi = nt & 1;
       ga[ks][2 * hi] = pack_bf16x2(gl[0], gl[1]);      // row g
       ga[ks][2 * hi + 1] = pack_bf16x2(gl[2], gl[3]);  // row g + 8
