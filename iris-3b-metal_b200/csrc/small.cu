@@ -26,20 +26,26 @@ inline unsigned grid_for(int64_t n, int per_thread = 1) {
 }
 
 // out[(b, l - token_start), (c, ky, kx)] = x[b, c, gy p + ky, gx p + kx] for the
-// patch tokens l = gy * gw + gx in [token_start, token_start + tokens)
-__global__ void patchify_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ out, int64_t total,
+// patch tokens l = gy * gw + gx in [token_start, token_start + tokens). A block
+// walks whole token rows (grid-stride): the row's image position is worked out
+// once, and consecutive threads take consecutive features, so a warp reads
+// runs of a patch row and writes one contiguous run of the token row.
+__global__ void patchify_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ out, int64_t rows,
                                 int channels, int64_t height, int64_t width, int patch, int64_t token_start,
                                 int64_t tokens) {
   const int64_t gw = width / patch;
-  const int64_t feat = static_cast<int64_t>(channels) * patch * patch;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t row = i / feat, f = i % feat;
-    const int64_t b = row / tokens, l = token_start + row % tokens;
-    const int c = static_cast<int>(f / (patch * patch));
-    const int k = static_cast<int>(f % (patch * patch));
-    const int64_t y = (l / gw) * patch + k / patch, xx = (l % gw) * patch + k % patch;
-    out[i] = __float2bfloat16_rn(x[((b * channels + c) * height + y) * width + xx]);
+  const int pp = patch * patch;
+  const int feat = channels * pp;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const int64_t b = row / tokens, l = token_start + (row - b * tokens);
+    const int64_t gy = l / gw, gx = l - gy * gw;
+    const float* src = x + b * channels * height * width + gy * patch * width + gx * patch;
+    __nv_bfloat16* dst = out + row * feat;
+    for (int f = threadIdx.x; f < feat; f += blockDim.x) {
+      const int c = f / pp, k = f - c * pp;
+      const int ky = k / patch;
+      dst[f] = __float2bfloat16_rn(src[(static_cast<int64_t>(c) * height + ky) * width + (k - ky * patch)]);
+    }
   }
 }
 
@@ -339,10 +345,12 @@ extern "C" int iris_patchify(const float* x, void* out, int64_t batch, int64_t c
                "input is not divisible by patch_size");
   IRIS_REQUIRE(token_start >= 0 && tokens >= 0 && token_start + tokens <= (height / patch) * (width / patch),
                "patchify: token range outside the patch grid");
-  const int64_t total = batch * tokens * channels * patch * patch;
-  if (total == 0) return IRIS_OK;
-  patchify_kernel<<<grid_for(total), THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
-      x, reinterpret_cast<__nv_bfloat16*>(out), total, static_cast<int>(channels), height, width,
+  IRIS_REQUIRE(channels * patch * patch < (1 << 30), "patchify: patch too large");
+  const int64_t rows = batch * tokens;
+  if (rows == 0) return IRIS_OK;
+  const int64_t cap = static_cast<int64_t>(num_sms()) * 8;
+  patchify_kernel<<<static_cast<unsigned>(rows < cap ? rows : cap), THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, reinterpret_cast<__nv_bfloat16*>(out), rows, static_cast<int>(channels), height, width,
       static_cast<int>(patch), token_start, tokens);
   IRIS_CUDA(cudaGetLastError());
   return IRIS_OK;
